@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""Benchmark: latent-descent sample-steps/s of the EBR energy network at L = 900.
+
+Workload (per rank, weak scaling): 128 synthetic 30 x 30 maze inputs x 5 samples = 640 latent rows, L = 900, the
+4-layer / hidden 512 / 8 x 64 / SwiGLU 4x energy network in bf16 with random-init weights. One step = one segment of
+16 inference microsteps (forward + first-order dE/dz each, no double backward), then the lowest-energy pick over the
+5 samples. Every attention call runs the sm_100a kernels (ebr_b200.fused_attn).
+
+Output (rank 0, one JSON line): ``value`` = sample-steps/s over all ranks with inputs resident on the device;
+``e2e`` = the same through the public API with the puzzles copied from pinned host memory and the energies / picks
+copied back inside the timed region; ``roofline`` = the dominant attention op's achieved TFLOP/s (algorithmic FLOPs
+per call / CUDA-event duration) against the measured bf16 peak; ``cpu_baseline`` = the reference's CPU path (oracle
+attention, torch CPU for the rest) timed on a bounded sample on this host.
+
+``--impl reference`` times only that CPU path (rank 0) on the same config and prints its own line.
+``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "latent-descent sample-steps/s (L=900, B=128)"
+UNIT = "sample-steps/s"
+INPUTS, SAMPLES, MICROSTEPS, BOARD = 128, 5, 16, 30
+PASS_FLOP = {"attn_fwd": 4, "attn_bwd": 10, "attn_bwd_bwd": 24}  # x N^2 D per (b, h) slice
+PASS_BYTES = {"attn_fwd": (8, 4), "attn_bwd": (16, 4), "attn_bwd_bwd": (24, 4)}  # (x N D, x N) per slice
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tf_burst": d["bf16_tflops"], "tf_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}  # fmt: skip
+    return {"hbm_gbs": 6650.0, "tf_burst": 1590.0, "tf_sustained": 1400.0, "source": "fallback"}
+
+
+def config_dict(rows: int, n_gpus: int) -> dict:
+    return {
+        "workload": "cfg3 maze-30x30 latent descent (inference: fwd + dE/dz per microstep)",
+        "inputs_per_gpu": INPUTS,
+        "samples": SAMPLES,
+        "rows_per_gpu": rows,
+        "seq_len": BOARD * BOARD,
+        "microsteps_per_step": MICROSTEPS,
+        "model": "energy net 4 layers, hidden 512, 8 heads x 64, SwiGLU 4x, RMSNorm, 2D RoPE (random init)",
+        "parallelism": f"dp{n_gpus} (batch-sharded replicas, no collective)",
+        "l2": "inputs larger than L2 (each activation tensor ~590 MB)",
+    }
+
+
+# --------------------------------------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region (200 ms period)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")  # fmt: skip
+
+    def __init__(self, device_index: int) -> None:
+        self.idx = device_index
+        self.lines: list[str] = []
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )  # fmt: skip
+            threading.Thread(target=self._pump, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _pump(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# --------------------------------------------------------------------------------------------------------- inputs
+
+
+def maze_tokens(n: int, gen: torch.Generator) -> torch.Tensor:
+    """Synthetic stand-in for Maze-Hard inputs (the dataset is not available): 30 x 30 boards, wall (1) with p = 0.5
+    else open (0), one start (2) and one goal (3) cell. Path cells (4) appear only in the labels."""
+    cells = BOARD * BOARD
+    tok = (torch.rand(n, cells, generator=gen) < 0.5).to(torch.int32)
+    idx = torch.stack([torch.randperm(cells, generator=gen)[:2] for _ in range(n)])
+    tok.scatter_(1, idx[:, :1], 2)
+    tok.scatter_(1, idx[:, 1:], 3)
+    return tok
+
+
+def build_model(device, attention=None):
+    from ebr_b200.energy import EnergyConfig, EnergyReasoner
+
+    torch.manual_seed(0)
+    cfg = EnergyConfig(board_height=BOARD, board_width=BOARD, vocab_size=5, softplus=True)
+    return EnergyReasoner(cfg, attention=attention).to(device)
+
+
+def run_segment(model, x: torch.Tensor, z: torch.Tensor):
+    """One segment: 16 inference microsteps, then each input's lowest-energy sample."""
+    from ebr_b200.energy import descend, lowest_energy_pick
+
+    z, e = descend(model, z, x, MICROSTEPS)
+    return z, e, lowest_energy_pick(e, SAMPLES)
+
+
+# --------------------------------------------------------------------------------------------------------- CPU path
+
+
+def cpu_reference_sample(seconds: float = 10.0, rows: int = 2, min_steps: int = 1) -> dict:
+    """The reference's CPU path (dense oracle attention + torch CPU), timed on `rows` rows of the same workload until
+    `seconds` have passed. Returns sample-steps/s and what was run."""
+    from ebr_b200.energy import descend
+    from oracle.torch_attention import oracle_attention
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = build_model("cpu", attention=oracle_attention)
+    gen = torch.Generator().manual_seed(1)
+    tok = maze_tokens(rows, gen)
+    with torch.no_grad():
+        x = model.input_embeddings(tok)
+    z = model.fresh_states(rows, "cpu")
+    steps, t0 = 0, time.perf_counter()
+    while steps < min_steps or time.perf_counter() - t0 < seconds:
+        z, _ = descend(model, z, x, 1)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {
+        "value": rows * steps / dt,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{rows} rows x {steps} microsteps at L=900 ({dt:.1f} s): numpy oracle attention (fp32), torch CPU "
+        f"bf16 for the rest, {threads} threads",
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    warm = [cpu_reference_sample(seconds=0.0, rows=2, min_steps=1) for _ in range(max(args.warmup, 0))]
+    del warm
+    vals, last = [], None
+    for _ in range(args.steps):
+        last = cpu_reference_sample(seconds=0.0, rows=2, min_steps=1)
+        vals.append(last["value"])
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * 2 / value if value else None,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded maze-like boards; Maze-Hard is not available offline), random-init weights",
+        "config": config_dict(INPUTS * SAMPLES, args.gpus),
+        "cpu_baseline": {**last, "value": value},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------------------- GPU path
+
+
+def run_ours(args) -> None:
+    from ebr_b200 import _native, fused_attn, runtime
+    from ebr_b200.build import build
+
+    rank, world, local = runtime.init_distributed()
+    n_gpus = world
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if rank == 0:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    model = build_model(device)
+    model.eval()
+    rows = INPUTS * SAMPLES
+    gen = torch.Generator().manual_seed(1000 + rank)
+    tokens_host = maze_tokens(INPUTS, gen).repeat_interleave(SAMPLES, dim=0).pin_memory()
+    tokens = tokens_host.to(device)
+    with torch.no_grad():
+        x = model.input_embeddings(tokens)
+    z0 = model.fresh_states(rows, device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    # warm-up
+    z = z0
+    for _ in range(args.warmup):
+        z, e, pick = run_segment(model, x, z)
+    torch.cuda.synchronize()
+    _native.device_status()
+
+    # timed region: inputs resident on the device
+    sampler = ClockSampler(torch.cuda.current_device() if not os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    launches0 = _native.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with fused_attn.kernel_timer() as timer:
+        start.record()
+        for _ in range(args.steps):
+            z, e, pick = run_segment(model, x, z)
+        end.record()
+        torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = _native.launch_count() - launches0
+    barrier()
+    ms = start.elapsed_time(end)
+    ms = runtime.max_over_ranks(ms)
+    ops = timer.summary()
+    value = n_gpus * rows * MICROSTEPS * args.steps / (ms / 1000.0)
+
+    # end to end through the public API with host buffers
+    e2e_steps = max(1, args.steps)
+    energies_host = torch.empty(rows, dtype=torch.float32).pin_memory()
+    picks_host = torch.empty(INPUTS, dtype=torch.int64).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    zz = z0
+    for _ in range(e2e_steps):
+        tok_d = tokens_host.to(device, non_blocking=True)
+        with torch.no_grad():
+            xx = model.input_embeddings(tok_d)
+        zz, ee, pp = run_segment(model, xx, zz)
+        energies_host.copy_(ee, non_blocking=True)
+        picks_host.copy_(pp, non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = runtime.max_over_ranks(a.elapsed_time(b))
+    e2e_value = n_gpus * rows * MICROSTEPS * e2e_steps / (e2e_ms / 1000.0)
+    h2d = tokens_host.numel() * tokens_host.element_size()
+    d2h = energies_host.numel() * 4 + picks_host.numel() * 8
+    _native.device_status()
+
+    # roofline of the dominant attention op
+    pk = peaks()
+    dom_name = max(ops, key=lambda n: ops[n]["ms"]) if ops else None
+    roofline = None
+    if dom_name:
+        d = ops[dom_name]
+        B_, H_, N_, D_ = d["shape"]
+        flop = PASS_FLOP[dom_name] * N_ * N_ * D_ * B_ * H_
+        avg_ms = d["ms"] / d["calls"]
+        achieved = flop / (avg_ms / 1000.0) / 1e12
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic.json"
+        if tfile.exists():
+            t = json.loads(tfile.read_text()).get(dom_name)
+            if t:
+                traffic = t["bytes_per_slice"] * B_ * H_
+        roofline = {
+            "bound": "tensor",
+            "kernel": f"{dom_name} (all launches of one call; {d['calls']} calls in the timed region)",
+            "achieved": round(achieved, 2),
+            "peak": pk["tf_sustained"],
+            "unit": "TFLOP/s",
+            "frac": round(achieved / pk["tf_sustained"], 4),
+            "peak_note": f"{pk['source']} bf16 sustained (kernel timed inside a long step); burst {pk['tf_burst']}",
+            "traffic": traffic,
+            "flop_per_call": flop,
+            "avg_ms_per_call": round(avg_ms, 4),
+            "ops": {n: {"calls": v["calls"], "ms_total": round(v["ms"], 3)} for n, v in ops.items()},
+        }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_sample(seconds=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": UNIT,
+            "n_gpus": n_gpus,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded maze-like boards; Maze-Hard is not available offline), random-init weights",
+            "config": config_dict(rows, n_gpus),
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+# --------------------------------------------------------------------------------------------------------- sweep
+
+
+def run_sweep(args) -> None:
+    """each pass alone, bf16, H = 8, B = 262144 // L (per GPU), CUDA events, median of K."""
+    from ebr_b200 import _native
+    from ebr_b200.build import build
+
+    build()
+    torch.cuda.set_device(0)
+    pk = peaks()
+    Ls = [int(v) for v in args.lengths.split(",")]
+    for D in [int(v) for v in args.head_dims.split(",")]:
+        for L in Ls:
+            B, H = 262144 // L, 8
+            g = torch.Generator(device="cuda").manual_seed(0)
+            mk = lambda s: (torch.randn(B, H, L, D, device="cuda", generator=g) * s).to(torch.bfloat16)
+            q, k, v, do, gq, gk, gv = mk(0.5), mk(0.5), mk(0.5), mk(1.0), mk(1.0), mk(1.0), mk(1.0)
+            s = D**-0.5
+            o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, s)
+            dq, _, _ = torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, s)
+            fns = {
+                "attn_fwd": lambda: torch.ops.ebr_fused.attn_fwd(q, k, v, s),
+                "attn_bwd": lambda: torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, s),
+                "attn_bwd_bwd": lambda: torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, gq, gk, gv, s),
+            }
+            out = {"mode": "sweep", "L": L, "D": D, "B": B, "H": H}
+            for name, fn in fns.items():
+                for _ in range(max(args.warmup, 1)):
+                    fn()
+                torch.cuda.synchronize()
+                ts = []
+                for _ in range(args.steps):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    torch.cuda.synchronize()
+                    ts.append(a.elapsed_time(b))
+                ms = statistics.median(ts)
+                flop = PASS_FLOP[name] * L * L * D * B * H
+                nd, nn = PASS_BYTES[name]
+                byt = (nd * L * D + nn * L) * B * H
+                tf, gbs = flop / ms / 1e9, byt / ms / 1e6
+                out[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "tc_frac": round(tf / pk["tf_burst"], 4),
+                             "gbs": round(gbs, 0), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}  # fmt: skip
+            _native.device_status()
+            print(json.dumps(out), flush=True)
+            del q, k, v, do, gq, gk, gv, o, lse, dq
+            torch.cuda.empty_cache()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["descent", "sweep"], default="descent")
+    ap.add_argument("--lengths", default="64,81,100,256,900,2048")
+    ap.add_argument("--head-dims", default="64,128")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.mode == "descent" and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    elif args.mode == "sweep":
+        run_sweep(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

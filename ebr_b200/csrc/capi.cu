@@ -1,0 +1,514 @@
+// capi.cu: the C ABI of include/ebr_attn.h. Validates arguments on the host, picks the kernel family for the call's
+// dtype / shape / strides (the counterpart of the reference's launch plans, triton_kernels.py:612-676), builds the TMA
+// tensor maps and launches on the caller's stream. Never allocates device memory and never traps.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "../../include/ebr_attn.h"
+#include "simt.cuh"
+#include "tc_attn.cuh"
+
+namespace {
+
+using namespace ebr;
+
+thread_local char g_last_error[512] = "";
+std::atomic<uint64_t> g_launch_count{0};
+
+int set_error(int status, const char* fmt, const char* a = "", const char* b = "") {
+  std::snprintf(g_last_error, sizeof(g_last_error), fmt, a, b);
+  return status;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(EBR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------------------------------------ device checks
+
+constexpr int kMaxDevices = 64;
+
+int check_device(int* device_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  static std::atomic<int> arch[kMaxDevices];  // 0 unknown, else major * 10 + minor
+  int a = (dev < kMaxDevices) ? arch[dev].load() : 0;
+  if (a == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    a = major * 10 + minor;
+    if (dev < kMaxDevices) arch[dev].store(a);
+  }
+  if (a != 100) return set_error(EBR_ERR_DEVICE, "ebr_attn needs an sm_100 (B200) device%s%s");
+  *device_out = dev;
+  return EBR_OK;
+}
+
+// Raise a kernel's dynamic shared memory limit once per device, and refuse a launch shape under which more CTAs
+// could share an SM than its tensor memory (512 columns) can serve: tcgen05.alloc would then block.
+int prepare_tc_kernel(const void* kernel, int device, uint32_t smem, uint32_t tmem_cols) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> verdicts;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = verdicts.find({kernel, device});
+  if (it != verdicts.end()) return it->second;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
+  int blocks = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, 128, smem);
+  if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  const int verdict = (blocks >= 1 && static_cast<uint32_t>(blocks) * tmem_cols <= 512u)
+                          ? EBR_OK
+                          : set_error(EBR_ERR_CUDA, "tensor-memory budget check failed%s%s");
+  verdicts[{kernel, device}] = verdict;
+  return verdict;
+}
+
+int check_launch(const char* what) {
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? EBR_OK : cuda_error(e, what);
+}
+
+// ------------------------------------------------------------------------------------------------ argument checks
+
+size_t elem_size(int dtype) {
+  switch (dtype) {
+    case EBR_FLOAT32: return 4;
+    case EBR_FLOAT16:
+    case EBR_BFLOAT16: return 2;
+    case EBR_FLOAT64: return 8;
+    default: return 0;
+  }
+}
+size_t stat_size(int dtype) { return dtype == EBR_FLOAT64 ? 8 : 4; }
+
+int check_shape(int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
+  if (elem_size(dtype) == 0) return set_error(EBR_ERR_DTYPE, "unknown dtype%s%s");
+  if (B < 0 || H < 0 || N < 0) return set_error(EBR_ERR_SHAPE, "negative size%s%s");
+  if (D < 1 || D > 256) return set_error(EBR_ERR_SHAPE, "head dim must be in [1, 256]%s%s");
+  if (N > (int64_t{1} << 30) || H > (int64_t{1} << 30) || B > (int64_t{1} << 30))
+    return set_error(EBR_ERR_SHAPE, "size too large%s%s");
+  return EBR_OK;
+}
+
+int check_operand(const ebr_operand* op, const char* name, bool optional = false) {
+  if (!op) return optional ? EBR_OK : set_error(EBR_ERR_NULL, "operand %s is NULL%s", name);
+  if (!op->data && !optional) return set_error(EBR_ERR_NULL, "operand %s has no data%s", name);
+  if (op->stride_b < 0 || op->stride_h < 0 || op->stride_n < 0)
+    return set_error(EBR_ERR_STRIDE, "operand %s has a negative stride%s", name);
+  return EBR_OK;
+}
+
+template <typename T>
+Strided<T> strided(const ebr_operand* op) {
+  if (!op || !op->data) return Strided<T>{nullptr, 0, 0, 0};
+  return Strided<T>{static_cast<const T*>(op->data), op->stride_b, op->stride_h, op->stride_n};
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Internal: a TMA tensor map could not be encoded for these operands; the CUDA-core kernels take the call instead.
+constexpr int kNoTensorMap = -1;
+
+// ------------------------------------------------------------------------------------------------ TMA tensor maps
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = []() -> EncodeTiled {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// A stride the tensor-core path can take: 16-byte multiple (TMA), or irrelevant because the dim has size 1.
+bool tma_stride_ok(int64_t stride_elems, int64_t extent) {
+  return extent <= 1 || ((stride_elems * 2) % 16 == 0 && stride_elems * 2 < (int64_t{1} << 40));
+}
+
+bool tc_operand_ok(const ebr_operand* op, int64_t B, int64_t H, int64_t N) {
+  if (!op || !op->data) return true;  // a zero operand is not loaded
+  return aligned16(op->data) && tma_stride_ok(op->stride_n, N) && tma_stride_ok(op->stride_h, H) &&
+         tma_stride_ok(op->stride_b, B) && (op->stride_n > 0 || N <= 1);
+}
+
+// [B, H, N, D] 16-bit operand -> 4-D tensor map (D, N, H, B), box 64 x 128 x 1 x 1, 128-byte swizzle, zero fill.
+int make_tile_map(CUtensorMap* map, const ebr_operand* op, int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
+  auto fix = [](int64_t stride, int64_t extent) -> cuuint64_t {
+    return static_cast<cuuint64_t>(extent <= 1 ? 16 : stride * 2);
+  };
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {fix(op->stride_n, N), fix(op->stride_h, H), fix(op->stride_b, B)};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(op->data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled failed%s%s");
+  return EBR_OK;
+}
+
+bool tc_eligible(int dtype, int64_t D, std::initializer_list<const ebr_operand*> ops, int64_t B, int64_t H, int64_t N) {
+  if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16) return false;
+  if (D != 64 && D != 128) return false;
+  for (const ebr_operand* op : ops)
+    if (!tc_operand_ok(op, B, H, N)) return false;
+  return true;
+}
+
+int simt_grid(int64_t rows) {
+  const int64_t cap = 148 * 32;
+  return static_cast<int>(rows < cap ? rows : cap);
+}
+
+// ------------------------------------------------------------------------------------------------ forward
+
+template <typename T>
+int launch_simt_fwd(int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                    const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
+  using C = typename Elem<T>::C;
+  const int64_t rows = B * H * N;
+  const size_t smem = (D + kSimtThreads + 8) * sizeof(C);
+  simt_fwd<T><<<simt_grid(rows), kSimtThreads, smem, st>>>(rows, static_cast<int>(H), static_cast<int>(N),
+                                                             static_cast<int>(D), scale, strided<T>(q), strided<T>(k),
+                                                             strided<T>(v), static_cast<T*>(o), static_cast<C*>(lse));
+  return check_launch("simt_fwd");
+}
+
+template <typename T, int D>
+int launch_tc_fwd(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                  const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
+  using L = FwdLayout<D>;
+  CUtensorMap tq, tk, tv;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D))
+    return kNoTensorMap;
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_fwd_kernel<T, D>), device, L::kSmem, L::kTmemCols);
+  if (s) return s;
+  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((N + kTile - 1) / kTile));
+  tc_fwd_kernel<T, D><<<grid, 128, L::kSmem, st>>>(tq, tk, tv, static_cast<T*>(o), static_cast<float*>(lse),
+                                                   static_cast<int>(H), static_cast<int>(N), static_cast<float>(scale));
+  return check_launch("tc_fwd_kernel");
+}
+
+// ------------------------------------------------------------------------------------------------ backward
+
+template <typename T>
+int launch_simt_bwd(int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                    const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                    const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, cudaStream_t st) {
+  using C = typename Elem<T>::C;
+  const int64_t rows = B * H * N;
+  C* di = static_cast<C*>(scratch);
+  simt_bwd_row<T><<<simt_grid(rows), kSimtThreads, (2 * D + kSimtThreads + 8) * sizeof(C), st>>>(
+      rows, static_cast<int>(H), static_cast<int>(N), static_cast<int>(D), scale, strided<T>(q), strided<T>(k),
+      strided<T>(v), static_cast<const T*>(o), static_cast<const C*>(lse), strided<T>(dout), static_cast<T*>(dq), di);
+  int s = check_launch("simt_bwd_row");
+  if (s) return s;
+  simt_bwd_col<T><<<simt_grid(rows), kSimtThreads, (2 * D + 2 * kSimtThreads) * sizeof(C), st>>>(
+      rows, static_cast<int>(H), static_cast<int>(N), static_cast<int>(D), scale, strided<T>(q), strided<T>(k),
+      strided<T>(v), static_cast<const C*>(lse), strided<T>(dout), di, static_cast<T*>(dk), static_cast<T*>(dv));
+  return check_launch("simt_bwd_col");
+}
+
+template <typename T, int D>
+int launch_tc_bwd_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                         const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                         const ebr_operand* dout, void* dq, void* dk, void* dv, cudaStream_t st) {
+  using L = BwdSingleLayout<D>;
+  CUtensorMap tq, tk, tv, tdo;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
+    return kNoTensorMap;
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_single_kernel<T, D>), device, L::kSmem, L::kTmemCols);
+  if (s) return s;
+  tc_bwd_single_kernel<T, D><<<static_cast<unsigned>(B * H), 128, L::kSmem, st>>>(
+      tq, tk, tv, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(dq),
+      static_cast<T*>(dk), static_cast<T*>(dv), static_cast<int>(H), static_cast<int>(N), static_cast<float>(scale));
+  return check_launch("tc_bwd_single_kernel");
+}
+
+template <typename T, int D>
+int launch_tc_bwd_tiled(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                        const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, cudaStream_t st) {
+  using LQ = BwdDqLayout<D>;
+  using LK = BwdDkdvLayout<D>;
+  CUtensorMap tq, tk, tv, tdo;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
+    return kNoTensorMap;
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_dq_kernel<T, D>), device, LQ::kSmem, LQ::kTmemCols);
+  if (s) return s;
+  s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_dkdv_kernel<T, D>), device, LK::kSmem, LK::kTmemCols);
+  if (s) return s;
+  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((N + kTile - 1) / kTile));
+  float* di = static_cast<float*>(scratch);
+  tc_bwd_dq_kernel<T, D><<<grid, 128, LQ::kSmem, st>>>(tq, tk, tv, tdo, static_cast<const T*>(o),
+                                                       static_cast<const float*>(lse), di, static_cast<T*>(dq),
+                                                       static_cast<int>(H), static_cast<int>(N),
+                                                       static_cast<float>(scale));
+  if ((s = check_launch("tc_bwd_dq_kernel"))) return s;
+  tc_bwd_dkdv_kernel<T, D><<<grid, 128, LK::kSmem, st>>>(tq, tk, tv, tdo, static_cast<const float*>(lse), di,
+                                                         static_cast<T*>(dk), static_cast<T*>(dv),
+                                                         static_cast<int>(H), static_cast<int>(N),
+                                                         static_cast<float>(scale));
+  return check_launch("tc_bwd_dkdv_kernel");
+}
+
+// ------------------------------------------------------------------------------------------------ double backward
+
+template <typename T>
+int launch_simt_bob(int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                    const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                    const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
+                    void* hq, void* hk, void* hv, void* hdo, void* scratch, cudaStream_t st) {
+  using C = typename Elem<T>::C;
+  const int64_t rows = B * H * N;
+  C* stats = static_cast<C*>(scratch);
+  simt_bob_row<T><<<simt_grid(rows), kSimtThreads, (3 * D + 4 * kSimtThreads + 8) * sizeof(C), st>>>(
+      rows, static_cast<int>(H), static_cast<int>(N), static_cast<int>(D), scale, strided<T>(q), strided<T>(k),
+      strided<T>(v), static_cast<const T*>(o), static_cast<const C*>(lse), strided<T>(dout), strided<T>(gq),
+      strided<T>(gk), strided<T>(gv), static_cast<T*>(hq), static_cast<T*>(hdo), stats);
+  int s = check_launch("simt_bob_row");
+  if (s) return s;
+  simt_bob_col<T><<<simt_grid(rows), kSimtThreads, (4 * D + 3 * kSimtThreads) * sizeof(C), st>>>(
+      rows, static_cast<int>(H), static_cast<int>(N), static_cast<int>(D), scale, strided<T>(q), strided<T>(k),
+      strided<T>(v), static_cast<const C*>(lse), strided<T>(dout), strided<T>(gq), strided<T>(gk), strided<T>(gv),
+      static_cast<T*>(hk), static_cast<T*>(hv), stats);
+  return check_launch("simt_bob_col");
+}
+
+template <typename T>
+int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                         const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                         const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
+                         void* hq, void* hk, void* hv, void* hdo, cudaStream_t st) {
+  using L = BobSingleLayout;
+  constexpr int D = 64;
+  CUtensorMap tq, tk, tv, tdo, tgq, tgk, tgv;
+  uint32_t zero_mask = 0;
+  const ebr_operand* gs[3] = {gq, gk, gv};
+  CUtensorMap* gm[3] = {&tgq, &tgk, &tgv};
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
+    return kNoTensorMap;
+  for (int i = 0; i < 3; ++i) {
+    if (!gs[i] || !gs[i]->data) {
+      zero_mask |= 1u << i;
+      *gm[i] = tq;  // never read
+    } else if (make_tile_map(gm[i], gs[i], dtype, B, H, N, D)) {
+      return kNoTensorMap;
+    }
+  }
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bob_single_kernel<T>), device, L::kSmem, L::kTmemCols);
+  if (s) return s;
+  tc_bob_single_kernel<T><<<static_cast<unsigned>(B * H), 128, L::kSmem, st>>>(
+      tq, tk, tv, tdo, tgq, tgk, tgv, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(hq),
+      static_cast<T*>(hk), static_cast<T*>(hv), static_cast<T*>(hdo), static_cast<int>(H), static_cast<int>(N),
+      static_cast<float>(scale), zero_mask);
+  return check_launch("tc_bob_single_kernel");
+}
+
+}  // namespace
+
+// ================================================================================================ C ABI
+
+extern "C" {
+
+int ebr_attn_uses_tensor_cores(int dtype, int64_t D, const ebr_operand* q, const ebr_operand* k,
+                               const ebr_operand* v) {
+  // Shape-independent part of the choice; N only decides between the single-tile and multi-tile kernels.
+  return tc_eligible(dtype, D, {q, k, v}, 2, 2, 2) ? 1 : 0;
+}
+
+int ebr_attn_fwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                 const ebr_operand* k, const ebr_operand* v, void* o, void* lse, void* stream) {
+  int s;
+  if ((s = check_shape(dtype, B, H, N, D)) || (s = check_operand(q, "q")) || (s = check_operand(k, "k")) ||
+      (s = check_operand(v, "v")))
+    return s;
+  if (!o || !lse) return set_error(EBR_ERR_NULL, "output pointer is NULL%s%s");
+  if (B * H * N == 0) return EBR_OK;
+  int device = 0;
+  if ((s = check_device(&device))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tc_eligible(dtype, D, {q, k, v}, B, H, N) && aligned16(o)) {
+    if (dtype == EBR_BFLOAT16)
+      s = D == 64 ? launch_tc_fwd<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                  : launch_tc_fwd<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+    else
+      s = D == 64 ? launch_tc_fwd<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                  : launch_tc_fwd<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+    if (s != kNoTensorMap) return s;
+  }
+  switch (dtype) {
+    case EBR_FLOAT32: return launch_simt_fwd<float>(B, H, N, D, scale, q, k, v, o, lse, st);
+    case EBR_FLOAT64: return launch_simt_fwd<double>(B, H, N, D, scale, q, k, v, o, lse, st);
+    case EBR_BFLOAT16: return launch_simt_fwd<__nv_bfloat16>(B, H, N, D, scale, q, k, v, o, lse, st);
+    default: return launch_simt_fwd<__half>(B, H, N, D, scale, q, k, v, o, lse, st);
+  }
+}
+
+size_t ebr_attn_bwd_scratch_bytes(int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
+  (void)D;
+  if (elem_size(dtype) == 0 || B < 0 || H < 0 || N < 0) return 0;
+  return static_cast<size_t>(B * H * N) * stat_size(dtype);
+}
+
+int ebr_attn_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                 const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                 const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, size_t scratch_bytes,
+                 void* stream) {
+  int s;
+  if ((s = check_shape(dtype, B, H, N, D)) || (s = check_operand(q, "q")) || (s = check_operand(k, "k")) ||
+      (s = check_operand(v, "v")) || (s = check_operand(dout, "dout")))
+    return s;
+  if (!o || !lse || !dq || !dk || !dv) return set_error(EBR_ERR_NULL, "o / lse / output pointer is NULL%s%s");
+  if (B * H * N == 0) return EBR_OK;
+  int device = 0;
+  if ((s = check_device(&device))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool outs_ok = aligned16(o) && aligned16(dq) && aligned16(dk) && aligned16(dv);
+  const bool scratch_ok = scratch && scratch_bytes >= ebr_attn_bwd_scratch_bytes(dtype, B, H, N, D);
+  if (N > kTile && scratch_ok && outs_ok && tc_eligible(dtype, D, {q, k, v, dout}, B, H, N)) {
+    if (dtype == EBR_BFLOAT16)
+      s = D == 64 ? launch_tc_bwd_tiled<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+                                                            dk, dv, scratch, st)
+                  : launch_tc_bwd_tiled<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+                                                             dk, dv, scratch, st);
+    else
+      s = D == 64 ? launch_tc_bwd_tiled<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk, dv,
+                                                    scratch, st)
+                  : launch_tc_bwd_tiled<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+                                                     dv, scratch, st);
+    if (s != kNoTensorMap) return s;
+  }
+  if (N <= kTile && outs_ok && tc_eligible(dtype, D, {q, k, v, dout}, B, H, N)) {
+    if (dtype == EBR_BFLOAT16)
+      s = D == 64 ? launch_tc_bwd_single<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+                                                             dk, dv, st)
+                  : launch_tc_bwd_single<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout,
+                                                              dq, dk, dv, st);
+    else
+      s = D == 64 ? launch_tc_bwd_single<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+                                                     dv, st)
+                  : launch_tc_bwd_single<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+                                                      dv, st);
+    if (s != kNoTensorMap) return s;
+  }
+  if (!scratch || scratch_bytes < ebr_attn_bwd_scratch_bytes(dtype, B, H, N, D))
+    return set_error(EBR_ERR_SCRATCH, "scratch missing or too small%s%s");
+  switch (dtype) {
+    case EBR_FLOAT32: return launch_simt_bwd<float>(B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch, st);
+    case EBR_FLOAT64:
+      return launch_simt_bwd<double>(B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch, st);
+    case EBR_BFLOAT16:
+      return launch_simt_bwd<__nv_bfloat16>(B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch, st);
+    default: return launch_simt_bwd<__half>(B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch, st);
+  }
+}
+
+size_t ebr_attn_bwd_bwd_scratch_bytes(int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
+  (void)D;
+  if (elem_size(dtype) == 0 || B < 0 || H < 0 || N < 0) return 0;
+  return 3 * static_cast<size_t>(B * H * N) * stat_size(dtype);
+}
+
+int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double scale, const ebr_operand* q,
+                     const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                     const ebr_operand* dout, const void* dq, const ebr_operand* gq, const ebr_operand* gk,
+                     const ebr_operand* gv, void* hq, void* hk, void* hv, void* hdout, void* scratch,
+                     size_t scratch_bytes, void* stream) {
+  (void)dq;  // accepted for the op contract, not read (reference.py:74)
+  int s;
+  if ((s = check_shape(dtype, B, H, N, D)) || (s = check_operand(q, "q")) || (s = check_operand(k, "k")) ||
+      (s = check_operand(v, "v")) || (s = check_operand(dout, "dout")) || (s = check_operand(gq, "gq", true)) ||
+      (s = check_operand(gk, "gk", true)) || (s = check_operand(gv, "gv", true)))
+    return s;
+  if (!o || !lse || !hq || !hk || !hv || !hdout)
+    return set_error(EBR_ERR_NULL, "o / lse / output pointer is NULL%s%s");
+  if (B * H * N == 0) return EBR_OK;
+  int device = 0;
+  if ((s = check_device(&device))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool outs_ok = aligned16(o) && aligned16(hq) && aligned16(hk) && aligned16(hv) && aligned16(hdout);
+  if (N <= kTile && D == 64 && outs_ok && tc_eligible(dtype, D, {q, k, v, dout, gq, gk, gv}, B, H, N)) {
+    if (dtype == EBR_BFLOAT16)
+      s = launch_tc_bob_single<__nv_bfloat16>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq,
+                                              hk, hv, hdout, st);
+    else
+      s = launch_tc_bob_single<__half>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv,
+                                       hdout, st);
+    if (s != kNoTensorMap) return s;
+  }
+  if (!scratch || scratch_bytes < ebr_attn_bwd_bwd_scratch_bytes(dtype, B, H, N, D))
+    return set_error(EBR_ERR_SCRATCH, "scratch missing or too small%s%s");
+  switch (dtype) {
+    case EBR_FLOAT32:
+      return launch_simt_bob<float>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout, scratch,
+                                    st);
+    case EBR_FLOAT64:
+      return launch_simt_bob<double>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout,
+                                     scratch, st);
+    case EBR_BFLOAT16:
+      return launch_simt_bob<__nv_bfloat16>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout,
+                                            scratch, st);
+    default:
+      return launch_simt_bob<__half>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout, scratch,
+                                     st);
+  }
+}
+
+int ebr_attn_device_status(void) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_error(e, "cudaDeviceSynchronize");
+  int flag = 0;
+  e = cudaMemcpyFromSymbol(&flag, ebr::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyFromSymbol");
+  if (flag != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(ebr::g_device_error, &zero, sizeof(int));
+    std::snprintf(g_last_error, sizeof(g_last_error), "bounded device wait ran out at site %d", flag);
+    return EBR_ERR_DEVICE_TIMEOUT;
+  }
+  return EBR_OK;
+}
+
+const char* ebr_attn_status_string(int status) {
+  switch (status) {
+    case EBR_OK: return "ok";
+    case EBR_ERR_NULL: return "null pointer";
+    case EBR_ERR_SHAPE: return "bad shape";
+    case EBR_ERR_DTYPE: return "unsupported dtype";
+    case EBR_ERR_STRIDE: return "bad stride";
+    case EBR_ERR_SCRATCH: return "scratch missing or too small";
+    case EBR_ERR_CUDA: return "CUDA error";
+    case EBR_ERR_DEVICE: return "unsupported device";
+    case EBR_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* ebr_attn_last_error(void) { return g_last_error; }
+
+uint64_t ebr_attn_launch_count(void) { return g_launch_count.load(); }
+
+}  // extern "C"

@@ -1,0 +1,942 @@
+// tc_attn.cuh: tcgen05 tensor-core kernels of the three attention passes for 16-bit inputs (bf16 / fp16).
+//
+// Layout. Every operand tile is a [128 rows x 64 cols] 16-bit tile in the 128-byte-swizzled layout that a TMA load
+// with CU_TENSOR_MAP_SWIZZLE_128B writes (rows of 128 B, 8-row atoms of 1 KiB, 16-byte chunk c of row r stored at
+// chunk c ^ (r % 8)); D = 128 uses two such tiles side by side (the "halves"). The same tile serves as a K-major
+// operand (K = the 64 columns) and, read the other way, as an MN-major operand (K = the 128 rows), so Q, K, V, dO and
+// the derived [query x key] tiles P / dS / A / gS are staged once and used in both orientations.
+//
+// Roles. 128 threads; thread t owns TMEM lane t, which is query row t of the tile (or key row t for the key-major
+// accumulators). Thread 0 issues the TMA loads and the tcgen05.mma instructions; all threads do the softmax and row
+// statistics on registers loaded from TMEM and write the derived 16-bit tiles to shared memory.
+//
+// Numerics follow the reference's Triton kernels (models/fused_attn/triton_kernels.py): 16-bit operands and fp32
+// accumulation in every dot; P and dS (and the second-order tiles) rounded to the input type before they enter a
+// dot (:576-586); exp applied as exp2 after subtracting in natural units (:48-56); P = exp(fma(q.k, scale, -lse))
+// (:87-88); D = rowsum(dO * O) from the stored O; the fp32 scale is shared by logits and gradients (:689-693).
+#pragma once
+
+#include <type_traits>
+
+#include "sm100.cuh"
+
+namespace ebr {
+
+constexpr int kTile = 128;                    // rows of a tile (queries or keys)
+constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // one [128 x 64] 16-bit SW128 tile
+
+template <typename T>
+__host__ __device__ constexpr bool is_bf16() {
+  return sizeof(T) == 2 && !std::is_same<T, __half>::value;
+}
+
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
+// Descriptor of a K-major operand: a [128 x (64 * halves)] tile, K-step kk (16 elements) of the K = columns axis.
+__device__ __forceinline__ uint64_t desc_kmajor(const unsigned char* tile, int kk) {
+  return sw128_desc(smem_u32(tile) + (kk >> 2) * kHalfBytes + (kk & 3) * 32u, 16u, 1024u);
+}
+// Descriptor of an MN-major operand read from the same tile: MN = the columns (64 per half, halves kHalfBytes apart),
+// K-step kk covers rows [16 kk, 16 kk + 16).
+__device__ __forceinline__ uint64_t desc_mnmajor(const unsigned char* tile, int kk) {
+  return sw128_desc(smem_u32(tile) + kk * 2048u, kHalfBytes, 1024u);
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..7 within a 64-column half) of row `row` in a SW128 tile.
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
+  return static_cast<uint32_t>(row) * 128u + ((static_cast<uint32_t>(chunk) ^ (static_cast<uint32_t>(row) & 7u)) << 4);
+}
+
+// Store 32 consecutive columns [c, c + 32) of row `row` (16 packed pairs) into a [128 x 128] 16-bit SW128 tile.
+__device__ __forceinline__ void st_row32(unsigned char* tile, int row, int c, const uint32_t (&pk)[16]) {
+  unsigned char* half = tile + (c >> 6) * kHalfBytes;
+  const int c0 = (c & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    *reinterpret_cast<uint4*>(half + sw128_off(row, c0 + q)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+}
+
+// Load 8 consecutive columns [8 chunk, 8 chunk + 8) of row `row` of a TMA-written SW128 operand tile, widened.
+template <typename T>
+__device__ __forceinline__ void ld_row8(const unsigned char* tile, int row, int chunk, float (&x)[8]) {
+  const unsigned char* half = tile + (chunk >> 3) * kHalfBytes;
+  const uint4 u = *reinterpret_cast<const uint4*>(half + sw128_off(row, chunk & 7));
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = static_cast<float>(e[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void ld_global8(const T* p, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = static_cast<float>(e[i]);
+}
+
+// Write one output row of D values (fp32 in TMEM columns [col, col + D) of this thread's lane) times `mul`.
+template <typename T, int D>
+__device__ __forceinline__ void store_row_from_tmem(uint32_t taddr, float mul, T* dst) {
+#pragma unroll
+  for (int c = 0; c < D; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+    if (dst) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u;
+        u.x = pack2<T>(__uint_as_float(r[8 * q + 0]) * mul, __uint_as_float(r[8 * q + 1]) * mul);
+        u.y = pack2<T>(__uint_as_float(r[8 * q + 2]) * mul, __uint_as_float(r[8 * q + 3]) * mul);
+        u.z = pack2<T>(__uint_as_float(r[8 * q + 4]) * mul, __uint_as_float(r[8 * q + 5]) * mul);
+        u.w = pack2<T>(__uint_as_float(r[8 * q + 6]) * mul, __uint_as_float(r[8 * q + 7]) * mul);
+        *reinterpret_cast<uint4*>(dst + c + 8 * q) = u;
+      }
+    }
+  }
+}
+
+// Issue the K-major x K-major product over the head dim: D[tmem] (+)= A[128 x D] * B[128 x D]^T (M = N = 128).
+template <int D>
+__device__ __forceinline__ void mma_rows_x_rows(uint32_t d_tmem, const unsigned char* a, const unsigned char* b,
+                                                uint32_t idesc, bool accumulate_first) {
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) mma_ss(d_tmem, desc_kmajor(a, kk), desc_kmajor(b, kk), idesc, (kk > 0 || accumulate_first) ? 1u : 0u);
+}
+// D[tmem] (+)= A[128 x 128 keys/queries] (K-major) * B (MN-major over the 128 rows of a [128 x D] tile).
+__device__ __forceinline__ void mma_tile_x_rows(uint32_t d_tmem, const unsigned char* a, const unsigned char* b,
+                                                uint32_t idesc, bool accumulate_first) {
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk)
+    mma_ss(d_tmem, desc_kmajor(a, kk), desc_mnmajor(b, kk), idesc, (kk > 0 || accumulate_first) ? 1u : 0u);
+}
+// D[tmem] (+)= A^T (A a [128 q x 128 k] tile read MN-major: M = keys) * B (MN-major [128 q x D] tile).
+__device__ __forceinline__ void mma_tileT_x_rows(uint32_t d_tmem, const unsigned char* a, const unsigned char* b,
+                                                 uint32_t idesc, bool accumulate_first) {
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk)
+    mma_ss(d_tmem, desc_mnmajor(a, kk), desc_mnmajor(b, kk), idesc, (kk > 0 || accumulate_first) ? 1u : 0u);
+}
+
+// ================================================================================================ forward
+
+template <int D>
+struct FwdLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK0 = kQ + kOp, kV0 = kK0 + kOp, kK1 = kV0 + kOp, kV1 = kK1 + kOp;
+  static constexpr uint32_t kPh = kV1 + kOp, kPl = kPh + 2 * kHalfBytes;
+  static constexpr uint32_t kBytes = kPl + 2 * kHalfBytes;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 256;  // S: [0, 128), O_j: [128, 128 + D)
+};
+
+// Forward for any N: grid (B * H, ceil(N / 128)); the CTA owns 128 query rows and sweeps the keys in tiles of 128
+// with an online softmax (the reference's _fwd_kernel, triton_kernels.py:98-163). K / V tiles are double-buffered
+// (the TMA of tile j + 1 runs under the math of tile j). Per key tile: S = Q K^T into TMEM; P goes to shared memory
+// as a 16-bit pair P_hi + P_lo (P_lo = P - P_hi rounded again), so O_j = P_hi V + P_lo V carries P to ~2^-16 and the
+// output meets a 2e-3 max-rel bar against fp32 attention; then acc = acc * alpha + O_j in registers. The row sum l
+// uses the unrounded P, as the reference does.
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1)
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, T* __restrict__ out, float* __restrict__ lse, int H, int N,
+                  float scale) {
+  using L = FwdLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sPh = smem + L::kPh;
+  unsigned char* sPl = smem + L::kPl;
+  __shared__ uint64_t bar_full[2], bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
+  const int m0 = blockIdx.y * kTile;
+  constexpr uint32_t kIdS = idesc_f16(is_bf16<T>(), 0, 0, 128, 128);
+  constexpr uint32_t kIdPV = idesc_f16(is_bf16<T>(), 0, 1, 128, D);
+  const int n_tiles = (N + kTile - 1) / kTile;
+  auto sK = [&](int st) { return smem + (st ? L::kK1 : L::kK0); };
+  auto sV = [&](int st) { return smem + (st ? L::kV1 : L::kV0); };
+  auto load_kv = [&](int jt, int st) {
+    mbar_arrive_expect_tx(&bar_full[st], (jt == 0 ? 3u : 2u) * L::kOp);
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      if (jt == 0) tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, m0, h, b);
+      tma_load_4d(sK(st) + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, jt * kTile, h, b);
+      tma_load_4d(sV(st) + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, jt * kTile, h, b);
+    }
+  };
+
+  if (tid == 0) {
+    mbar_init(&bar_full[0], 1);
+    mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    load_kv(0, 0);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  float acc[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) acc[d] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  uint32_t ph_mma = 0;
+  bool fail = false;
+
+  for (int jt = 0; jt < n_tiles; ++jt) {
+    const int st = jt & 1;
+    // Stage st ^ 1 held tile jt - 1, whose P V product completed before the end of the last iteration.
+    if (tid == 0 && jt + 1 < n_tiles) load_kv(jt + 1, st ^ 1);
+    fail |= !mbar_wait(&bar_full[st], (jt >> 1) & 1, 101);
+    if (__syncthreads_or(fail)) break;
+    if (tid == 0) {
+      tc_fence_after();
+      mma_rows_x_rows<D>(tS, sQ, sK(st), kIdS, false);
+      mma_commit(&bar_mma);
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 102);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+
+    // Row max of this key tile (pass 1), then P = exp(s - m_new) as a 16-bit hi / lo pair (pass 2).
+    const int j0 = jt * kTile;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < kTile; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tS + lane_off + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (j0 + c + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * scale);
+    }
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = exp_nat(m_run - m_new);
+    float psum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < kTile; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tS + lane_off + c, r);
+      tmem_wait_ld();
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const float p0 = (j0 + c + e < N) ? exp_nat(__uint_as_float(r[e]) * scale - m_new) : 0.f;
+        const float p1 = (j0 + c + e + 1 < N) ? exp_nat(__uint_as_float(r[e + 1]) * scale - m_new) : 0.f;
+        psum += p0 + p1;
+        const float h0 = round16<T>(p0), h1 = round16<T>(p1);
+        hi[e >> 1] = pack2<T>(h0, h1);
+        lo[e >> 1] = pack2<T>(p0 - h0, p1 - h1);
+      }
+      st_row32(sPh, tid, c, hi);
+      st_row32(sPl, tid, c, lo);
+    }
+    l_run = l_run * alpha + psum;
+    m_run = m_new;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_tile_x_rows(tO, sPh, sV(st), kIdPV, false);
+      mma_tile_x_rows(tO, sPl, sV(st), kIdPV, true);
+      mma_commit(&bar_mma);
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 103);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tO + lane_off + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) acc[c + e] = acc[c + e] * alpha + __uint_as_float(r[e]);
+    }
+    tc_fence_before();
+    __syncthreads();  // S, O_j, P and this stage's K / V are free
+  }
+
+  const int row = m0 + tid;
+  if (!fail && row < N) {
+    const float inv = 1.f / l_run;
+    T* orow = out + (static_cast<int64_t>(bh) * N + row) * D;
+#pragma unroll
+    for (int d = 0; d < D; d += 8) {
+      uint4 u;
+      u.x = pack2<T>(acc[d] * inv, acc[d + 1] * inv);
+      u.y = pack2<T>(acc[d + 2] * inv, acc[d + 3] * inv);
+      u.z = pack2<T>(acc[d + 4] * inv, acc[d + 5] * inv);
+      u.w = pack2<T>(acc[d + 6] * inv, acc[d + 7] * inv);
+      *reinterpret_cast<uint4*>(orow + d) = u;
+    }
+    lse[static_cast<int64_t>(bh) * N + row] = m_run + logf(l_run);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// ================================================================================================ backward, N > 128
+
+// Shared helper: thread `row`'s D_i = <dO_i, O_i> from the TMA-staged dO tile and the stored (contiguous) O.
+template <typename T, int D>
+__device__ __forceinline__ float row_delta(const unsigned char* sDO, int row, const T* orow) {
+  float di = 0.f;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float x[8], y[8];
+    ld_row8<T>(sDO, row, c, x);
+    ld_global8<T>(orow + 8 * c, y);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) di += x[i] * y[i];
+  }
+  return di;
+}
+
+// From S and dP in TMEM (this thread's query row), write P (optional) and dS = P (dP - D) as 16-bit tiles.
+// Keys at or past N and query rows at or past N give zeros.
+template <typename T, bool kWriteP>
+__device__ __forceinline__ void softmax_grad_tiles(uint32_t tS, uint32_t tDP, int row, bool row_ok, int key0, int N,
+                                                   float Li, float Di, float scale, unsigned char* sP,
+                                                   unsigned char* sDS) {
+#pragma unroll 1
+  for (int c = 0; c < kTile; c += 32) {
+    uint32_t rs[32], rp[32];
+    tmem_ld32(tS + c, rs);
+    tmem_ld32(tDP + c, rp);
+    tmem_wait_ld();
+    uint32_t pk[16], dk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      float p[2], ds[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const bool ok = row_ok && (key0 + c + e + u < N);
+        p[u] = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+        ds[u] = p[u] * (__uint_as_float(rp[e + u]) - Di);
+      }
+      pk[e >> 1] = pack2<T>(p[0], p[1]);
+      dk[e >> 1] = pack2<T>(ds[0], ds[1]);
+    }
+    if (kWriteP) st_row32(sP, row, c, pk);
+    st_row32(sDS, row, c, dk);
+  }
+}
+
+template <int D>
+struct BwdDqLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
+  static constexpr uint32_t kQ = 0, kDO = kQ + kOp;
+  static constexpr uint32_t kK0 = kDO + kOp, kV0 = kK0 + kOp, kK1 = kV0 + kOp, kV1 = kK1 + kOp;
+  static constexpr uint32_t kDS = kV1 + kOp;
+  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;  // S [0,128), dP [128,256), dQ [256, 256 + D)
+};
+
+// Row pass of the backward for N > 128 (the reference's _bwd_dq_kernel, triton_kernels.py:277-339, with the row
+// scalar D computed in the prologue as its _rowdot_kernel does, :171-181): grid (B * H, ceil(N / 128)); the CTA owns
+// 128 query rows, writes D_i to `di` for the column pass, and sweeps double-buffered K / V tiles accumulating
+// dQ = scale * dS K in TMEM.
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1)
+    tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                     const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
+                     T* __restrict__ dq, int H, int N, float scale) {
+  using L = BwdDqLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sDO = smem + L::kDO;
+  unsigned char* sDS = smem + L::kDS;
+  __shared__ uint64_t bar_full[2], bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
+  const int m0 = blockIdx.y * kTile;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
+  const int n_tiles = (N + kTile - 1) / kTile;
+  auto sK = [&](int st) { return smem + (st ? L::kK1 : L::kK0); };
+  auto sV = [&](int st) { return smem + (st ? L::kV1 : L::kV0); };
+  auto load_kv = [&](int jt, int st) {
+    mbar_arrive_expect_tx(&bar_full[st], (jt == 0 ? 4u : 2u) * L::kOp);
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      if (jt == 0) {
+        tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, m0, h, b);
+        tma_load_4d(sDO + hh * kHalfBytes, &tdo, &bar_full[st], hh * 64, m0, h, b);
+      }
+      tma_load_4d(sK(st) + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, jt * kTile, h, b);
+      tma_load_4d(sV(st) + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, jt * kTile, h, b);
+    }
+  };
+
+  if (tid == 0) {
+    mbar_init(&bar_full[0], 1);
+    mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    load_kv(0, 0);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  const int row = m0 + tid;
+  const bool row_ok = row < N;
+  const int64_t grow = static_cast<int64_t>(bh) * N + row;
+  const float Li = row_ok ? lse[grow] : 0.f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  uint32_t ph_mma = 0;
+  float Di = 0.f;
+  bool fail = false;
+
+  for (int jt = 0; jt < n_tiles; ++jt) {
+    const int st = jt & 1;
+    if (tid == 0 && jt + 1 < n_tiles) load_kv(jt + 1, st ^ 1);
+    fail |= !mbar_wait(&bar_full[st], (jt >> 1) & 1, 211);
+    if (__syncthreads_or(fail)) break;
+    if (tid == 0) {
+      tc_fence_after();
+      mma_rows_x_rows<D>(tmem + 0, sQ, sK(st), kIdNN, false);
+      mma_rows_x_rows<D>(tmem + 128, sDO, sV(st), kIdNN, false);
+      mma_commit(&bar_mma);
+    }
+    if (jt == 0 && row_ok) {
+      Di = row_delta<T, D>(sDO, tid, o + grow * D);
+      di_out[grow] = Di;
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 212);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+    softmax_grad_tiles<T, false>(tmem + lane_off, tmem + 128 + lane_off, tid, row_ok, jt * kTile, N, Li, Di, scale,
+                                 nullptr, sDS);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_tile_x_rows(tmem + 256, sDS, sK(st), kIdKM, jt > 0);
+      mma_commit(&bar_mma);
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 213);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+  }
+  if (!fail) {
+    T* none = nullptr;
+    store_row_from_tmem<T, D>(tmem + 256 + lane_off, scale, row_ok ? dq + grow * D : none);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+template <int D>
+struct BwdDkdvLayout {
+  static constexpr int kStages = D == 64 ? 2 : 1;
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
+  static constexpr uint32_t kK = 0, kV = kK + kOp;
+  static constexpr uint32_t kQ0 = kV + kOp, kDO0 = kQ0 + kOp;
+  static constexpr uint32_t kQ1 = kDO0 + kOp, kDO1 = kQ1 + (kStages - 1) * kOp;
+  static constexpr uint32_t kP = kDO1 + (kStages - 1) * kOp, kDS = kP + 2 * kHalfBytes;
+  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;  // S [0,128), dP [128,256), dK [256, 256 + D), dV after dK
+};
+
+// Column pass of the backward for N > 128 (the reference's _bwd_col_kernel, triton_kernels.py:184-274, two-kernel
+// mode): grid (B * H, ceil(N / 128)); the CTA owns 128 keys and sweeps the query tiles (double-buffered for D = 64),
+// recomputing S and dP with the row scalars lse and D from the row pass, and accumulating dV = P^T dO and
+// dK = scale * dS^T Q in TMEM (M = keys: lane t is key t).
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1)
+    tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                       const float* __restrict__ lse, const float* __restrict__ di, T* __restrict__ dk,
+                       T* __restrict__ dv, int H, int N, float scale) {
+  using L = BwdDkdvLayout<D>;
+  constexpr int S = L::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sK = smem + L::kK;
+  unsigned char* sV = smem + L::kV;
+  unsigned char* sP = smem + L::kP;
+  unsigned char* sDS = smem + L::kDS;
+  __shared__ uint64_t bar_full[2], bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
+  const int n0 = blockIdx.y * kTile;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
+  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);
+  const int n_tiles = (N + kTile - 1) / kTile;
+  auto sQ = [&](int st) { return smem + (st ? L::kQ1 : L::kQ0); };
+  auto sDO = [&](int st) { return smem + (st ? L::kDO1 : L::kDO0); };
+  auto load_q = [&](int it, int st) {
+    mbar_arrive_expect_tx(&bar_full[st], (it == 0 ? 4u : 2u) * L::kOp);
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      if (it == 0) {
+        tma_load_4d(sK + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, n0, h, b);
+        tma_load_4d(sV + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, n0, h, b);
+      }
+      tma_load_4d(sQ(st) + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, it * kTile, h, b);
+      tma_load_4d(sDO(st) + hh * kHalfBytes, &tdo, &bar_full[st], hh * 64, it * kTile, h, b);
+    }
+  };
+
+  if (tid == 0) {
+    mbar_init(&bar_full[0], 1);
+    mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    load_q(0, 0);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  uint32_t ph_mma = 0;
+  bool fail = false;
+
+  for (int it = 0; it < n_tiles; ++it) {
+    const int st = (S == 2) ? (it & 1) : 0;
+    if (tid == 0) {
+      if (S == 2 && it + 1 < n_tiles) load_q(it + 1, st ^ 1);
+      if (S == 1 && it > 0) load_q(it, 0);  // the previous tile's products have completed
+    }
+    const int qrow = it * kTile + tid;
+    const bool row_ok = qrow < N;
+    const int64_t gq = static_cast<int64_t>(bh) * N + qrow;
+    const float Li = row_ok ? lse[gq] : 0.f;
+    const float Di = row_ok ? di[gq] : 0.f;
+    fail |= !mbar_wait(&bar_full[st], (S == 2 ? (it >> 1) : it) & 1, 221);
+    if (__syncthreads_or(fail)) break;
+    if (tid == 0) {
+      tc_fence_after();
+      mma_rows_x_rows<D>(tmem + 0, sQ(st), sK, kIdNN, false);
+      mma_rows_x_rows<D>(tmem + 128, sDO(st), sV, kIdNN, false);
+      mma_commit(&bar_mma);
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 222);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+    softmax_grad_tiles<T, true>(tmem + lane_off, tmem + 128 + lane_off, tid, row_ok, n0, N, Li, Di, scale, sP, sDS);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_tileT_x_rows(tmem + 256 + D, sP, sDO(st), kIdMM, it > 0);
+      mma_tileT_x_rows(tmem + 256, sDS, sQ(st), kIdMM, it > 0);
+      mma_commit(&bar_mma);
+    }
+    fail |= !mbar_wait(&bar_mma, ph_mma, 223);
+    ph_mma ^= 1;
+    if (__syncthreads_or(fail)) break;
+    tc_fence_after();
+  }
+  if (!fail) {
+    const int key = n0 + tid;
+    const int64_t gk = static_cast<int64_t>(bh) * N + key;
+    T* none = nullptr;
+    store_row_from_tmem<T, D>(tmem + 256 + lane_off, scale, key < N ? dk + gk * D : none);
+    store_row_from_tmem<T, D>(tmem + 256 + D + lane_off, 1.f, key < N ? dv + gk * D : none);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// ================================================================================================ backward, N <= 128
+
+template <int D>
+struct BwdSingleLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
+  static constexpr uint32_t kQ = 0, kK = kQ + kOp, kV = kK + kOp, kDO = kV + kOp;
+  static constexpr uint32_t kP = kDO + kOp, kDS = kP + 2 * kHalfBytes;
+  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM columns: S [0,128), dP [128,256), dQ [256, 256+D), dK after it; dV after dK for D = 64, in S for D = 128.
+  static constexpr uint32_t cS = 0, cDP = 128, cDQ = 256, cDK = 256 + D, cDV = (D == 64) ? 384 : 0;
+};
+
+// One CTA per (b, h) slice with N <= 128: S and dP once, P and dS to shared memory, then dQ = dS K, dK = dS^T Q and
+// dV = P^T dO from the same tiles (the reference's SINGLE mode, triton_kernels.py:250-264, :742-768).
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1)
+    tc_bwd_single_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                         const T* __restrict__ o, const float* __restrict__ lse, T* __restrict__ dq,
+                         T* __restrict__ dk, T* __restrict__ dv, int H, int N, float scale) {
+  using L = BwdSingleLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sK = smem + L::kK;
+  unsigned char* sV = smem + L::kV;
+  unsigned char* sDO = smem + L::kDO;
+  unsigned char* sP = smem + L::kP;
+  unsigned char* sDS = smem + L::kDS;
+  __shared__ uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);  // S, dP
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);    // dQ = dS K
+  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);    // dK = dS^T Q, dV = P^T dO
+
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&bar_load, 4u * L::kOp);
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh) {
+      tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_load, hh * 64, 0, h, b);
+      tma_load_4d(sK + hh * kHalfBytes, &tk, &bar_load, hh * 64, 0, h, b);
+      tma_load_4d(sV + hh * kHalfBytes, &tv, &bar_load, hh * 64, 0, h, b);
+      tma_load_4d(sDO + hh * kHalfBytes, &tdo, &bar_load, hh * 64, 0, h, b);
+    }
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  // Row statistics of this thread's query row while the tiles land: lse and D = <dO, O> (stored O).
+  const int row = tid;
+  const bool row_ok = row < N;
+  const int64_t grow = static_cast<int64_t>(bh) * N + row;
+  const float Li = row_ok ? lse[grow] : 0.f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  bool fail = !mbar_wait(&bar_load, 0, 201);
+  if (!__syncthreads_or(fail)) {
+    if (tid == 0) {
+      tc_fence_after();
+      mma_rows_x_rows<D>(tmem + L::cS, sQ, sK, kIdNN, false);
+      mma_rows_x_rows<D>(tmem + L::cDP, sDO, sV, kIdNN, false);
+      mma_commit(&bar_mma);
+    }
+    float Di = 0.f;
+    if (row_ok) {
+      const T* orow = o + grow * D;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        float x[8], y[8];
+        ld_row8<T>(sDO, row, c, x);
+        ld_global8<T>(orow + 8 * c, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) Di += x[i] * y[i];
+      }
+    }
+    fail |= !mbar_wait(&bar_mma, 0, 202);
+    if (!__syncthreads_or(fail)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kTile; c += 32) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tmem + L::cS + lane_off + c, rs);
+        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
+        tmem_wait_ld();
+        uint32_t pk[16], dk_[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p[2], ds[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool ok = row_ok && (c + e + u < N);
+            p[u] = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+            ds[u] = p[u] * (__uint_as_float(rp[e + u]) - Di);
+          }
+          pk[e >> 1] = pack2<T>(p[0], p[1]);
+          dk_[e >> 1] = pack2<T>(ds[0], ds[1]);
+        }
+        st_row32(sP, row, c, pk);
+        st_row32(sDS, row, c, dk_);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        mma_tile_x_rows(tmem + L::cDQ, sDS, sK, kIdKM, false);
+        mma_tileT_x_rows(tmem + L::cDK, sDS, sQ, kIdMM, false);
+        mma_tileT_x_rows(tmem + L::cDV, sP, sDO, kIdMM, false);
+        mma_commit(&bar_mma);
+      }
+      fail |= !mbar_wait(&bar_mma, 1, 203);
+      if (!__syncthreads_or(fail)) {
+        tc_fence_after();
+        // Lane t holds query row t of dQ and key row t of dK, dV.
+        T* off = nullptr;
+        store_row_from_tmem<T, D>(tmem + L::cDQ + lane_off, scale, row_ok ? dq + grow * D : off);
+        store_row_from_tmem<T, D>(tmem + L::cDK + lane_off, scale, row_ok ? dk + grow * D : off);
+        store_row_from_tmem<T, D>(tmem + L::cDV + lane_off, 1.f, row_ok ? dv + grow * D : off);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// ================================================================================================ double backward, N <= 128
+
+struct BobSingleLayout {  // D = 64
+  static constexpr uint32_t kOp = kHalfBytes;
+  static constexpr uint32_t kQ = 0, kK = kQ + kOp, kV = kK + kOp, kDO = kV + kOp, kGQ = kDO + kOp,
+                            kGK = kGQ + kOp, kGV = kGK + kOp;
+  static constexpr uint32_t kGS = kGV + kOp, kDS = kGS + 2 * kHalfBytes, kA = kDS + 2 * kHalfBytes;
+  static constexpr uint32_t kBytes = kA + 2 * kHalfBytes;  // 7 * 16 KiB + 3 * 32 KiB = 208 KiB
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  // Phase 1: S [0,128), dP [128,256), G [256,384), R [384,512). Phase 2: packed 16-bit P in [0,64) (written over S
+  // after it is read), hQ [256,320), hdO [320,384), hK [384,448), hV [448,512).
+  static constexpr uint32_t cS = 0, cDP = 128, cG = 256, cR = 384;
+  static constexpr uint32_t cP16 = 0, cHQ = 256, cHDO = 320, cHK = 384, cHV = 448;
+};
+
+// One CTA per (b, h) slice with N <= 128, D = 64: the closed form of reference.py:61-91 in one pass.
+//   S = Q K^T, dP = dO V^T, G = gQ K^T + Q gK^T (scaled), R = dO gV^T           (4 tcgen05 products into TMEM)
+//   per query row: D, e = sum P G, t = sum P gp, then P, dS, A = P (G - e), gS = P (gp - t)
+//   hQ = scale (gS K + dS gK), hdO = A V + P gV, hK = scale (gS^T Q + dS^T gQ), hV = A^T dO   (7 products)
+// gS, dS and A go to shared memory (K-major for hQ / hdO, MN-major for hK / hV); P goes to TMEM for P gV.
+// The reference's Triton kernels do this as a SINGLE column pass (triton_kernels.py:448-551, :878-909).
+template <typename T>
+__global__ void __launch_bounds__(128, 1)
+    tc_bob_single_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                         const __grid_constant__ CUtensorMap tgq, const __grid_constant__ CUtensorMap tgk,
+                         const __grid_constant__ CUtensorMap tgv, const T* __restrict__ o,
+                         const float* __restrict__ lse, T* __restrict__ hq, T* __restrict__ hk,
+                         T* __restrict__ hv, T* __restrict__ hdo, int H, int N, float scale, uint32_t zero_mask) {
+  constexpr int D = 64;
+  using L = BobSingleLayout;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sK = smem + L::kK;
+  unsigned char* sV = smem + L::kV;
+  unsigned char* sDO = smem + L::kDO;
+  unsigned char* sGQ = smem + L::kGQ;
+  unsigned char* sGK = smem + L::kGK;
+  unsigned char* sGV = smem + L::kGV;
+  unsigned char* sGS = smem + L::kGS;
+  unsigned char* sDS = smem + L::kDS;
+  unsigned char* sA = smem + L::kA;
+  __shared__ uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
+  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);
+
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+    // A zero cotangent (bit 0 gq, 1 gk, 2 gv of zero_mask) is not loaded; its tile is cleared below.
+    mbar_arrive_expect_tx(&bar_load, (7u - __popc(zero_mask & 7u)) * L::kOp);
+    tma_load_4d(sQ, &tq, &bar_load, 0, 0, h, b);
+    tma_load_4d(sK, &tk, &bar_load, 0, 0, h, b);
+    tma_load_4d(sV, &tv, &bar_load, 0, 0, h, b);
+    tma_load_4d(sDO, &tdo, &bar_load, 0, 0, h, b);
+    if (!(zero_mask & 1u)) tma_load_4d(sGQ, &tgq, &bar_load, 0, 0, h, b);
+    if (!(zero_mask & 2u)) tma_load_4d(sGK, &tgk, &bar_load, 0, 0, h, b);
+    if (!(zero_mask & 4u)) tma_load_4d(sGV, &tgv, &bar_load, 0, 0, h, b);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+#pragma unroll
+  for (int z = 0; z < 3; ++z) {
+    if (zero_mask & (1u << z)) {
+      uint4* t = reinterpret_cast<uint4*>(z == 0 ? sGQ : (z == 1 ? sGK : sGV));
+      for (int i = tid; i < static_cast<int>(L::kOp / 16); i += 128) t[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  fence_proxy_async_smem();
+  const int row = tid;
+  const bool row_ok = row < N;
+  const int64_t grow = static_cast<int64_t>(bh) * N + row;
+  const float Li = row_ok ? lse[grow] : 0.f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  bool fail = !mbar_wait(&bar_load, 0, 301);
+  if (!__syncthreads_or(fail)) {
+    if (tid == 0) {
+      tc_fence_after();
+      mma_rows_x_rows<D>(tmem + L::cS, sQ, sK, kIdNN, false);
+      mma_rows_x_rows<D>(tmem + L::cDP, sDO, sV, kIdNN, false);
+      mma_rows_x_rows<D>(tmem + L::cG, sGQ, sK, kIdNN, false);
+      mma_rows_x_rows<D>(tmem + L::cG, sQ, sGK, kIdNN, true);
+      mma_rows_x_rows<D>(tmem + L::cR, sDO, sGV, kIdNN, false);
+      mma_commit(&bar_mma);
+    }
+    float Di = 0.f;
+    if (row_ok) {
+      const T* orow = o + grow * D;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        float x[8], y[8];
+        ld_row8<T>(sDO, row, c, x);
+        ld_global8<T>(orow + 8 * c, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) Di += x[i] * y[i];
+      }
+    }
+    fail |= !mbar_wait(&bar_mma, 0, 302);
+    if (!__syncthreads_or(fail)) {
+      tc_fence_after();
+      // Pass 1: e = sum P g, and sum P gp = sum dS g - e sum P dP + sum P r.
+      float e_ = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kTile; c += 16) {
+        uint32_t rs[16], rp[16], rg[16], rr[16];
+        tmem_ld16(tmem + L::cS + lane_off + c, rs);
+        tmem_ld16(tmem + L::cDP + lane_off + c, rp);
+        tmem_ld16(tmem + L::cG + lane_off + c, rg);
+        tmem_ld16(tmem + L::cR + lane_off + c, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const bool ok = row_ok && (c + u < N);
+          const float p = ok ? exp_nat(fmaf(__uint_as_float(rs[u]), scale, -Li)) : 0.f;
+          const float g = __uint_as_float(rg[u]) * scale;
+          const float dp = __uint_as_float(rp[u]);
+          e_ += p * g;
+          c1 += p * (dp - Di) * g;
+          c2 += p * dp;
+          c3 += p * __uint_as_float(rr[u]);
+        }
+      }
+      const float t_ = c1 - e_ * c2 + c3;
+      // Pass 2: the derived tiles. P (16-bit) is packed into TMEM columns [c/2, c/2 + 16) over S columns this thread
+      // has already read.
+#pragma unroll 1
+      for (int c = 0; c < kTile; c += 32) {
+        uint32_t rs[32], rp[32], rg[32], rr[32];
+        tmem_ld32(tmem + L::cS + lane_off + c, rs);
+        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
+        tmem_ld32(tmem + L::cG + lane_off + c, rg);
+        tmem_ld32(tmem + L::cR + lane_off + c, rr);
+        tmem_wait_ld();
+        uint32_t pk_p[16], pk_gs[16], pk_ds[16], pk_a[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p[2], gs[2], ds[2], a[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool ok = row_ok && (c + e + u < N);
+            const float pp = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+            const float g = __uint_as_float(rg[e + u]) * scale;
+            const float dp = __uint_as_float(rp[e + u]);
+            const float gp = (dp - Di) * g - e_ * dp + __uint_as_float(rr[e + u]);
+            p[u] = pp;
+            ds[u] = pp * (dp - Di);
+            a[u] = pp * (g - e_);
+            gs[u] = pp * (gp - t_);
+          }
+          pk_p[e >> 1] = pack2<T>(p[0], p[1]);
+          pk_gs[e >> 1] = pack2<T>(gs[0], gs[1]);
+          pk_ds[e >> 1] = pack2<T>(ds[0], ds[1]);
+          pk_a[e >> 1] = pack2<T>(a[0], a[1]);
+        }
+        st_row32(sGS, row, c, pk_gs);
+        st_row32(sDS, row, c, pk_ds);
+        st_row32(sA, row, c, pk_a);
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          lo[i] = pk_p[i];
+          hi[i] = pk_p[8 + i];
+        }
+        tmem_st8(tmem + L::cP16 + lane_off + (c >> 1), lo);
+        tmem_st8(tmem + L::cP16 + lane_off + (c >> 1) + 8, hi);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        mma_tile_x_rows(tmem + L::cHQ, sGS, sK, kIdKM, false);
+        mma_tile_x_rows(tmem + L::cHQ, sDS, sGK, kIdKM, true);
+        mma_tile_x_rows(tmem + L::cHDO, sA, sV, kIdKM, false);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_ts(tmem + L::cHDO, tmem + L::cP16 + kk * 8, desc_mnmajor(sGV, kk), kIdKM, 1u);
+        mma_tileT_x_rows(tmem + L::cHK, sGS, sQ, kIdMM, false);
+        mma_tileT_x_rows(tmem + L::cHK, sDS, sGQ, kIdMM, true);
+        mma_tileT_x_rows(tmem + L::cHV, sA, sDO, kIdMM, false);
+        mma_commit(&bar_mma);
+      }
+      fail |= !mbar_wait(&bar_mma, 1, 303);
+      if (!__syncthreads_or(fail)) {
+        tc_fence_after();
+        T* none = nullptr;
+        store_row_from_tmem<T, D>(tmem + L::cHQ + lane_off, scale, row_ok ? hq + grow * D : none);
+        store_row_from_tmem<T, D>(tmem + L::cHDO + lane_off, 1.f, row_ok ? hdo + grow * D : none);
+        store_row_from_tmem<T, D>(tmem + L::cHK + lane_off, scale, row_ok ? hk + grow * D : none);
+        store_row_from_tmem<T, D>(tmem + L::cHV + lane_off, 1.f, row_ok ? hv + grow * D : none);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+}  // namespace ebr

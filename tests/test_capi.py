@@ -1,0 +1,96 @@
+"""The C ABI library on the CPU host: it loads, exports every symbol include/ebr_attn.h declares, and rejects bad
+arguments with the documented status codes before touching a device (no compute without a GPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from ebr_b200 import _native
+from ebr_b200.build import OUT, build
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ebr_attn.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _native.lib()
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*|uint64_t)\s+(ebr_attn_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_reference_entry_points():
+    names = declared_functions()
+    for n in ("ebr_attn_fwd", "ebr_attn_bwd", "ebr_attn_bwd_bwd"):
+        assert n in names
+    assert set(_native.EXPORTED) <= set(names)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    assert OUT.exists()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def _op(ptr=0x1000, sb=0, sh=0, sn=64):
+    return _native.Operand(ptr, sb, sh, sn)
+
+
+def test_argument_errors_before_device(lib):
+    q = _op()
+    r = ctypes.byref
+    # D out of range
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1, 1, 4, 0, 0.1, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_SHAPE
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1, 1, 4, 300, 0.1, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_SHAPE
+    # unknown dtype
+    assert lib.ebr_attn_fwd(9, 1, 1, 4, 64, 0.1, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_DTYPE
+    # null operand / output
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1, 1, 4, 64, 0.1, None, r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_NULL
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1, 1, 4, 64, 0.1, r(q), r(q), r(q), None, 0x3000, None) == _native.ERR_NULL
+    # negative stride
+    bad = _op(sn=-64)
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1, 1, 4, 64, 0.1, r(q), r(bad), r(q), 0x2000, 0x3000, None) == _native.ERR_STRIDE
+    # negative size
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, -1, 1, 4, 64, 0.1, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_SHAPE
+    assert lib.ebr_attn_last_error()  # a message was recorded
+
+
+def test_empty_problem_is_a_no_op(lib):
+    q = _op()
+    r = ctypes.byref
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 0, 8, 81, 64, 0.125, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.OK
+    assert lib.ebr_attn_bwd(_native.FLOAT32, 2, 8, 0, 64, 0.125, r(q), r(q), r(q), 0x2, 0x3, r(q), 0x4, 0x5, 0x6,
+                            None, 0, None) == _native.OK  # fmt: skip
+    assert lib.ebr_attn_bwd_bwd(_native.FLOAT32, 2, 0, 5, 64, 0.125, r(q), r(q), r(q), 0x2, 0x3, r(q), None,
+                                None, None, None, 0x4, 0x5, 0x6, 0x7, None, 0, None) == _native.OK  # fmt: skip
+
+
+def test_scratch_sizes(lib):
+    assert lib.ebr_attn_bwd_scratch_bytes(_native.BFLOAT16, 2, 8, 81, 64) == 2 * 8 * 81 * 4
+    assert lib.ebr_attn_bwd_scratch_bytes(_native.FLOAT64, 2, 8, 81, 64) == 2 * 8 * 81 * 8
+    assert lib.ebr_attn_bwd_bwd_scratch_bytes(_native.BFLOAT16, 2, 8, 81, 64) == 3 * 2 * 8 * 81 * 4
+
+
+def test_kernel_family_choice(lib):
+    r = ctypes.byref
+    ok = _op(0x1000, 81 * 64 * 8, 81 * 64, 64)
+    assert lib.ebr_attn_uses_tensor_cores(_native.BFLOAT16, 64, r(ok), r(ok), r(ok)) == 1
+    assert lib.ebr_attn_uses_tensor_cores(_native.FLOAT16, 128, r(ok), r(ok), r(ok)) == 1
+    assert lib.ebr_attn_uses_tensor_cores(_native.FLOAT32, 64, r(ok), r(ok), r(ok)) == 0
+    assert lib.ebr_attn_uses_tensor_cores(_native.BFLOAT16, 32, r(ok), r(ok), r(ok)) == 0
+    odd = _op(0x1000, 81 * 65, 81 * 65, 65)  # token stride not a 16-byte multiple: CUDA-core kernels
+    assert lib.ebr_attn_uses_tensor_cores(_native.BFLOAT16, 64, r(odd), r(ok), r(ok)) == 0
+    misaligned = _op(0x1002, 0, 0, 64)
+    assert lib.ebr_attn_uses_tensor_cores(_native.BFLOAT16, 64, r(misaligned), r(ok), r(ok)) == 0
+
+
+def test_status_strings(lib):
+    assert lib.ebr_attn_status_string(0) == b"ok"
+    assert lib.ebr_attn_status_string(_native.ERR_DEVICE_TIMEOUT) == b"device wait timed out"

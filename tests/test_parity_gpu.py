@@ -1,0 +1,273 @@
+"""GPU parity of the sm_100a attention kernels against the CPU oracle (numpy restatement of reference.py).
+
+Tolerances: with 16-bit I/O the forward output is within 2e-3 max-rel of an fp32 reference on
+top of its own final rounding to the 16-bit type (half an ulp, 2^-8 relative for bf16, 2^-11 for fp16); first- and
+second-order gradients are within 1e-2 max-rel. float32 calls (IEEE CUDA-core kernels) are within 1e-4, float64
+within 1e-10. max-rel is the reference's metric, max|a - r| / max|r| (models/attention.py:156-161).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oracle
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from ebr_b200 import _native, fused_attn
+    from ebr_b200.build import build
+
+    build()
+
+DEV = "cuda"
+FWD_TOL = 2e-3
+GRAD_TOL = 1e-2
+TOL32, TOL64 = 1e-4, 1e-10
+HALF_ULP = {torch.bfloat16: 2.0**-8, torch.float16: 2.0**-11}
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.float()
+    return t.numpy()
+
+
+def _maxrel(a, r) -> float:
+    return oracle.max_rel(_np(a) if isinstance(a, torch.Tensor) else a, r)
+
+
+def check_out(got: torch.Tensor, ref: np.ndarray, dtype, tol16: float, what: str, ulps: float = 0.5,
+              floor: float = 1e-3) -> float:
+    """Assert ``got`` (device) matches the oracle's ``ref``; returns the plain max-rel for the log.
+
+    ``ulps``: 16-bit rounding allowance on top of the tolerance, in units of the type's ulp (0.5 against an unrounded
+    reference, 1 against a reference rounded to the same type). ``floor``: smallest max|ref| used as the denominator,
+    so outputs that are zero up to rounding (N = 1 gives dQ = dK = 0) are measured on the inputs' unit scale.
+    """
+    g = _np(got).astype(np.float64)
+    r = ref.astype(np.float64)
+    assert np.isfinite(g).all(), f"{what}: non-finite output"
+    denom = max(np.abs(r).max(), floor) if r.size else 1.0
+    plain = float(np.abs(g - r).max() / denom) if r.size else 0.0
+    if dtype in HALF_ULP:
+        allow = 2 * ulps * HALF_ULP[dtype]
+        err = float(np.maximum(np.abs(g - r) - allow * np.abs(r), 0).max() / denom) if r.size else 0.0
+        assert err <= tol16, f"{what}: {err:.3e} (plain max-rel {plain:.3e}) > {tol16}"
+    else:
+        tol = TOL64 if dtype == torch.float64 else TOL32
+        assert plain <= tol, f"{what}: max-rel {plain:.3e} > {tol}"
+    return plain
+
+
+def make_inputs(B, H, N, D, dtype, seed=0, layout="contiguous"):
+    """q, k, v (scaled like projected activations), dO, gQ, gK, gV on the device, seeded."""
+    g = torch.Generator().manual_seed(seed)
+    draw = lambda s=1.0: torch.randn(B, H, N, D, generator=g, dtype=torch.float64) * s
+    q, k, v = draw(0.5), draw(0.5), draw(0.5)
+    do, gq, gk, gv = draw(), draw(), draw(), draw()
+    if layout == "qkv":
+        # q / k / v as head-major views of one [B, N, 3 H D] projection, as EnergyAttention produces them.
+        qkv = torch.cat([t.transpose(1, 2).reshape(B, N, H * D) for t in (q, k, v)], dim=-1)
+        qkv = qkv.to(dtype).to(DEV)
+        q, k, v = (x.view(B, N, H, D).transpose(1, 2) for x in qkv.split(H * D, dim=-1))
+    elif layout == "odd":
+        # token stride D + 8 elements keeps 16-byte rows; D + 1 does not (CUDA-core kernels take those).
+        def pad(t):
+            big = torch.zeros(B, H, N, D + 1, dtype=torch.float64)
+            big[..., :D] = t
+            return big.to(dtype).to(DEV)[..., :D]
+
+        q, k, v = pad(q), pad(k), pad(v)
+    else:
+        q, k, v = (t.to(dtype).to(DEV) for t in (q, k, v))
+    do, gq, gk, gv = (t.to(dtype).to(DEV) for t in (do, gq, gk, gv))
+    return q, k, v, do, gq, gk, gv
+
+
+SHAPES_16 = [
+    (2, 3, 81, 64),  # cfg2-like slice count, ragged N
+    (1, 2, 17, 64),
+    (1, 1, 1, 64),
+    (2, 2, 64, 64),
+    (2, 2, 128, 64),
+    (1, 2, 100, 64),
+    (1, 2, 100, 128),
+    (1, 2, 81, 128),
+    (1, 2, 256, 64),
+    (1, 1, 300, 128),
+    (1, 1, 900, 64),
+]
+
+
+def run_all(q, k, v, do, gq, gk, gv, scale):
+    o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, scale)
+    dq, dk, dv = torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, scale)
+    hs = torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, gq, gk, gv, scale)
+    torch.cuda.synchronize()
+    _native.device_status()
+    return o, lse, (dq, dk, dv), hs
+
+
+def oracle_all(q, k, v, do, gq, gk, gv, o, lse, scale):
+    """Oracle on the same (rounded) inputs; the backward passes take the kernel's stored o / lse, as the op chain
+    does (the reference's ops pass the forward's outputs along)."""
+    n = lambda t: _np(t).astype(np.float64 if t.dtype == torch.float64 else np.float32)
+    Q, K, V, DO, GQ, GK, GV = map(n, (q, k, v, do, gq, gk, gv))
+    O, LSE = oracle.attn_fwd(Q, K, V, scale)
+    On, Ln = n(o), _np(lse)
+    grads = oracle.attn_bwd(Q, K, V, On, Ln, DO, scale)
+    hs = oracle.attn_bwd_bwd(Q, K, V, On, Ln, DO, None, GQ, GK, GV, scale)
+    return O, LSE, grads, hs
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", SHAPES_16, ids=lambda s: "x".join(map(str, s)))
+def test_parity_16bit(shape, dtype):
+    B, H, N, D = shape
+    scale = D**-0.5
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=N * 7 + D)
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, scale)
+    O, LSE, G, HS = oracle_all(q, k, v, do, gq, gk, gv, o, lse, scale)
+    check_out(o, O, dtype, FWD_TOL, "o")
+    assert _maxrel(lse, LSE) < 1e-5
+    for name, got, ref in zip(("dq", "dk", "dv"), grads, G):
+        check_out(got, ref, dtype, GRAD_TOL, name)
+    for name, got, ref in zip(("hq", "hk", "hv", "hdo"), hs, HS):
+        check_out(got, ref, dtype, GRAD_TOL, name)
+
+
+@pytest.mark.parametrize("layout", ["qkv", "odd"])
+def test_parity_strided_operands(layout):
+    B, H, N, D = 2, 4, 81, 64
+    dtype = torch.bfloat16
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=3, layout=layout)
+    assert not q.is_contiguous()
+    assert fused_attn.uses_tensor_cores(q, k, v) == (layout == "qkv")
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, D**-0.5)
+    O, LSE, G, HS = oracle_all(q, k, v, do, gq, gk, gv, o, lse, D**-0.5)
+    check_out(o, O, dtype, FWD_TOL, "o")
+    for got, ref in zip((*grads, *hs), (*G, *HS)):
+        check_out(got, ref, dtype, GRAD_TOL, "grad")
+
+
+@pytest.mark.parametrize("dtype,shape", [
+    (torch.float32, (2, 3, 81, 64)),
+    (torch.float32, (1, 2, 33, 16)),
+    (torch.float32, (1, 1, 300, 128)),
+    (torch.float64, (1, 2, 17, 16)),
+    (torch.float64, (1, 1, 130, 64)),
+    (torch.bfloat16, (1, 2, 40, 32)),  # D = 32: CUDA-core kernels
+])  # fmt: skip
+def test_parity_cuda_core_kernels(dtype, shape):
+    B, H, N, D = shape
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=11)
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, D**-0.5)
+    O, LSE, G, HS = oracle_all(q, k, v, do, gq, gk, gv, o, lse, D**-0.5)
+    tol16 = GRAD_TOL
+    check_out(o, O, dtype, FWD_TOL, "o")
+    for got, ref in zip((*grads, *hs), (*G, *HS)):
+        check_out(got, ref, dtype, tol16, "grad")
+
+
+def test_golden_cases_on_device(golden):
+    """The committed reference outputs, reproduced by the kernels on the same inputs."""
+    from tests.conftest import GOLDEN_CASES, golden_case
+
+    tdt = {"float32": torch.float32, "float64": torch.float64, "bfloat16": torch.bfloat16}
+    for name in GOLDEN_CASES:
+        c = golden_case(golden, name)
+        dtype = tdt[c["_dtype"]]
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dtype).to(DEV)
+        q, k, v, do, gq, gk, gv = (dev(c[n]) for n in ("q", "k", "v", "do", "gq", "gk", "gv"))
+        o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, c["_scale"])
+        # The golden outputs are already rounded to the input type: allow one ulp of rounding difference.
+        check_out(o, c["o"], dtype, FWD_TOL, f"{name}/o", ulps=1.0)
+        for n_, got in zip(("dq", "dk", "dv"), grads):
+            check_out(got, c[n_], dtype, GRAD_TOL, f"{name}/{n_}", ulps=1.0)
+        for n_, got in zip(("hq", "hk", "hv", "hdo"), hs):
+            check_out(got, c[n_], dtype, GRAD_TOL, f"{name}/{n_}", ulps=1.0)
+
+
+def test_zero_cotangents_through_c_abi():
+    """NULL gk / gv at the C ABI equal explicit zeros (the reference expands a zero row, triton_kernels.py:868-873)."""
+    import ctypes
+
+    B, H, N, D = 2, 2, 81, 64
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, torch.bfloat16, seed=5)
+    o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, 0.125)
+    dq, _, _ = torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, 0.125)
+    z = torch.zeros_like(q)
+    ref = torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, gq, z, z, 0.125)
+    outs = [torch.empty_like(q) for _ in range(4)]
+    lib = _native.lib()
+    nbytes = lib.ebr_attn_bwd_bwd_scratch_bytes(_native.BFLOAT16, B, H, N, D)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    op = lambda t: _native.Operand(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+    ops = [op(t) for t in (q, k, v, do, gq)]
+    r = ctypes.byref
+    st = lib.ebr_attn_bwd_bwd(_native.BFLOAT16, B, H, N, D, 0.125, r(ops[0]), r(ops[1]), r(ops[2]), o.data_ptr(),
+                              lse.data_ptr(), r(ops[3]), dq.data_ptr(), r(ops[4]), None, None,
+                              *[t.data_ptr() for t in outs], scratch.data_ptr(), nbytes,
+                              torch.cuda.current_stream().cuda_stream)  # fmt: skip
+    assert st == 0
+    torch.cuda.synchronize()
+    for a, b in zip(outs, ref):
+        assert torch.equal(a, b)
+
+
+def test_autograd_second_order_matches_oracle():
+    """fused_attention with create_graph=True, then the gradient of <dQ, R> (bf16 and fp32)."""
+    for dtype in (torch.bfloat16, torch.float32):
+        B, H, N, D = 4, 8, 81, 64
+        q0, k0, v0, do, r, _, _ = make_inputs(B, H, N, D, dtype, seed=0)
+        q, k, v = (t.detach().clone().requires_grad_(True) for t in (q0, k0, v0))
+        o = fused_attn.fused_attention(q, k, v)
+        dq, dk, dv = torch.autograd.grad(o, (q, k, v), grad_outputs=do, create_graph=True)
+        hq, hk, hv = torch.autograd.grad((dq * r).sum(), (q, k, v))
+        n = lambda t: _np(t).astype(np.float32)
+        Q, K, V, DO, R = map(n, (q0, k0, v0, do, r))
+        O, L = oracle.attn_fwd(Q, K, V, 0.125)
+        On = n(o)
+        G = oracle.attn_bwd(Q, K, V, On, L, DO, 0.125)
+        HS = oracle.attn_bwd_bwd(Q, K, V, On, L, DO, None, R, None, None, 0.125)
+        check_out(o, O, dtype, FWD_TOL, "o")
+        for got, ref in zip((dq, dk, dv, hq, hk, hv), (*G, *HS[:3])):
+            check_out(got, ref, dtype, GRAD_TOL, "autograd")
+
+
+def test_deterministic():
+    q, k, v, do, gq, gk, gv = make_inputs(3, 4, 100, 64, torch.bfloat16, seed=9)
+    a = run_all(q, k, v, do, gq, gk, gv, 0.125)
+    b = run_all(q, k, v, do, gq, gk, gv, 0.125)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    for x, y in zip((*a[2], *a[3]), (*b[2], *b[3])):
+        assert torch.equal(x, y)
+
+
+def test_compiled_func_grad_smoke():
+    """torch.compile(torch.func.grad(...)) traces the ops as opaque nodes (the reference's energy_compile path)."""
+    q, k, v, *_ = make_inputs(2, 2, 81, 64, torch.bfloat16, seed=1)
+
+    def energy(x):
+        return fused_attn.fused_attention(x, k, v).float().square().sum()
+
+    eager = torch.func.grad(energy)(q)
+    compiled = torch.compile(torch.func.grad(energy), backend="aot_eager")(q)
+    assert torch.equal(eager, compiled)
+
+
+def test_large_batch_slices():
+    """Many (b, h) slices in one launch (grid x = B * H), cfg2-sized head count."""
+    B, H, N, D = 96, 8, 81, 64
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, torch.bfloat16, seed=21)
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, 0.125)
+    sel = slice(90, 96)
+    sub = lambda t: t[sel]
+    O, LSE, G, HS = oracle_all(*(sub(t) for t in (q, k, v, do, gq, gk, gv)), sub(o), sub(lse), 0.125)
+    check_out(sub(o), O, torch.bfloat16, FWD_TOL, "o")
+    for got, ref in zip((*grads, *hs), (*G, *HS)):
+        check_out(sub(got), ref, torch.bfloat16, GRAD_TOL, "grad")
