@@ -29,6 +29,7 @@ EXPORTED = (
     "ebr_attn_status_string",
     "ebr_attn_last_error",
     "ebr_attn_launch_count",
+    "ebr_attn_bwd_noalloc",
 )
 
 
@@ -65,6 +66,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         sz,
         vp,
     ]
+    lib.ebr_attn_bwd_noalloc.argtypes = dims + [ctypes.c_double, op, op, op, vp, vp, op, vp, vp, vp, vp]
+    lib.ebr_attn_bwd_noalloc.restype = ctypes.c_int
     lib.ebr_attn_bwd_scratch_bytes.argtypes = dims
     lib.ebr_attn_bwd_scratch_bytes.restype = sz
     lib.ebr_attn_bwd_bwd_scratch_bytes.argtypes = dims

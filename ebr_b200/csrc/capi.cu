@@ -327,6 +327,26 @@ int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N,
   return check_launch("tc_bob_single_kernel");
 }
 
+// Built-in row scratch of ebr_attn_bwd_noalloc (see include/ebr_attn.h). Host code must not pass the symbol itself
+// to a kernel: it names a host-side stand-in. noalloc_scratch() returns this device's address of it.
+static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[EBR_ATTN_NOALLOC_SCRATCH_BYTES];
+
+// The device address of g_bwd_noalloc_scratch on `device` (the current device), looked up once per device.
+int noalloc_scratch(int device, void** out) {
+  static std::mutex mu;
+  static void* ptrs[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return set_error(EBR_ERR_DEVICE, "device index out of range%s%s");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_error(e, "cudaGetSymbolAddress(g_bwd_noalloc_scratch)");
+    ptrs[device] = p;
+  }
+  *out = ptrs[device];
+  return EBR_OK;
+}
+
 }  // namespace
 
 // ================================================================================================ C ABI
@@ -475,6 +495,31 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
       return launch_simt_bob<__half>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout, scratch,
                                      st);
   }
+}
+
+int ebr_attn_bwd_noalloc(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double scale,
+                         const ebr_operand* q, const ebr_operand* k, const ebr_operand* v, const void* o,
+                         const void* lse, const ebr_operand* dout, void* dq, void* dk, void* dv, void* stream) {
+  int s;
+  if ((s = check_shape(dtype, B, H, N, D)) || (s = check_operand(q, "q")) || (s = check_operand(k, "k")) ||
+      (s = check_operand(v, "v")) || (s = check_operand(dout, "dout")))
+    return s;
+  if (!o || !lse || !dq || !dk || !dv) return set_error(EBR_ERR_NULL, "o / lse / output pointer is NULL%s%s");
+  if (B * H * N == 0) return EBR_OK;
+  const size_t need = ebr_attn_bwd_scratch_bytes(dtype, B, H, N, D);
+  if (need > EBR_ATTN_NOALLOC_SCRATCH_BYTES) {
+    std::snprintf(g_last_error, sizeof(g_last_error),
+                  "ebr_attn_bwd_noalloc: B*H*N = %lld rows need %zu bytes of row scratch; the built-in buffer holds "
+                  "%zu bytes (use ebr_attn_bwd with a caller-provided buffer)",
+                  static_cast<long long>(B * H * N), need, static_cast<size_t>(EBR_ATTN_NOALLOC_SCRATCH_BYTES));
+    return EBR_ERR_SCRATCH;
+  }
+  int device = 0;
+  if ((s = check_device(&device))) return s;
+  void* scratch = nullptr;
+  if ((s = noalloc_scratch(device, &scratch))) return s;
+  return ebr_attn_bwd(dtype, B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch,
+                      EBR_ATTN_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int ebr_attn_device_status(void) {

@@ -93,6 +93,26 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
                      const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
                      void* hq, void* hk, void* hv, void* hdout, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Allocation-free variant of ebr_attn_bwd. No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory at call time, for example a host program whose GPU memory is handed out up front by another
+ * allocator (a serving runtime with a fixed memory plan), or a plugin host that passes a plugin only its input and
+ * output buffers and no workspace. Instead of a caller-provided scratch buffer it uses a built-in device buffer of
+ * EBR_ATTN_NOALLOC_SCRATCH_BYTES (8 MiB), a static array that every GPU which loads the library holds until the
+ * process exits. It calls no allocator of any kind.
+ *   - Limit: the row scratch needs B*H*N*4 bytes (B*H*N*8 for float64), so B*H*N <= 2,097,152 rows (1,048,576 for
+ *     float64). Larger calls return EBR_ERR_SCRATCH before any launch.
+ *   - The first call on a device looks up that device's address of the buffer (cudaGetSymbolAddress); make that first
+ *     call before any stream capture.
+ *   - All calls share the one buffer per device and it keeps the last call's contents (every value a call reads is
+ *     written earlier in the same call). Calls whose executions overlap on the GPU (for example on two streams) race
+ *     on it: serialize them.
+ * Arguments and results are those of ebr_attn_bwd without scratch / scratch_bytes. */
+#define EBR_ATTN_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int ebr_attn_bwd_noalloc(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double scale,
+                         const ebr_operand* q, const ebr_operand* k, const ebr_operand* v,
+                         const void* o, const void* lse, const ebr_operand* dout,
+                         void* dq, void* dk, void* dv, void* stream);
+
 /* Which kernel family a call with these arguments would use: 1 = tcgen05 tensor-core kernels, 0 = the CUDA-core
  * kernels (float32 / float64, and half types whose shape or strides the tensor-core path does not take). */
 int ebr_attn_uses_tensor_cores(int dtype, int64_t D, const ebr_operand* q, const ebr_operand* k,
