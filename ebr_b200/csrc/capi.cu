@@ -52,7 +52,7 @@ int check_device(int* device_out) {
 
 // Raise a kernel's dynamic shared memory limit once per device, and refuse a launch shape under which more CTAs
 // could share an SM than its tensor memory (512 columns) can serve: tcgen05.alloc would then block.
-int prepare_tc_kernel(const void* kernel, int device, uint32_t smem, uint32_t tmem_cols) {
+int prepare_tc_kernel(const void* kernel, int device, uint32_t smem, uint32_t tmem_cols, int threads = 128) {
   static std::mutex mu;
   static std::map<std::pair<const void*, int>, int> verdicts;
   std::lock_guard<std::mutex> lock(mu);
@@ -61,7 +61,7 @@ int prepare_tc_kernel(const void* kernel, int device, uint32_t smem, uint32_t tm
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
   int blocks = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, 128, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem);
   if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   const int verdict = (blocks >= 1 && static_cast<uint32_t>(blocks) * tmem_cols <= 512u)
                           ? EBR_OK
@@ -146,8 +146,10 @@ bool tc_operand_ok(const ebr_operand* op, int64_t B, int64_t H, int64_t N) {
          tma_stride_ok(op->stride_b, B) && (op->stride_n > 0 || N <= 1);
 }
 
-// [B, H, N, D] 16-bit operand -> 4-D tensor map (D, N, H, B), box 64 x 128 x 1 x 1, 128-byte swizzle, zero fill.
-int make_tile_map(CUtensorMap* map, const ebr_operand* op, int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
+// [B, H, N, D] 16-bit operand -> 4-D tensor map (D, N, H, B), box 64 x box_rows x 1 x 1, 128-byte swizzle, zero
+// fill outside the tensor.
+int make_tile_map(CUtensorMap* map, const ebr_operand* op, int dtype, int64_t B, int64_t H, int64_t N, int64_t D,
+                  uint32_t box_rows = 128) {
   EncodeTiled enc = encode_fn();
   if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
   auto fix = [](int64_t stride, int64_t extent) -> cuuint64_t {
@@ -156,7 +158,7 @@ int make_tile_map(CUtensorMap* map, const ebr_operand* op, int dtype, int64_t B,
   const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H),
                               static_cast<cuuint64_t>(B)};
   const cuuint64_t strides[3] = {fix(op->stride_n, N), fix(op->stride_h, H), fix(op->stride_b, B)};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t box[4] = {64, box_rows, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                    const_cast<void*>(op->data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -208,6 +210,38 @@ int launch_tc_fwd(int device, int dtype, int64_t B, int64_t H, int64_t N, double
   return check_launch("tc_fwd_kernel");
 }
 
+int sm_count(int device) {
+  static std::atomic<int> counts[kMaxDevices];
+  int c = counts[device].load();
+  if (c == 0) {
+    cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, device);
+    if (c <= 0) c = 148;
+    counts[device].store(c);
+  }
+  return c;
+}
+
+template <typename T, int D>
+int launch_tc_fwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                       const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
+  using L = FwdPipeLayout<D>;
+  CUtensorMap tq, tk, tv;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D))
+    return kNoTensorMap;
+  const void* fn = reinterpret_cast<const void*>(tc_fwd_pipe_kernel<T, D>);
+  int s = prepare_tc_kernel(fn, device, L::kSmem, L::kTmemCols, L::kThreads);
+  if (s) return s;
+  const int64_t items = B * H * ((N + kTile - 1) / kTile);
+  const int64_t cap = static_cast<int64_t>(L::kCtasPerSm) * sm_count(device);
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  tc_fwd_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, static_cast<T*>(o),
+                                                                 static_cast<float*>(lse), static_cast<int>(B * H),
+                                                                 static_cast<int>(H), static_cast<int>(N),
+                                                                 static_cast<float>(scale));
+  return check_launch("tc_fwd_pipe_kernel");
+}
+
 // ------------------------------------------------------------------------------------------------ backward
 
 template <typename T>
@@ -243,6 +277,38 @@ int launch_tc_bwd_single(int device, int dtype, int64_t B, int64_t H, int64_t N,
       tq, tk, tv, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(dq),
       static_cast<T*>(dk), static_cast<T*>(dv), static_cast<int>(H), static_cast<int>(N), static_cast<float>(scale));
   return check_launch("tc_bwd_single_kernel");
+}
+
+template <typename T, int D>
+int launch_tc_bwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                       const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                       const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, cudaStream_t st) {
+  using L = BwdPipeLayout<D>;
+  CUtensorMap tq, tk, tv, tdo, tq64, tk64, tv64, tdo64;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D) ||
+      make_tile_map(&tq64, q, dtype, B, H, N, D, 64) || make_tile_map(&tk64, k, dtype, B, H, N, D, 64) ||
+      make_tile_map(&tv64, v, dtype, B, H, N, D, 64) || make_tile_map(&tdo64, dout, dtype, B, H, N, D, 64))
+    return kNoTensorMap;
+  const void* fq = reinterpret_cast<const void*>(tc_bwd_dq_pipe_kernel<T, D>);
+  const void* fk = reinterpret_cast<const void*>(tc_bwd_dkdv_pipe_kernel<T, D>);
+  int s = prepare_tc_kernel(fq, device, L::kSmem, 256, L::kThreads);
+  if (s) return s;
+  s = prepare_tc_kernel(fk, device, L::kSmem, D == 64 ? 256 : 512, L::kThreads);
+  if (s) return s;
+  const int64_t items = B * H * ((N + kTile - 1) / kTile);
+  const int64_t cap = static_cast<int64_t>(L::kCtasPerSm) * sm_count(device);
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  float* di = static_cast<float*>(scratch);
+  const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
+  tc_bwd_dq_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+      tq, tk64, tv64, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), di, static_cast<T*>(dq), BH, Hi,
+      Ni, static_cast<float>(scale));
+  if ((s = check_launch("tc_bwd_dq_pipe_kernel"))) return s;
+  tc_bwd_dkdv_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+      tk, tv, tq64, tdo64, static_cast<const float*>(lse), di, static_cast<T*>(dk), static_cast<T*>(dv), BH, Hi, Ni,
+      static_cast<float>(scale));
+  return check_launch("tc_bwd_dkdv_pipe_kernel");
 }
 
 template <typename T, int D>
@@ -372,11 +438,11 @@ int ebr_attn_fwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double s
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (tc_eligible(dtype, D, {q, k, v}, B, H, N) && aligned16(o)) {
     if (dtype == EBR_BFLOAT16)
-      s = D == 64 ? launch_tc_fwd<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                  : launch_tc_fwd<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+      s = D == 64 ? launch_tc_fwd_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                  : launch_tc_fwd_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
     else
-      s = D == 64 ? launch_tc_fwd<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                  : launch_tc_fwd<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+      s = D == 64 ? launch_tc_fwd_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                  : launch_tc_fwd_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
     if (s != kNoTensorMap) return s;
   }
   switch (dtype) {
@@ -410,15 +476,15 @@ int ebr_attn_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double s
   const bool scratch_ok = scratch && scratch_bytes >= ebr_attn_bwd_scratch_bytes(dtype, B, H, N, D);
   if (N > kTile && scratch_ok && outs_ok && tc_eligible(dtype, D, {q, k, v, dout}, B, H, N)) {
     if (dtype == EBR_BFLOAT16)
-      s = D == 64 ? launch_tc_bwd_tiled<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
-                                                            dk, dv, scratch, st)
-                  : launch_tc_bwd_tiled<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
-                                                             dk, dv, scratch, st);
+      s = D == 64 ? launch_tc_bwd_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+                                                           dk, dv, scratch, st)
+                  : launch_tc_bwd_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+                                                            dk, dv, scratch, st);
     else
-      s = D == 64 ? launch_tc_bwd_tiled<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk, dv,
-                                                    scratch, st)
-                  : launch_tc_bwd_tiled<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
-                                                     dv, scratch, st);
+      s = D == 64 ? launch_tc_bwd_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk, dv,
+                                                   scratch, st)
+                  : launch_tc_bwd_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+                                                    dv, scratch, st);
     if (s != kNoTensorMap) return s;
   }
   if (N <= kTile && outs_ok && tc_eligible(dtype, D, {q, k, v, dout}, B, H, N)) {

@@ -79,6 +79,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   }
 }
 
+// As mbar_wait, but also gives up at once when another role of the CTA has raised `*abort` (so one failed wait does
+// not leave the other roles waiting out their own limits), and raises it on its own failure.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int site, volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(&g_device_error, site);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ TMA
 
 // 4-D tiled TMA load into shared memory, completing `bytes` of transaction count on `bar`. No multicast.

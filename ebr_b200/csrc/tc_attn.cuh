@@ -295,6 +295,255 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
 }
 
+// ================================================================================================ forward (pipelined)
+
+template <int D>
+struct FwdPipeLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;  // one [128 x D] 16-bit tile
+  static constexpr int kStages = 2;                       // K / V ring depth
+  static constexpr uint32_t kQ0 = 0;                      // Q double buffer: kQ0, kQ0 + kOp
+  static constexpr uint32_t kKV = 2 * kOp;                // stage s: K at kKV + 2 s kOp, V at + kOp
+  static constexpr uint32_t kBytes = kKV + kStages * 2 * kOp;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 256;              // S / P: [0, 128), O: [128, 128 + D)
+  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+  static constexpr int kThreads = 192;
+};
+
+// Forward for any N, persistent and warp-specialized (2 CTAs per SM at D = 64, so one CTA's MMAs run under the
+// other's softmax):
+//   warps 0-3  softmax: thread t owns query row t of the current tile (TMEM lane t);
+//   warp 4     TMA producer: Q tile per item (double-buffered), K / V tiles into a 2-stage ring;
+//   warp 5     MMA issuer: S = Q K^T into TMEM, then O += P V with P read from TMEM (tcgen05.mma A-from-TMEM).
+// An item is one 128-row query tile of one (b, h) slice; a CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...
+// with the query tile fastest, so the CTAs working on one slice at the same time share its K / V through L2.
+// Per key tile the softmax warps write P as a 16-bit hi / lo pair over the S columns they have read (P_hi in
+// [c, c + 16), P_lo in [c + 16, c + 32) of each 32-column chunk c) and the MMA warp accumulates O += P_hi V + P_lo V in
+// TMEM. The running max is updated lazily: O and l are rescaled only when a tile's max exceeds the max in use by
+// more than 8 (in log2 units), so P stays below 256 and the common case touches O not at all. O / l and
+// lse = m + log l at the end of the item. Same math as the reference's _fwd_kernel (triton_kernels.py:98-163).
+template <typename T, int D>
+__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+    tc_fwd_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, T* __restrict__ out, float* __restrict__ lse, int BH,
+                       int H, int N, float scale) {
+  using L = FwdPipeLayout<D>;
+  constexpr int NS = L::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_kt = (N + kTile - 1) / kTile;
+  const int64_t items = static_cast<int64_t>(BH) * n_kt;  // query tiles: ceil(N / 128) per slice
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdS = idesc_f16(kB, 0, 0, 128, 128);
+  constexpr uint32_t kIdPV = idesc_f16(kB, 0, 1, 128, D);
+  constexpr float kTau = 5.545177444479562f;  // 8 ln 2: lazy-rescale threshold in natural units
+  auto sQ = [&](int b) { return smem + L::kQ0 + b * L::kOp; };
+  auto sK = [&](int s) { return smem + L::kKV + s * 2 * L::kOp; };
+  auto sV = [&](int s) { return smem + L::kKV + s * 2 * L::kOp + L::kOp; };
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      uint32_t kv_use = 0;
+      int64_t li = 0;
+      for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++li) {
+        const int bh = static_cast<int>(it / n_kt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
+        const int b = bh / H, h = bh - (bh / H) * H;
+        const int qb = static_cast<int>(li & 1);
+        if (!mbar_wait_or_abort(&q_empty[qb], ((li >> 1) & 1) ^ 1, 111, abort)) break;
+        mbar_arrive_expect_tx(&q_full[qb], L::kOp);
+        for (int hh = 0; hh < D / 64; ++hh)
+          tma_load_4d(sQ(qb) + hh * kHalfBytes, &tq, &q_full[qb], hh * 64, qt * kTile, h, b);
+        bool ok = true;
+        for (int j = 0; j < n_kt && ok; ++j, ++kv_use) {
+          const int s = static_cast<int>(kv_use % NS);
+          const uint32_t u = kv_use / NS;
+          ok = mbar_wait_or_abort(&kv_empty[s], (u & 1) ^ 1, 112, abort);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::kOp);
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_4d(sK(s) + hh * kHalfBytes, &tk, &kv_full[s], hh * 64, j * kTile, h, b);
+            tma_load_4d(sV(s) + hh * kHalfBytes, &tv, &kv_full[s], hh * 64, j * kTile, h, b);
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t tS = tmem, tO = tmem + 128;
+      uint32_t kv_use = 0, t = 0;
+      int64_t li = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int qb = static_cast<int>(li & 1);
+        ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 121, abort);
+        for (int j = 0; j < n_kt && ok; ++j, ++kv_use, ++t) {
+          const int s = static_cast<int>(kv_use % NS);
+          ok = mbar_wait_or_abort(&kv_full[s], (kv_use / NS) & 1, 122, abort);
+          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 123, abort);  // S / P columns free
+          if (!ok) break;
+          tc_fence_after();
+          mma_rows_x_rows<D>(tS, sQ(qb), sK(s), kIdS, false);
+          mma_commit(&s_full);
+          if (j == n_kt - 1) mma_commit(&q_empty[qb]);
+          ok = mbar_wait_or_abort(&p_full, t & 1, 124, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint32_t a_hi = tS + (kk >> 1) * 32 + (kk & 1) * 8;
+            const uint64_t bdesc = desc_mnmajor(sV(s), kk);
+            mma_ts(tO, a_hi, bdesc, kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tO, a_hi + 16, bdesc, kIdPV, 1u);
+          }
+          mma_commit(&o_done);
+          mma_commit(&kv_empty[s]);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax / epilogue (warps 0-3)
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tO = tmem + 128 + lane_off;
+    uint32_t t = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int bh = static_cast<int>(it / n_kt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
+      const int row = qt * kTile + tid;
+      float m_used = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < n_kt; ++j, ++t) {
+        ok = mbar_wait_or_abort(&s_full, t & 1, 131, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int j0 = j * kTile;
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kTile; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tS + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (j0 + c + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * scale);
+        }
+        // Lazy rescale. tcgen05.ld / st are warp-collective, so the decision is made per warp: if any row of the warp
+        // needs it, the whole warp rewrites its O rows, with alpha = 1 for the rows that keep their max. The previous
+        // P V product has completed (S of this tile was issued after it), so O can be rewritten.
+        const bool need = (j == 0) || (mx > m_used + kTau);
+        if (j == 0) {
+          m_used = mx;
+        } else if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? exp_nat(m_used - mx) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tO + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            uint32_t a[8], b8[8], c8[8], d8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              a[e] = r[e];
+              b8[e] = r[8 + e];
+              c8[e] = r[16 + e];
+              d8[e] = r[24 + e];
+            }
+            tmem_st8(tO + c, a);
+            tmem_st8(tO + c + 8, b8);
+            tmem_st8(tO + c + 16, c8);
+            tmem_st8(tO + c + 24, d8);
+          }
+          if (need) {
+            l_run *= alpha;
+            m_used = mx;
+          }
+        }
+        float psum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTile; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tS + c, r);
+          tmem_wait_ld();
+          uint32_t hi[8], hi2[8], lo[8], lo2[8];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = (j0 + c + e < N) ? exp_nat(__uint_as_float(r[e]) * scale - m_used) : 0.f;
+            const float p1 = (j0 + c + e + 1 < N) ? exp_nat(__uint_as_float(r[e + 1]) * scale - m_used) : 0.f;
+            psum += p0 + p1;
+            const float h0 = round16<T>(p0), h1 = round16<T>(p1);
+            const uint32_t ph = pack2<T>(h0, h1), pl = pack2<T>(p0 - h0, p1 - h1);
+            if (e < 16) {
+              hi[e >> 1] = ph;
+              lo[e >> 1] = pl;
+            } else {
+              hi2[(e - 16) >> 1] = ph;
+              lo2[(e - 16) >> 1] = pl;
+            }
+          }
+          tmem_st8(tS + c, hi);
+          tmem_st8(tS + c + 8, hi2);
+          tmem_st8(tS + c + 16, lo);
+          tmem_st8(tS + c + 24, lo2);
+        }
+        l_run += psum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full);
+      }
+      if (!ok) break;
+      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 132, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      T* none = nullptr;
+      const bool row_ok = row < N;
+      const int64_t grow = static_cast<int64_t>(bh) * N + row;
+      store_row_from_tmem<T, D>(tO, 1.f / l_run, row_ok ? out + grow * D : none);
+      if (row_ok) lse[grow] = m_used + logf(l_run);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
 // ================================================================================================ backward, N > 128
 
 // Shared helper: thread `row`'s D_i = <dO_i, O_i> from the TMA-staged dO tile and the stored (contiguous) O.
@@ -584,6 +833,406 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// ================================================================================================ backward (pipelined)
+
+// Descriptors for tiles of `rows` rows (64 or 128): the 64-column halves of a D = 128 tile are rows * 128 B apart.
+__device__ __forceinline__ uint64_t desc_kmajor_r(const unsigned char* tile, int kk, uint32_t half_bytes) {
+  return sw128_desc(smem_u32(tile) + (kk >> 2) * half_bytes + (kk & 3) * 32u, 16u, 1024u);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor_r(const unsigned char* tile, int kk, uint32_t half_bytes) {
+  return sw128_desc(smem_u32(tile) + kk * 2048u, half_bytes, 1024u);
+}
+
+template <int D>
+struct BwdPipeLayout {
+  static constexpr uint32_t kHalf64 = 64u * 128u;              // [64 x 64] 16-bit tile
+  static constexpr uint32_t kBig = (D / 64) * kHalfBytes;      // [128 x D] tile
+  static constexpr uint32_t kSmall = (D / 64) * kHalf64;       // [64 x D] tile
+  static constexpr int kStages = 2;
+  // Big-tile pair (double-buffered per item): buffer b holds tiles at kBigPair + b * 2 kBig and + kBig.
+  static constexpr uint32_t kBigPair = 0;
+  static constexpr uint32_t kRing = 4 * kBig;                  // stage s: small tiles at kRing + s * 2 kSmall, + kSmall
+  static constexpr uint32_t kStats = kRing + kStages * 2 * kSmall;  // [2][2][64] floats (column-pass row scalars)
+  static constexpr uint32_t kBytes = kStats + 2 * 2 * 64 * 4;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+  static constexpr int kThreads = 192;
+};
+
+// Row pass of the backward for N > 128, persistent and warp-specialized like the forward: an item is 128 query rows
+// of one slice (Q, dO double-buffered per item); the key tiles stream through a 2-stage ring in steps of 64 keys.
+// Per step: S = Q K^T and dP = dO V^T (M = 128 queries, N = 64 keys) into TMEM; the compute warps (thread t = query
+// row t) form dS = P (dP - D) with P = exp(fma(s, scale, -lse)), pack it to 16 bits over the S columns they have
+// read, and the MMA warp accumulates dQ += dS K with dS read from TMEM. D_i = <dO_i, O_i> is computed at the start of
+// each item (stored O) and written to `di` for the column pass. The reference's _bwd_dq_kernel + _rowdot_kernel
+// (triton_kernels.py:277-339, :171-181). TMEM: S [0, 64), dP [64, 128), dQ [128, 128 + D).
+template <typename T, int D>
+__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+    tc_bwd_dq_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk64,
+                          const __grid_constant__ CUtensorMap tv64, const __grid_constant__ CUtensorMap tdo,
+                          const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
+                          T* __restrict__ dq, int BH, int H, int N, float scale) {
+  using L = BwdPipeLayout<D>;
+  constexpr int NS = L::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_qt = (N + kTile - 1) / kTile, n_ks = (N + 63) / 64;
+  const int64_t items = static_cast<int64_t>(BH) * n_qt;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 64);
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
+  auto sQ = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig; };
+  auto sDO = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig + L::kBig; };
+  auto sK = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
+  auto sV = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      uint32_t kv_use = 0;
+      int64_t li = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
+        const int b = bh / H, h = bh - (bh / H) * H;
+        const int qb = static_cast<int>(li & 1);
+        ok = mbar_wait_or_abort(&q_empty[qb], ((li >> 1) & 1) ^ 1, 241, abort);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * L::kBig);
+        for (int hh = 0; hh < D / 64; ++hh) {
+          tma_load_4d(sQ(qb) + hh * kHalfBytes, &tq, &q_full[qb], hh * 64, qt * kTile, h, b);
+          tma_load_4d(sDO(qb) + hh * kHalfBytes, &tdo, &q_full[qb], hh * 64, qt * kTile, h, b);
+        }
+        for (int j = 0; j < n_ks; ++j, ++kv_use) {
+          const int s = static_cast<int>(kv_use % NS);
+          ok = mbar_wait_or_abort(&kv_empty[s], ((kv_use / NS) & 1) ^ 1, 242, abort);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::kSmall);
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_4d(sK(s) + hh * L::kHalf64, &tk64, &kv_full[s], hh * 64, j * 64, h, b);
+            tma_load_4d(sV(s) + hh * L::kHalf64, &tv64, &kv_full[s], hh * 64, j * 64, h, b);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t tS = tmem, tDP = tmem + 64, tDQ = tmem + 128;
+      uint32_t kv_use = 0, t = 0;
+      int64_t li = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int qb = static_cast<int>(li & 1);
+        ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 251, abort);
+        for (int j = 0; j < n_ks && ok; ++j, ++kv_use, ++t) {
+          const int s = static_cast<int>(kv_use % NS);
+          ok = mbar_wait_or_abort(&kv_full[s], (kv_use / NS) & 1, 252, abort);
+          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 253, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            mma_ss(tS, desc_kmajor(sQ(qb), kk), desc_kmajor_r(sK(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
+            mma_ss(tDP, desc_kmajor(sDO(qb), kk), desc_kmajor_r(sV(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full);
+          if (j == n_ks - 1) mma_commit(&q_empty[qb]);
+          ok = mbar_wait_or_abort(&p_full, t & 1, 254, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tDQ, tS + kk * 8, desc_mnmajor_r(sK(s), kk, L::kHalf64), kIdKM, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&o_done);
+          mma_commit(&kv_empty[s]);
+        }
+      }
+    }
+  } else {
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tDP = tmem + 64 + lane_off, tDQ = tmem + 128 + lane_off;
+    uint32_t t = 0;
+    int64_t li = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+      const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
+      const int qb = static_cast<int>(li & 1);
+      const int row = qt * kTile + tid;
+      const bool row_ok = row < N;
+      const int64_t grow = static_cast<int64_t>(bh) * N + row;
+      const float Li = row_ok ? lse[grow] : 0.f;
+      ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 261, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      float Di = 0.f;
+      if (row_ok) {
+        Di = row_delta<T, D>(sDO(qb), tid, o + grow * D);
+        di_out[grow] = Di;
+      }
+      for (int j = 0; j < n_ks; ++j, ++t) {
+        ok = mbar_wait_or_abort(&s_full, t & 1, 262, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t rs[32], rp[32];
+          tmem_ld32(tS + c, rs);
+          tmem_ld32(tDP + c, rp);
+          tmem_wait_ld();
+          uint32_t a[8], b8[8];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const bool okk = row_ok && (j * 64 + c + e + u < N);
+              const float p = okk ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+              ds[u] = p * (__uint_as_float(rp[e + u]) - Di);
+            }
+            const uint32_t pk = pack2<T>(ds[0], ds[1]);
+            if (e < 16) a[e >> 1] = pk;
+            else b8[(e - 16) >> 1] = pk;
+          }
+          tmem_st8(tS + (c >> 1), a);
+          tmem_st8(tS + (c >> 1) + 8, b8);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full);
+      }
+      if (!ok) break;
+      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 263, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      T* none = nullptr;
+      store_row_from_tmem<T, D>(tDQ, scale, row_ok ? dq + grow * D : none);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// Column pass of the backward for N > 128: an item is 128 keys of one slice (K, V double-buffered per item); the
+// query tiles stream through a 2-stage ring in steps of 64 queries. Per step: S^T = K Q^T and dP^T = V dO^T
+// (M = 128 keys, N = 64 queries) into TMEM; the compute warps (thread t = key t) form P^T and dS^T with the queries'
+// lse and D staged in shared memory, pack both to 16 bits over the columns they have read, and the MMA warp
+// accumulates dV += P^T dO and dK += dS^T Q with A read from TMEM. The reference's _bwd_col_kernel
+// (triton_kernels.py:184-274, two-kernel mode). TMEM: S^T [0, 64), dP^T [64, 128), dK [128, 128 + D), dV after dK.
+template <typename T, int D>
+__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+    tc_bwd_dkdv_pipe_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                            const __grid_constant__ CUtensorMap tq64, const __grid_constant__ CUtensorMap tdo64,
+                            const float* __restrict__ lse, const float* __restrict__ di, T* __restrict__ dk,
+                            T* __restrict__ dv, int BH, int H, int N, float scale) {
+  using L = BwdPipeLayout<D>;
+  constexpr int NS = L::kStages;
+  constexpr uint32_t kCols = (D == 64) ? 256 : 512;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t k_full[2], k_empty[2], q_full[NS], q_empty[NS], s_full, p_full, o_done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_kt = (N + kTile - 1) / kTile, n_qs = (N + 63) / 64;
+  const int64_t items = static_cast<int64_t>(BH) * n_kt;
+  constexpr bool kB = is_bf16<T>();
+  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 64);
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
+  auto sK = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig; };
+  auto sV = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig + L::kBig; };
+  auto sQ = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
+  auto sDO = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      uint32_t q_use = 0;
+      int64_t li = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
+        const int b = bh / H, h = bh - (bh / H) * H;
+        const int kb = static_cast<int>(li & 1);
+        ok = mbar_wait_or_abort(&k_empty[kb], ((li >> 1) & 1) ^ 1, 271, abort);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&k_full[kb], 2 * L::kBig);
+        for (int hh = 0; hh < D / 64; ++hh) {
+          tma_load_4d(sK(kb) + hh * kHalfBytes, &tk, &k_full[kb], hh * 64, kt * kTile, h, b);
+          tma_load_4d(sV(kb) + hh * kHalfBytes, &tv, &k_full[kb], hh * 64, kt * kTile, h, b);
+        }
+        for (int i = 0; i < n_qs; ++i, ++q_use) {
+          const int s = static_cast<int>(q_use % NS);
+          ok = mbar_wait_or_abort(&q_empty[s], ((q_use / NS) & 1) ^ 1, 272, abort);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&q_full[s], 2 * L::kSmall);
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_4d(sQ(s) + hh * L::kHalf64, &tq64, &q_full[s], hh * 64, i * 64, h, b);
+            tma_load_4d(sDO(s) + hh * L::kHalf64, &tdo64, &q_full[s], hh * 64, i * 64, h, b);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t tS = tmem, tDP = tmem + 64, tDK = tmem + 128, tDV = tmem + 128 + D;
+      uint32_t q_use = 0, t = 0;
+      int64_t li = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int kb = static_cast<int>(li & 1);
+        ok = mbar_wait_or_abort(&k_full[kb], (li >> 1) & 1, 281, abort);
+        for (int i = 0; i < n_qs && ok; ++i, ++q_use, ++t) {
+          const int s = static_cast<int>(q_use % NS);
+          ok = mbar_wait_or_abort(&q_full[s], (q_use / NS) & 1, 282, abort);
+          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 283, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            mma_ss(tS, desc_kmajor(sK(kb), kk), desc_kmajor_r(sQ(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
+            mma_ss(tDP, desc_kmajor(sV(kb), kk), desc_kmajor_r(sDO(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full);
+          ok = mbar_wait_or_abort(&p_full, t & 1, 284, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_ts(tDV, tS + kk * 8, desc_mnmajor_r(sDO(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tDK, tDP + kk * 8, desc_mnmajor_r(sQ(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&o_done);
+          mma_commit(&q_empty[s]);
+          if (i == n_qs - 1) mma_commit(&k_empty[kb]);
+        }
+      }
+    }
+  } else {
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tDP = tmem + 64 + lane_off;
+    const uint32_t tDK = tmem + 128 + lane_off, tDV = tmem + 128 + D + lane_off;
+    uint32_t t = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
+      const int64_t base = static_cast<int64_t>(bh) * N;
+      for (int i = 0; i < n_qs; ++i, ++t) {
+        // This step's 64 query scalars (lse, D): every thread reads the same addresses (broadcast loads).
+        const float* lse_i = lse + base + i * 64;
+        const float* di_i = di + base + i * 64;
+        ok = mbar_wait_or_abort(&s_full, t & 1, 291, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t rs[32], rp[32];
+          tmem_ld32(tS + c, rs);
+          tmem_ld32(tDP + c, rp);
+          tmem_wait_ld();
+          uint32_t p0[8], p1[8], d0[8], d1[8];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float p[2], ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int qc = c + e + u;
+              const bool okk = i * 64 + qc < N;
+              p[u] = okk ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -__ldg(lse_i + qc))) : 0.f;
+              ds[u] = okk ? p[u] * (__uint_as_float(rp[e + u]) - __ldg(di_i + qc)) : 0.f;
+            }
+            const uint32_t pp = pack2<T>(p[0], p[1]), pd = pack2<T>(ds[0], ds[1]);
+            if (e < 16) {
+              p0[e >> 1] = pp;
+              d0[e >> 1] = pd;
+            } else {
+              p1[(e - 16) >> 1] = pp;
+              d1[(e - 16) >> 1] = pd;
+            }
+          }
+          tmem_st8(tS + (c >> 1), p0);
+          tmem_st8(tS + (c >> 1) + 8, p1);
+          tmem_st8(tDP + (c >> 1), d0);
+          tmem_st8(tDP + (c >> 1) + 8, d1);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full);
+      }
+      if (!ok) break;
+      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 292, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int key = kt * kTile + tid;
+      const int64_t gk = base + key;
+      T* none = nullptr;
+      store_row_from_tmem<T, D>(tDK, scale, key < N ? dk + gk * D : none);
+      store_row_from_tmem<T, D>(tDV, 1.f, key < N ? dv + gk * D : none);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
 // ================================================================================================ backward, N <= 128

@@ -140,6 +140,27 @@ def test_parity_16bit(shape, dtype):
         check_out(got, ref, dtype, GRAD_TOL, name)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_parity_growing_logits(dtype):
+    """Logits that grow from one key tile to the next, differently per row, so the forward's lazy rescale of O runs
+    for some rows of a warp and not others (unit-scale random inputs never trigger it)."""
+    B, H, N, D = 2, 2, 900, 64
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=77)
+    g = torch.Generator().manual_seed(78)
+    row_scale = (torch.rand(B, H, N, 1, generator=g) * 3.0 + 0.5).to(DEV)
+    key_scale = torch.ones(1, 1, N, 1, device=DEV)
+    key_scale[:, :, 384:] = 2.5
+    key_scale[:, :, 768:] = 5.0
+    q = (q.float() * row_scale * (1.0 if dtype == torch.bfloat16 else 0.5)).to(dtype)
+    k = (k.float() * key_scale).to(dtype)
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, D**-0.5)
+    O, LSE, G, HS = oracle_all(q, k, v, do, gq, gk, gv, o, lse, D**-0.5)
+    check_out(o, O, dtype, FWD_TOL, "o")
+    assert _maxrel(lse, LSE) < 1e-5
+    for got, ref in zip(grads, G):
+        check_out(got, ref, dtype, GRAD_TOL, "grad")
+
+
 @pytest.mark.parametrize("layout", ["qkv", "odd"])
 def test_parity_strided_operands(layout):
     B, H, N, D = 2, 4, 81, 64
