@@ -194,22 +194,6 @@ int launch_simt_fwd(int64_t B, int64_t H, int64_t N, int64_t D, double scale, co
   return check_launch("simt_fwd");
 }
 
-template <typename T, int D>
-int launch_tc_fwd(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
-                  const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
-  using L = FwdLayout<D>;
-  CUtensorMap tq, tk, tv;
-  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
-      make_tile_map(&tv, v, dtype, B, H, N, D))
-    return kNoTensorMap;
-  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_fwd_kernel<T, D>), device, L::kSmem, L::kTmemCols);
-  if (s) return s;
-  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((N + kTile - 1) / kTile));
-  tc_fwd_kernel<T, D><<<grid, 128, L::kSmem, st>>>(tq, tk, tv, static_cast<T*>(o), static_cast<float*>(lse),
-                                                   static_cast<int>(H), static_cast<int>(N), static_cast<float>(scale));
-  return check_launch("tc_fwd_kernel");
-}
-
 int sm_count(int device) {
   static std::atomic<int> counts[kMaxDevices];
   int c = counts[device].load();
@@ -309,34 +293,6 @@ int launch_tc_bwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, d
       tk, tv, tq64, tdo64, static_cast<const float*>(lse), di, static_cast<T*>(dk), static_cast<T*>(dv), BH, Hi, Ni,
       static_cast<float>(scale));
   return check_launch("tc_bwd_dkdv_pipe_kernel");
-}
-
-template <typename T, int D>
-int launch_tc_bwd_tiled(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
-                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
-                        const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, cudaStream_t st) {
-  using LQ = BwdDqLayout<D>;
-  using LK = BwdDkdvLayout<D>;
-  CUtensorMap tq, tk, tv, tdo;
-  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
-      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
-    return kNoTensorMap;
-  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_dq_kernel<T, D>), device, LQ::kSmem, LQ::kTmemCols);
-  if (s) return s;
-  s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_dkdv_kernel<T, D>), device, LK::kSmem, LK::kTmemCols);
-  if (s) return s;
-  const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((N + kTile - 1) / kTile));
-  float* di = static_cast<float*>(scratch);
-  tc_bwd_dq_kernel<T, D><<<grid, 128, LQ::kSmem, st>>>(tq, tk, tv, tdo, static_cast<const T*>(o),
-                                                       static_cast<const float*>(lse), di, static_cast<T*>(dq),
-                                                       static_cast<int>(H), static_cast<int>(N),
-                                                       static_cast<float>(scale));
-  if ((s = check_launch("tc_bwd_dq_kernel"))) return s;
-  tc_bwd_dkdv_kernel<T, D><<<grid, 128, LK::kSmem, st>>>(tq, tk, tv, tdo, static_cast<const float*>(lse), di,
-                                                         static_cast<T*>(dk), static_cast<T*>(dv),
-                                                         static_cast<int>(H), static_cast<int>(N),
-                                                         static_cast<float>(scale));
-  return check_launch("tc_bwd_dkdv_kernel");
 }
 
 // ------------------------------------------------------------------------------------------------ double backward

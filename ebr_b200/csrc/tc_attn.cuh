@@ -123,178 +123,6 @@ __device__ __forceinline__ void mma_tileT_x_rows(uint32_t d_tmem, const unsigned
     mma_ss(d_tmem, desc_mnmajor(a, kk), desc_mnmajor(b, kk), idesc, (kk > 0 || accumulate_first) ? 1u : 0u);
 }
 
-// ================================================================================================ forward
-
-template <int D>
-struct FwdLayout {
-  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
-  static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kK0 = kQ + kOp, kV0 = kK0 + kOp, kK1 = kV0 + kOp, kV1 = kK1 + kOp;
-  static constexpr uint32_t kPh = kV1 + kOp, kPl = kPh + 2 * kHalfBytes;
-  static constexpr uint32_t kBytes = kPl + 2 * kHalfBytes;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 256;  // S: [0, 128), O_j: [128, 128 + D)
-};
-
-// Forward for any N: grid (B * H, ceil(N / 128)); the CTA owns 128 query rows and sweeps the keys in tiles of 128
-// with an online softmax (the reference's _fwd_kernel, triton_kernels.py:98-163). K / V tiles are double-buffered
-// (the TMA of tile j + 1 runs under the math of tile j). Per key tile: S = Q K^T into TMEM; P goes to shared memory
-// as a 16-bit pair P_hi + P_lo (P_lo = P - P_hi rounded again), so O_j = P_hi V + P_lo V carries P to ~2^-16 and the
-// output meets a 2e-3 max-rel bar against fp32 attention; then acc = acc * alpha + O_j in registers. The row sum l
-// uses the unrounded P, as the reference does.
-template <typename T, int D>
-__global__ void __launch_bounds__(128, 1)
-    tc_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, T* __restrict__ out, float* __restrict__ lse, int H, int N,
-                  float scale) {
-  using L = FwdLayout<D>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  unsigned char* sQ = smem + L::kQ;
-  unsigned char* sPh = smem + L::kPh;
-  unsigned char* sPl = smem + L::kPl;
-  __shared__ uint64_t bar_full[2], bar_mma;
-  __shared__ uint32_t tmem_slot;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
-  const int m0 = blockIdx.y * kTile;
-  constexpr uint32_t kIdS = idesc_f16(is_bf16<T>(), 0, 0, 128, 128);
-  constexpr uint32_t kIdPV = idesc_f16(is_bf16<T>(), 0, 1, 128, D);
-  const int n_tiles = (N + kTile - 1) / kTile;
-  auto sK = [&](int st) { return smem + (st ? L::kK1 : L::kK0); };
-  auto sV = [&](int st) { return smem + (st ? L::kV1 : L::kV0); };
-  auto load_kv = [&](int jt, int st) {
-    mbar_arrive_expect_tx(&bar_full[st], (jt == 0 ? 3u : 2u) * L::kOp);
-#pragma unroll
-    for (int hh = 0; hh < D / 64; ++hh) {
-      if (jt == 0) tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, m0, h, b);
-      tma_load_4d(sK(st) + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, jt * kTile, h, b);
-      tma_load_4d(sV(st) + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, jt * kTile, h, b);
-    }
-  };
-
-  if (tid == 0) {
-    mbar_init(&bar_full[0], 1);
-    mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-    load_kv(0, 0);
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t tS = tmem, tO = tmem + 128;
-
-  float acc[D];
-#pragma unroll
-  for (int d = 0; d < D; ++d) acc[d] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
-  uint32_t ph_mma = 0;
-  bool fail = false;
-
-  for (int jt = 0; jt < n_tiles; ++jt) {
-    const int st = jt & 1;
-    // Stage st ^ 1 held tile jt - 1, whose P V product completed before the end of the last iteration.
-    if (tid == 0 && jt + 1 < n_tiles) load_kv(jt + 1, st ^ 1);
-    fail |= !mbar_wait(&bar_full[st], (jt >> 1) & 1, 101);
-    if (__syncthreads_or(fail)) break;
-    if (tid == 0) {
-      tc_fence_after();
-      mma_rows_x_rows<D>(tS, sQ, sK(st), kIdS, false);
-      mma_commit(&bar_mma);
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 102);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-
-    // Row max of this key tile (pass 1), then P = exp(s - m_new) as a 16-bit hi / lo pair (pass 2).
-    const int j0 = jt * kTile;
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < kTile; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tS + lane_off + c, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (j0 + c + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * scale);
-    }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = exp_nat(m_run - m_new);
-    float psum = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < kTile; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tS + lane_off + c, r);
-      tmem_wait_ld();
-      uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        const float p0 = (j0 + c + e < N) ? exp_nat(__uint_as_float(r[e]) * scale - m_new) : 0.f;
-        const float p1 = (j0 + c + e + 1 < N) ? exp_nat(__uint_as_float(r[e + 1]) * scale - m_new) : 0.f;
-        psum += p0 + p1;
-        const float h0 = round16<T>(p0), h1 = round16<T>(p1);
-        hi[e >> 1] = pack2<T>(h0, h1);
-        lo[e >> 1] = pack2<T>(p0 - h0, p1 - h1);
-      }
-      st_row32(sPh, tid, c, hi);
-      st_row32(sPl, tid, c, lo);
-    }
-    l_run = l_run * alpha + psum;
-    m_run = m_new;
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tile_x_rows(tO, sPh, sV(st), kIdPV, false);
-      mma_tile_x_rows(tO, sPl, sV(st), kIdPV, true);
-      mma_commit(&bar_mma);
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 103);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < D; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tO + lane_off + c, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e) acc[c + e] = acc[c + e] * alpha + __uint_as_float(r[e]);
-    }
-    tc_fence_before();
-    __syncthreads();  // S, O_j, P and this stage's K / V are free
-  }
-
-  const int row = m0 + tid;
-  if (!fail && row < N) {
-    const float inv = 1.f / l_run;
-    T* orow = out + (static_cast<int64_t>(bh) * N + row) * D;
-#pragma unroll
-    for (int d = 0; d < D; d += 8) {
-      uint4 u;
-      u.x = pack2<T>(acc[d] * inv, acc[d + 1] * inv);
-      u.y = pack2<T>(acc[d + 2] * inv, acc[d + 3] * inv);
-      u.z = pack2<T>(acc[d + 4] * inv, acc[d + 5] * inv);
-      u.w = pack2<T>(acc[d + 6] * inv, acc[d + 7] * inv);
-      *reinterpret_cast<uint4*>(orow + d) = u;
-    }
-    lse[static_cast<int64_t>(bh) * N + row] = m_run + logf(l_run);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-}
-
 // ================================================================================================ forward (pipelined)
 
 template <int D>
@@ -544,7 +372,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
 }
 
-// ================================================================================================ backward, N > 128
+// ================================================================================================ backward helpers
 
 // Shared helper: thread `row`'s D_i = <dO_i, O_i> from the TMA-staged dO tile and the stored (contiguous) O.
 template <typename T, int D>
@@ -559,280 +387,6 @@ __device__ __forceinline__ float row_delta(const unsigned char* sDO, int row, co
     for (int i = 0; i < 8; ++i) di += x[i] * y[i];
   }
   return di;
-}
-
-// From S and dP in TMEM (this thread's query row), write P (optional) and dS = P (dP - D) as 16-bit tiles.
-// Keys at or past N and query rows at or past N give zeros.
-template <typename T, bool kWriteP>
-__device__ __forceinline__ void softmax_grad_tiles(uint32_t tS, uint32_t tDP, int row, bool row_ok, int key0, int N,
-                                                   float Li, float Di, float scale, unsigned char* sP,
-                                                   unsigned char* sDS) {
-#pragma unroll 1
-  for (int c = 0; c < kTile; c += 32) {
-    uint32_t rs[32], rp[32];
-    tmem_ld32(tS + c, rs);
-    tmem_ld32(tDP + c, rp);
-    tmem_wait_ld();
-    uint32_t pk[16], dk[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      float p[2], ds[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const bool ok = row_ok && (key0 + c + e + u < N);
-        p[u] = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
-        ds[u] = p[u] * (__uint_as_float(rp[e + u]) - Di);
-      }
-      pk[e >> 1] = pack2<T>(p[0], p[1]);
-      dk[e >> 1] = pack2<T>(ds[0], ds[1]);
-    }
-    if (kWriteP) st_row32(sP, row, c, pk);
-    st_row32(sDS, row, c, dk);
-  }
-}
-
-template <int D>
-struct BwdDqLayout {
-  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
-  static constexpr uint32_t kQ = 0, kDO = kQ + kOp;
-  static constexpr uint32_t kK0 = kDO + kOp, kV0 = kK0 + kOp, kK1 = kV0 + kOp, kV1 = kK1 + kOp;
-  static constexpr uint32_t kDS = kV1 + kOp;
-  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;  // S [0,128), dP [128,256), dQ [256, 256 + D)
-};
-
-// Row pass of the backward for N > 128 (the reference's _bwd_dq_kernel, triton_kernels.py:277-339, with the row
-// scalar D computed in the prologue as its _rowdot_kernel does, :171-181): grid (B * H, ceil(N / 128)); the CTA owns
-// 128 query rows, writes D_i to `di` for the column pass, and sweeps double-buffered K / V tiles accumulating
-// dQ = scale * dS K in TMEM.
-template <typename T, int D>
-__global__ void __launch_bounds__(128, 1)
-    tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                     const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
-                     T* __restrict__ dq, int H, int N, float scale) {
-  using L = BwdDqLayout<D>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  unsigned char* sQ = smem + L::kQ;
-  unsigned char* sDO = smem + L::kDO;
-  unsigned char* sDS = smem + L::kDS;
-  __shared__ uint64_t bar_full[2], bar_mma;
-  __shared__ uint32_t tmem_slot;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
-  const int m0 = blockIdx.y * kTile;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
-  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
-  const int n_tiles = (N + kTile - 1) / kTile;
-  auto sK = [&](int st) { return smem + (st ? L::kK1 : L::kK0); };
-  auto sV = [&](int st) { return smem + (st ? L::kV1 : L::kV0); };
-  auto load_kv = [&](int jt, int st) {
-    mbar_arrive_expect_tx(&bar_full[st], (jt == 0 ? 4u : 2u) * L::kOp);
-#pragma unroll
-    for (int hh = 0; hh < D / 64; ++hh) {
-      if (jt == 0) {
-        tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, m0, h, b);
-        tma_load_4d(sDO + hh * kHalfBytes, &tdo, &bar_full[st], hh * 64, m0, h, b);
-      }
-      tma_load_4d(sK(st) + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, jt * kTile, h, b);
-      tma_load_4d(sV(st) + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, jt * kTile, h, b);
-    }
-  };
-
-  if (tid == 0) {
-    mbar_init(&bar_full[0], 1);
-    mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-    load_kv(0, 0);
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  const int row = m0 + tid;
-  const bool row_ok = row < N;
-  const int64_t grow = static_cast<int64_t>(bh) * N + row;
-  const float Li = row_ok ? lse[grow] : 0.f;
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  uint32_t ph_mma = 0;
-  float Di = 0.f;
-  bool fail = false;
-
-  for (int jt = 0; jt < n_tiles; ++jt) {
-    const int st = jt & 1;
-    if (tid == 0 && jt + 1 < n_tiles) load_kv(jt + 1, st ^ 1);
-    fail |= !mbar_wait(&bar_full[st], (jt >> 1) & 1, 211);
-    if (__syncthreads_or(fail)) break;
-    if (tid == 0) {
-      tc_fence_after();
-      mma_rows_x_rows<D>(tmem + 0, sQ, sK(st), kIdNN, false);
-      mma_rows_x_rows<D>(tmem + 128, sDO, sV(st), kIdNN, false);
-      mma_commit(&bar_mma);
-    }
-    if (jt == 0 && row_ok) {
-      Di = row_delta<T, D>(sDO, tid, o + grow * D);
-      di_out[grow] = Di;
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 212);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-    softmax_grad_tiles<T, false>(tmem + lane_off, tmem + 128 + lane_off, tid, row_ok, jt * kTile, N, Li, Di, scale,
-                                 nullptr, sDS);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tile_x_rows(tmem + 256, sDS, sK(st), kIdKM, jt > 0);
-      mma_commit(&bar_mma);
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 213);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-  }
-  if (!fail) {
-    T* none = nullptr;
-    store_row_from_tmem<T, D>(tmem + 256 + lane_off, scale, row_ok ? dq + grow * D : none);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-}
-
-template <int D>
-struct BwdDkdvLayout {
-  static constexpr int kStages = D == 64 ? 2 : 1;
-  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
-  static constexpr uint32_t kK = 0, kV = kK + kOp;
-  static constexpr uint32_t kQ0 = kV + kOp, kDO0 = kQ0 + kOp;
-  static constexpr uint32_t kQ1 = kDO0 + kOp, kDO1 = kQ1 + (kStages - 1) * kOp;
-  static constexpr uint32_t kP = kDO1 + (kStages - 1) * kOp, kDS = kP + 2 * kHalfBytes;
-  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;  // S [0,128), dP [128,256), dK [256, 256 + D), dV after dK
-};
-
-// Column pass of the backward for N > 128 (the reference's _bwd_col_kernel, triton_kernels.py:184-274, two-kernel
-// mode): grid (B * H, ceil(N / 128)); the CTA owns 128 keys and sweeps the query tiles (double-buffered for D = 64),
-// recomputing S and dP with the row scalars lse and D from the row pass, and accumulating dV = P^T dO and
-// dK = scale * dS^T Q in TMEM (M = keys: lane t is key t).
-template <typename T, int D>
-__global__ void __launch_bounds__(128, 1)
-    tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                       const float* __restrict__ lse, const float* __restrict__ di, T* __restrict__ dk,
-                       T* __restrict__ dv, int H, int N, float scale) {
-  using L = BwdDkdvLayout<D>;
-  constexpr int S = L::kStages;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  unsigned char* sK = smem + L::kK;
-  unsigned char* sV = smem + L::kV;
-  unsigned char* sP = smem + L::kP;
-  unsigned char* sDS = smem + L::kDS;
-  __shared__ uint64_t bar_full[2], bar_mma;
-  __shared__ uint32_t tmem_slot;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
-  const int n0 = blockIdx.y * kTile;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
-  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);
-  const int n_tiles = (N + kTile - 1) / kTile;
-  auto sQ = [&](int st) { return smem + (st ? L::kQ1 : L::kQ0); };
-  auto sDO = [&](int st) { return smem + (st ? L::kDO1 : L::kDO0); };
-  auto load_q = [&](int it, int st) {
-    mbar_arrive_expect_tx(&bar_full[st], (it == 0 ? 4u : 2u) * L::kOp);
-#pragma unroll
-    for (int hh = 0; hh < D / 64; ++hh) {
-      if (it == 0) {
-        tma_load_4d(sK + hh * kHalfBytes, &tk, &bar_full[st], hh * 64, n0, h, b);
-        tma_load_4d(sV + hh * kHalfBytes, &tv, &bar_full[st], hh * 64, n0, h, b);
-      }
-      tma_load_4d(sQ(st) + hh * kHalfBytes, &tq, &bar_full[st], hh * 64, it * kTile, h, b);
-      tma_load_4d(sDO(st) + hh * kHalfBytes, &tdo, &bar_full[st], hh * 64, it * kTile, h, b);
-    }
-  };
-
-  if (tid == 0) {
-    mbar_init(&bar_full[0], 1);
-    mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-    load_q(0, 0);
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  uint32_t ph_mma = 0;
-  bool fail = false;
-
-  for (int it = 0; it < n_tiles; ++it) {
-    const int st = (S == 2) ? (it & 1) : 0;
-    if (tid == 0) {
-      if (S == 2 && it + 1 < n_tiles) load_q(it + 1, st ^ 1);
-      if (S == 1 && it > 0) load_q(it, 0);  // the previous tile's products have completed
-    }
-    const int qrow = it * kTile + tid;
-    const bool row_ok = qrow < N;
-    const int64_t gq = static_cast<int64_t>(bh) * N + qrow;
-    const float Li = row_ok ? lse[gq] : 0.f;
-    const float Di = row_ok ? di[gq] : 0.f;
-    fail |= !mbar_wait(&bar_full[st], (S == 2 ? (it >> 1) : it) & 1, 221);
-    if (__syncthreads_or(fail)) break;
-    if (tid == 0) {
-      tc_fence_after();
-      mma_rows_x_rows<D>(tmem + 0, sQ(st), sK, kIdNN, false);
-      mma_rows_x_rows<D>(tmem + 128, sDO(st), sV, kIdNN, false);
-      mma_commit(&bar_mma);
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 222);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-    softmax_grad_tiles<T, true>(tmem + lane_off, tmem + 128 + lane_off, tid, row_ok, n0, N, Li, Di, scale, sP, sDS);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tileT_x_rows(tmem + 256 + D, sP, sDO(st), kIdMM, it > 0);
-      mma_tileT_x_rows(tmem + 256, sDS, sQ(st), kIdMM, it > 0);
-      mma_commit(&bar_mma);
-    }
-    fail |= !mbar_wait(&bar_mma, ph_mma, 223);
-    ph_mma ^= 1;
-    if (__syncthreads_or(fail)) break;
-    tc_fence_after();
-  }
-  if (!fail) {
-    const int key = n0 + tid;
-    const int64_t gk = static_cast<int64_t>(bh) * N + key;
-    T* none = nullptr;
-    store_row_from_tmem<T, D>(tmem + 256 + lane_off, scale, key < N ? dk + gk * D : none);
-    store_row_from_tmem<T, D>(tmem + 256 + D + lane_off, 1.f, key < N ? dv + gk * D : none);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
 }
 
 // ================================================================================================ backward (pipelined)
