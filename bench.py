@@ -388,6 +388,8 @@ def run_sweep(args) -> None:
             }
             out = {"mode": "sweep", "L": L, "D": D, "B": B, "H": H}
             for name, fn in fns.items():
+                if name not in args.passes.split(","):
+                    continue
                 for _ in range(max(args.warmup, 1)):
                     fn()
                 torch.cuda.synchronize()
@@ -421,6 +423,7 @@ def main() -> None:
     ap.add_argument("--mode", choices=["descent", "sweep"], default="descent")
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
+    ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd", help="sweep: which passes to time")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -259,7 +259,14 @@ struct Elem<__half> {
 
 // exp(x) for x = (score - row statistic) in natural units, as exp2(x * log2 e): the log2(e) factor is applied to the
 // small difference, not to the raw score (the reference's _exp, triton_kernels.py:48-56).
-__device__ __forceinline__ float exp_nat(float x) { return exp2f(x * 1.4426950408889634f); }
+// 2^x by the SFU instruction ex2.approx.ftz.f32 (relative error ~2^-22, subnormal results flushed to zero): the
+// instruction the reference's Triton kernels reach through tl.exp2.
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp_nat(float x) { return exp2_approx(x * 1.4426950408889634f); }
 __device__ __forceinline__ double exp_nat(double x) { return exp(x); }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -279,6 +286,28 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return pack_f16(lo, hi);
+}
+
+// The two 16-bit halves of a packed pair, widened to float.
+template <typename T>
+__device__ __forceinline__ float unpack_lo(uint32_t v);
+template <typename T>
+__device__ __forceinline__ float unpack_hi(uint32_t v);
+template <>
+__device__ __forceinline__ float unpack_lo<__nv_bfloat16>(uint32_t v) {
+  return __uint_as_float(v << 16);
+}
+template <>
+__device__ __forceinline__ float unpack_hi<__nv_bfloat16>(uint32_t v) {
+  return __uint_as_float(v & 0xFFFF0000u);
+}
+template <>
+__device__ __forceinline__ float unpack_lo<__half>(uint32_t v) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+}
+template <>
+__device__ __forceinline__ float unpack_hi<__half>(uint32_t v) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
 }
 
 // Round a float to the 16-bit type and back (P and dS are rounded before they enter a tensor-core dot).

@@ -280,16 +280,30 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
         if (!ok) break;
         tc_fence_after();
         const int j0 = j * kTile;
-        float mx = -INFINITY;
+        const int valid = min(kTile, N - j0);  // keys of this tile inside [0, N); uniform over the CTA
+        // Pass 1: the tile's row max of the raw scores, scaled once (rounding is monotonic, so this equals the max of
+        // the scaled scores; a negative scale turns it into the min).
+        float mraw = scale >= 0.f ? -INFINITY : INFINITY;
 #pragma unroll 1
         for (int c = 0; c < kTile; c += 32) {
           uint32_t r[32];
           tmem_ld32(tS + c, r);
           tmem_wait_ld();
+          if (valid == kTile) {
+            if (scale >= 0.f) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (j0 + c + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * scale);
+              for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(r[e]));
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) mraw = fminf(mraw, __uint_as_float(r[e]));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c + e < valid) mraw = scale >= 0.f ? fmaxf(mraw, __uint_as_float(r[e])) : fminf(mraw, __uint_as_float(r[e]));
+          }
         }
+        const float mx = mraw * scale;
         // Lazy rescale. tcgen05.ld / st are warp-collective, so the decision is made per warp: if any row of the warp
         // needs it, the whole warp rewrites its O rows, with alpha = 1 for the rows that keep their max. The previous
         // P V product has completed (S of this tile was issued after it), so O can be rewritten.
@@ -303,17 +317,15 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
             uint32_t r[32];
             tmem_ld32(tO + c, r);
             tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            uint32_t a[8], b8[8], c8[8], d8[8];
+            uint32_t a8[8], b8[8], c8[8], d8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              a[e] = r[e];
-              b8[e] = r[8 + e];
-              c8[e] = r[16 + e];
-              d8[e] = r[24 + e];
+              a8[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              b8[e] = __float_as_uint(__uint_as_float(r[8 + e]) * alpha);
+              c8[e] = __float_as_uint(__uint_as_float(r[16 + e]) * alpha);
+              d8[e] = __float_as_uint(__uint_as_float(r[24 + e]) * alpha);
             }
-            tmem_st8(tO + c, a);
+            tmem_st8(tO + c, a8);
             tmem_st8(tO + c + 8, b8);
             tmem_st8(tO + c + 16, c8);
             tmem_st8(tO + c + 24, d8);
@@ -323,6 +335,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
             m_used = mx;
           }
         }
+        // Pass 2: P = exp(s * scale - m_used) as a 16-bit hi / lo pair over the S columns just read.
         float psum = 0.f;
 #pragma unroll 1
         for (int c = 0; c < kTile; c += 32) {
@@ -332,11 +345,16 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
           uint32_t hi[8], hi2[8], lo[8], lo2[8];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float p0 = (j0 + c + e < N) ? exp_nat(__uint_as_float(r[e]) * scale - m_used) : 0.f;
-            const float p1 = (j0 + c + e + 1 < N) ? exp_nat(__uint_as_float(r[e + 1]) * scale - m_used) : 0.f;
+            float p0 = exp_nat(fmaf(__uint_as_float(r[e]), scale, -m_used));
+            float p1 = exp_nat(fmaf(__uint_as_float(r[e + 1]), scale, -m_used));
+            if (valid < kTile) {
+              if (c + e >= valid) p0 = 0.f;
+              if (c + e + 1 >= valid) p1 = 0.f;
+            }
             psum += p0 + p1;
-            const float h0 = round16<T>(p0), h1 = round16<T>(p1);
-            const uint32_t ph = pack2<T>(h0, h1), pl = pack2<T>(p0 - h0, p1 - h1);
+            const uint32_t ph = pack2<T>(p0, p1);
+            const float h0 = unpack_lo<T>(ph), h1 = unpack_hi<T>(ph);
+            const uint32_t pl = pack2<T>(p0 - h0, p1 - h1);
             if (e < 16) {
               hi[e >> 1] = ph;
               lo[e >> 1] = pl;
@@ -565,14 +583,17 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
           tmem_ld32(tS + c, rs);
           tmem_ld32(tDP + c, rp);
           tmem_wait_ld();
+          // Query rows past N have zero Q / dO (TMA fill) and Li = Di = 0, so their dS is exactly 0 without a mask;
+          // keys past N (the last step only) are masked so exp(-Li) cannot reach dQ.
+          const int valid = N - j * 64;
           uint32_t a[8], b8[8];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
             float ds[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              const bool okk = row_ok && (j * 64 + c + e + u < N);
-              const float p = okk ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+              float p = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li));
+              if (valid < 64 && c + e + u >= valid) p = 0.f;
               ds[u] = p * (__uint_as_float(rp[e + u]) - Di);
             }
             const uint32_t pk = pack2<T>(ds[0], ds[1]);
@@ -638,7 +659,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       mbar_init(&k_empty[i], 1);
     }
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&q_full[i], 1);
+      mbar_init(&q_full[i], 33);  // the TMA transaction arrive + one arrive per producer lane after its lse / D writes
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(&s_full, 1);
@@ -647,6 +668,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
     abort_flag = 0;
     fence_barrier_init();
   }
+  float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [stage][lse 64 | D 64]
   if (warp == 0) {
     tmem_alloc(&tmem_slot, kCols);
     tmem_relinquish();
@@ -658,31 +680,47 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   volatile int* abort = &abort_flag;
 
   if (warp == 4) {
-    if (lane == 0) {
-      uint32_t q_use = 0;
-      int64_t li = 0;
-      bool ok = true;
-      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-        const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-        const int b = bh / H, h = bh - (bh / H) * H;
-        const int kb = static_cast<int>(li & 1);
+    // Lane 0 issues the TMA loads; all 32 lanes stage each query step's lse and D (64 + 64 floats) in shared memory.
+    uint32_t q_use = 0;
+    int64_t li = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+      const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
+      const int b = bh / H, h = bh - (bh / H) * H;
+      const int64_t base = static_cast<int64_t>(bh) * N;
+      const int kb = static_cast<int>(li & 1);
+      if (lane == 0) {
         ok = mbar_wait_or_abort(&k_empty[kb], ((li >> 1) & 1) ^ 1, 271, abort);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&k_full[kb], 2 * L::kBig);
-        for (int hh = 0; hh < D / 64; ++hh) {
-          tma_load_4d(sK(kb) + hh * kHalfBytes, &tk, &k_full[kb], hh * 64, kt * kTile, h, b);
-          tma_load_4d(sV(kb) + hh * kHalfBytes, &tv, &k_full[kb], hh * 64, kt * kTile, h, b);
+        if (ok) {
+          mbar_arrive_expect_tx(&k_full[kb], 2 * L::kBig);
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_4d(sK(kb) + hh * kHalfBytes, &tk, &k_full[kb], hh * 64, kt * kTile, h, b);
+            tma_load_4d(sV(kb) + hh * kHalfBytes, &tv, &k_full[kb], hh * 64, kt * kTile, h, b);
+          }
         }
-        for (int i = 0; i < n_qs; ++i, ++q_use) {
-          const int s = static_cast<int>(q_use % NS);
-          ok = mbar_wait_or_abort(&q_empty[s], ((q_use / NS) & 1) ^ 1, 272, abort);
-          if (!ok) break;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int i = 0; i < n_qs && ok; ++i, ++q_use) {
+        const int s = static_cast<int>(q_use % NS);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_empty[s], ((q_use / NS) & 1) ^ 1, 272, abort));
+        if (!ok) break;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&q_full[s], 2 * L::kSmall);
           for (int hh = 0; hh < D / 64; ++hh) {
             tma_load_4d(sQ(s) + hh * L::kHalf64, &tq64, &q_full[s], hh * 64, i * 64, h, b);
             tma_load_4d(sDO(s) + hh * L::kHalf64, &tdo64, &q_full[s], hh * 64, i * 64, h, b);
           }
         }
+        // Queries past N get lse = D = 0: with their zero Q / dO rows this makes P^T = 1 and dS^T = 0 there, and
+        // dO = 0 keeps them out of dV, so the compute warps need no mask.
+        float* st = stats + s * 128;
+#pragma unroll
+        for (int k2 = lane; k2 < 64; k2 += 32) {
+          const int qi = i * 64 + k2;
+          st[k2] = qi < N ? lse[base + qi] : 0.f;
+          st[64 + k2] = qi < N ? di[base + qi] : 0.f;
+        }
+        mbar_arrive(&q_full[s]);
       }
     }
   } else if (warp == 5) {
@@ -730,9 +768,11 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
       const int64_t base = static_cast<int64_t>(bh) * N;
       for (int i = 0; i < n_qs; ++i, ++t) {
-        // This step's 64 query scalars (lse, D): every thread reads the same addresses (broadcast loads).
-        const float* lse_i = lse + base + i * 64;
-        const float* di_i = di + base + i * 64;
+        const int s = static_cast<int>(t % NS);
+        ok = mbar_wait_or_abort(&q_full[s], (t / NS) & 1, 293, abort);  // this step's staged lse / D
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const float* st = stats + s * 128;
         ok = mbar_wait_or_abort(&s_full, t & 1, 291, abort);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -750,9 +790,8 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int qc = c + e + u;
-              const bool okk = i * 64 + qc < N;
-              p[u] = okk ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -__ldg(lse_i + qc))) : 0.f;
-              ds[u] = okk ? p[u] * (__uint_as_float(rp[e + u]) - __ldg(di_i + qc)) : 0.f;
+              p[u] = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -st[qc]));
+              ds[u] = p[u] * (__uint_as_float(rp[e + u]) - st[64 + qc]);
             }
             const uint32_t pp = pack2<T>(p[0], p[1]), pd = pack2<T>(ds[0], ds[1]);
             if (e < 16) {
