@@ -318,6 +318,59 @@ int launch_simt_bob(int64_t B, int64_t H, int64_t N, int64_t D, double scale, co
   return check_launch("simt_bob_col");
 }
 
+template <typename T, int D>
+int launch_tc_bob_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                       const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                       const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
+                       void* hq, void* hk, void* hv, void* hdo, void* scratch, cudaStream_t st) {
+  using L = BobPipeLayout<D>;
+  const bool has[3] = {gq && gq->data, gk && gk->data, gv && gv->data};
+  const uint32_t flags = (has[0] ? 1u : 0u) | (has[1] ? 2u : 0u) | (has[2] ? 4u : 0u);
+  CUtensorMap tq, tdo, tgq, tk, tv, tgk, tgv, tq64, tdo64, tgq64, tk64, tv64, tgk64, tgv64;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D) ||
+      make_tile_map(&tk, k, dtype, B, H, N, D) || make_tile_map(&tv, v, dtype, B, H, N, D) ||
+      make_tile_map(&tq64, q, dtype, B, H, N, D, 64) || make_tile_map(&tdo64, dout, dtype, B, H, N, D, 64) ||
+      make_tile_map(&tk64, k, dtype, B, H, N, D, 64) || make_tile_map(&tv64, v, dtype, B, H, N, D, 64))
+    return kNoTensorMap;
+  // An absent cotangent's maps are never read (its loads and products are skipped); any valid map fills the slot.
+  const ebr_operand* gs[3] = {gq, gk, gv};
+  CUtensorMap* big[3] = {&tgq, &tgk, &tgv};
+  CUtensorMap* small[3] = {&tgq64, &tgk64, &tgv64};
+  for (int i = 0; i < 3; ++i) {
+    if (!has[i]) {
+      *big[i] = tq;
+      *small[i] = tq64;
+    } else if (make_tile_map(big[i], gs[i], dtype, B, H, N, D) || make_tile_map(small[i], gs[i], dtype, B, H, N, D, 64)) {
+      return kNoTensorMap;
+    }
+  }
+  const void* f0 = reinterpret_cast<const void*>(tc_bob_row_pipe_kernel<T, D, 0>);
+  const void* f1 = reinterpret_cast<const void*>(tc_bob_row_pipe_kernel<T, D, 1>);
+  const void* f2 = reinterpret_cast<const void*>(tc_bob_col_pipe_kernel<T, D>);
+  int s = prepare_tc_kernel(f0, device, L::kSmem, 256, L::kThreads);
+  if (s || (s = prepare_tc_kernel(f1, device, L::kSmem, 512, L::kThreads)) ||
+      (s = prepare_tc_kernel(f2, device, L::kSmem, 512, L::kThreads)))
+    return s;
+  const int64_t items = B * H * ((N + kTile - 1) / kTile);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  float* stats = static_cast<float*>(scratch);
+  const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
+  const float sc = static_cast<float>(scale);
+  tc_bob_row_pipe_kernel<T, D, 0><<<grid, L::kThreads, L::kSmem, st>>>(
+      tq, tdo, tgq, tk64, tv64, tgk64, tgv64, static_cast<const T*>(o), static_cast<const float*>(lse), stats,
+      nullptr, nullptr, BH, Hi, Ni, sc, flags);
+  if ((s = check_launch("tc_bob_row_pipe_kernel<0>"))) return s;
+  tc_bob_row_pipe_kernel<T, D, 1><<<grid, L::kThreads, L::kSmem, st>>>(
+      tq, tdo, tgq, tk64, tv64, tgk64, tgv64, static_cast<const T*>(o), static_cast<const float*>(lse), stats,
+      static_cast<T*>(hq), static_cast<T*>(hdo), BH, Hi, Ni, sc, flags);
+  if ((s = check_launch("tc_bob_row_pipe_kernel<1>"))) return s;
+  tc_bob_col_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+      tk, tv, tgk, tgv, tq64, tdo64, tgq64, static_cast<const float*>(lse), stats, static_cast<T*>(hk),
+      static_cast<T*>(hv), BH, Hi, Ni, sc, flags);
+  return check_launch("tc_bob_col_pipe_kernel");
+}
+
 template <typename T>
 int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
                          const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
@@ -503,6 +556,19 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
   }
   if (!scratch || scratch_bytes < ebr_attn_bwd_bwd_scratch_bytes(dtype, B, H, N, D))
     return set_error(EBR_ERR_SCRATCH, "scratch missing or too small%s%s");
+  if (outs_ok && tc_eligible(dtype, D, {q, k, v, dout, gq, gk, gv}, B, H, N)) {
+    if (dtype == EBR_BFLOAT16)
+      s = D == 64 ? launch_tc_bob_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk,
+                                                           gv, hq, hk, hv, hdout, scratch, st)
+                  : launch_tc_bob_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq,
+                                                            gk, gv, hq, hk, hv, hdout, scratch, st);
+    else
+      s = D == 64 ? launch_tc_bob_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv,
+                                                   hq, hk, hv, hdout, scratch, st)
+                  : launch_tc_bob_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv,
+                                                    hq, hk, hv, hdout, scratch, st);
+    if (s != kNoTensorMap) return s;
+  }
   switch (dtype) {
     case EBR_FLOAT32:
       return launch_simt_bob<float>(B, H, N, D, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv, hdout, scratch,

@@ -213,31 +213,40 @@ def test_golden_cases_on_device(golden):
             check_out(got, c[n_], dtype, GRAD_TOL, f"{name}/{n_}", ulps=1.0)
 
 
-def test_zero_cotangents_through_c_abi():
-    """NULL gk / gv at the C ABI equal explicit zeros (the reference expands a zero row, triton_kernels.py:868-873)."""
+@pytest.mark.parametrize("shape", [(2, 2, 81, 64), (1, 2, 300, 64), (1, 2, 200, 128)], ids=str)
+@pytest.mark.parametrize("null", ["gk_gv", "gq", "gq_gk_gv"])
+def test_zero_cotangents_through_c_abi(shape, null):
+    """NULL cotangents at the C ABI equal explicit zeros (the reference expands a zero row, triton_kernels.py:868-873),
+    for the single-tile and the tiled double-backward kernels."""
     import ctypes
 
-    B, H, N, D = 2, 2, 81, 64
+    B, H, N, D = shape
     q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, torch.bfloat16, seed=5)
-    o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, 0.125)
-    dq, _, _ = torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, 0.125)
+    scale = D**-0.5
+    o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, scale)
+    dq, _, _ = torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, scale)
     z = torch.zeros_like(q)
-    ref = torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, gq, z, z, 0.125)
+    nulls = set(null.split("_"))
+    g = {n: (z if n in nulls else t) for n, t in (("gq", gq), ("gk", gk), ("gv", gv))}
+    ref = torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, g["gq"], g["gk"], g["gv"], scale)
     outs = [torch.empty_like(q) for _ in range(4)]
     lib = _native.lib()
     nbytes = lib.ebr_attn_bwd_bwd_scratch_bytes(_native.BFLOAT16, B, H, N, D)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
     op = lambda t: _native.Operand(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
-    ops = [op(t) for t in (q, k, v, do, gq)]
+    ops = [op(t) for t in (q, k, v, do)]
+    gops = {n: (None if n in nulls else op(t)) for n, t in (("gq", gq), ("gk", gk), ("gv", gv))}
     r = ctypes.byref
-    st = lib.ebr_attn_bwd_bwd(_native.BFLOAT16, B, H, N, D, 0.125, r(ops[0]), r(ops[1]), r(ops[2]), o.data_ptr(),
-                              lse.data_ptr(), r(ops[3]), dq.data_ptr(), r(ops[4]), None, None,
+    rr = lambda x: None if x is None else r(x)
+    st = lib.ebr_attn_bwd_bwd(_native.BFLOAT16, B, H, N, D, scale, r(ops[0]), r(ops[1]), r(ops[2]), o.data_ptr(),
+                              lse.data_ptr(), r(ops[3]), dq.data_ptr(), rr(gops["gq"]), rr(gops["gk"]), rr(gops["gv"]),
                               *[t.data_ptr() for t in outs], scratch.data_ptr(), nbytes,
                               torch.cuda.current_stream().cuda_stream)  # fmt: skip
     assert st == 0
     torch.cuda.synchronize()
     for a, b in zip(outs, ref):
-        assert torch.equal(a, b)
+        # Skipped zero products leave the same sums; allow the last-bit differences of a different summation order.
+        assert _maxrel(a, _np(b)) <= 1e-2
 
 
 def test_autograd_second_order_matches_oracle():
