@@ -101,6 +101,28 @@ __device__ __forceinline__ void store_row_from_tmem(uint32_t taddr, float mul, T
   }
 }
 
+// Store columns [col0, col0 + NC) of this thread's TMEM lane (fp32) times `mul` to dst[col0 .. col0 + NC).
+template <typename T, int NC>
+__device__ __forceinline__ void store_cols_from_tmem(uint32_t taddr, int col0, float mul, T* dst) {
+#pragma unroll
+  for (int c = 0; c < NC; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(taddr + col0 + c, r);
+    tmem_wait_ld();
+    if (dst) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u;
+        u.x = pack2<T>(__uint_as_float(r[8 * q + 0]) * mul, __uint_as_float(r[8 * q + 1]) * mul);
+        u.y = pack2<T>(__uint_as_float(r[8 * q + 2]) * mul, __uint_as_float(r[8 * q + 3]) * mul);
+        u.z = pack2<T>(__uint_as_float(r[8 * q + 4]) * mul, __uint_as_float(r[8 * q + 5]) * mul);
+        u.w = pack2<T>(__uint_as_float(r[8 * q + 6]) * mul, __uint_as_float(r[8 * q + 7]) * mul);
+        *reinterpret_cast<uint4*>(dst + col0 + c + 8 * q) = u;
+      }
+    }
+  }
+}
+
 // Issue the K-major x K-major product over the head dim: D[tmem] (+)= A[128 x D] * B[128 x D]^T (M = N = 128).
 template <int D>
 __device__ __forceinline__ void mma_rows_x_rows(uint32_t d_tmem, const unsigned char* a, const unsigned char* b,
@@ -135,23 +157,26 @@ struct FwdPipeLayout {
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 256;              // S / P: [0, 128), O: [128, 128 + D)
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;
 };
 
 // Forward for any N, persistent and warp-specialized (2 CTAs per SM at D = 64, so one CTA's MMAs run under the
 // other's softmax):
-//   warps 0-3  softmax: thread t owns query row t of the current tile (TMEM lane t);
-//   warp 4     TMA producer: Q tile per item (double-buffered), K / V tiles into a 2-stage ring;
-//   warp 5     MMA issuer: S = Q K^T into TMEM, then O += P V with P read from TMEM (tcgen05.mma A-from-TMEM).
+//   warps 0-7  softmax, two warpgroups: warp w owns query rows 32 (w % 4) .. + 31 of the current tile (TMEM lanes)
+//              and key columns 64 (w / 4) .. + 63 of each 128-key tile, so each row is shared by two threads, which
+//              exchange their partial row max per tile and their partial row sum per item through shared memory;
+//   warp 8     TMA producer: Q tile per item (double-buffered), K / V tiles into a 2-stage ring;
+//   warp 9     MMA issuer: S = Q K^T into TMEM, then O += P V with P read from TMEM (tcgen05.mma A-from-TMEM).
 // An item is one 128-row query tile of one (b, h) slice; a CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...
 // with the query tile fastest, so the CTAs working on one slice at the same time share its K / V through L2.
-// Per key tile the softmax warps write P as a 16-bit hi / lo pair over the S columns they have read (P_hi in
-// [c, c + 16), P_lo in [c + 16, c + 32) of each 32-column chunk c) and the MMA warp accumulates O += P_hi V + P_lo V in
-// TMEM. The running max is updated lazily: O and l are rescaled only when a tile's max exceeds the max in use by
-// more than 8 (in log2 units), so P stays below 256 and the common case touches O not at all. O / l and
-// lse = m + log l at the end of the item. Same math as the reference's _fwd_kernel (triton_kernels.py:98-163).
+// Per key tile the softmax warps write P as a 16-bit hi / lo pair over the S columns they have read (for keys
+// [16 k, 16 k + 16): P_hi in columns [16 k, 16 k + 8), P_lo in [16 k + 8, 16 k + 16)) and the MMA warp accumulates
+// O += P_hi V + P_lo V in TMEM. The running max is updated lazily: O and l are rescaled only when a tile's max exceeds
+// the max in use by more than 8 (in log2 units), so P stays below 256 and the common case touches O not at all.
+// O / l and lse = m + log l at the end of the item. Same math as the reference's _fwd_kernel
+// (triton_kernels.py:98-163).
 template <typename T, int D>
-__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
     tc_fwd_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, T* __restrict__ out, float* __restrict__ lse, int BH,
                        int H, int N, float scale) {
@@ -159,7 +184,8 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   constexpr int NS = L::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
-  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done;
+  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done, xch[2];
+  __shared__ float xval[2][2][128];  // [exchange parity][warpgroup][row]: partial row max (per tile) or sum (per item)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -178,13 +204,14 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+      mbar_init(&xch[i], 256);
     }
     for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(&s_full, 1);
-    mbar_init(&p_full, 128);
+    mbar_init(&p_full, 256);
     mbar_init(&o_done, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -199,7 +226,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tq);
@@ -230,7 +257,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
         if (!ok) break;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t tS = tmem, tO = tmem + 128;
@@ -254,10 +281,10 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk) {
-            const uint32_t a_hi = tS + (kk >> 1) * 32 + (kk & 1) * 8;
+            const uint32_t a_hi = tS + kk * 16;
             const uint64_t bdesc = desc_mnmajor(sV(s), kk);
             mma_ts(tO, a_hi, bdesc, kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
-            mma_ts(tO, a_hi + 16, bdesc, kIdPV, 1u);
+            mma_ts(tO, a_hi + 8, bdesc, kIdPV, 1u);
           }
           mma_commit(&o_done);
           mma_commit(&kv_empty[s]);
@@ -265,31 +292,39 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- softmax / epilogue (warps 0-3)
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tO = tmem + 128 + lane_off;
-    uint32_t t = 0;
+    // ---------------------------------------------------------------- softmax / epilogue (warps 0-7)
+    const int half = warp >> 2, lrow = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + half * 64, tO = tmem + 128 + lane_off;
+    uint32_t t = 0, x = 0;  // tile counter, exchange counter
     bool ok = true;
+    // Exchange a per-row partial value with the other warpgroup's thread of the same row; returns the partner's.
+    auto exchange = [&](float v) -> float {
+      const int b = static_cast<int>(x & 1);
+      xval[b][half][lrow] = v;
+      mbar_arrive(&xch[b]);
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&xch[b], (x >> 1) & 1, 133, abort));
+      ++x;
+      return xval[b][half ^ 1][lrow];
+    };
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
       const int bh = static_cast<int>(it / n_kt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-      const int row = qt * kTile + tid;
+      const int row = qt * kTile + lrow;
       float m_used = -INFINITY, l_run = 0.f;
       for (int j = 0; j < n_kt; ++j, ++t) {
-        ok = mbar_wait_or_abort(&s_full, t & 1, 131, abort);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 131, abort));
         if (!ok) break;
         tc_fence_after();
-        const int j0 = j * kTile;
-        const int valid = min(kTile, N - j0);  // keys of this tile inside [0, N); uniform over the CTA
-        // Pass 1: the tile's row max of the raw scores, scaled once (rounding is monotonic, so this equals the max of
-        // the scaled scores; a negative scale turns it into the min).
+        const int valid = min(kTile, N - j * kTile) - half * 64;  // this thread's keys inside [0, N)
+        // Pass 1: the row max of the raw scores over both halves, scaled once (rounding is monotonic, so this equals
+        // the max of the scaled scores; a negative scale turns it into the min).
         float mraw = scale >= 0.f ? -INFINITY : INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < kTile; c += 32) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
           uint32_t r[32];
           tmem_ld32(tS + c, r);
           tmem_wait_ld();
-          if (valid == kTile) {
+          if (valid >= 64) {
             if (scale >= 0.f) {
 #pragma unroll
               for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(r[e]));
@@ -303,17 +338,20 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
               if (c + e < valid) mraw = scale >= 0.f ? fmaxf(mraw, __uint_as_float(r[e])) : fminf(mraw, __uint_as_float(r[e]));
           }
         }
+        const float other = exchange(mraw);
+        if (!ok) break;
+        mraw = scale >= 0.f ? fmaxf(mraw, other) : fminf(mraw, other);
         const float mx = mraw * scale;
-        // Lazy rescale. tcgen05.ld / st are warp-collective, so the decision is made per warp: if any row of the warp
-        // needs it, the whole warp rewrites its O rows, with alpha = 1 for the rows that keep their max. The previous
-        // P V product has completed (S of this tile was issued after it), so O can be rewritten.
+        // Lazy rescale. tcgen05.ld / st are warp-collective, so the decision is made per warp (both warpgroups see the
+        // same rows and make the same decision); each warpgroup rewrites its half of the O columns, alpha = 1 for the
+        // rows that keep their max. The previous P V product has completed (S of this tile was issued after it).
         const bool need = (j == 0) || (mx > m_used + kTau);
         if (j == 0) {
           m_used = mx;
         } else if (__any_sync(0xffffffffu, need)) {
           const float alpha = need ? exp_nat(m_used - mx) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
+          for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
             uint32_t r[32];
             tmem_ld32(tO + c, r);
             tmem_wait_ld();
@@ -335,38 +373,31 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
             m_used = mx;
           }
         }
-        // Pass 2: P = exp(s * scale - m_used) as a 16-bit hi / lo pair over the S columns just read.
+        // Pass 2: P = exp(s * scale - m_used) as a 16-bit hi / lo pair over the S columns just read: for keys
+        // [16 k, 16 k + 16), P_hi in columns [16 k, 16 k + 8) and P_lo in [16 k + 8, 16 k + 16).
         float psum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < kTile; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tS + c, r);
-          tmem_wait_ld();
-          uint32_t hi[8], hi2[8], lo[8], lo2[8];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
+        for (int c = 0; c < 64; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tS + c, r);
+          tmem_wait_ld();
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
             float p0 = exp_nat(fmaf(__uint_as_float(r[e]), scale, -m_used));
             float p1 = exp_nat(fmaf(__uint_as_float(r[e + 1]), scale, -m_used));
-            if (valid < kTile) {
+            if (valid < 64) {
               if (c + e >= valid) p0 = 0.f;
               if (c + e + 1 >= valid) p1 = 0.f;
             }
             psum += p0 + p1;
             const uint32_t ph = pack2<T>(p0, p1);
             const float h0 = unpack_lo<T>(ph), h1 = unpack_hi<T>(ph);
-            const uint32_t pl = pack2<T>(p0 - h0, p1 - h1);
-            if (e < 16) {
-              hi[e >> 1] = ph;
-              lo[e >> 1] = pl;
-            } else {
-              hi2[(e - 16) >> 1] = ph;
-              lo2[(e - 16) >> 1] = pl;
-            }
+            hi[e >> 1] = ph;
+            lo[e >> 1] = pack2<T>(p0 - h0, p1 - h1);
           }
           tmem_st8(tS + c, hi);
-          tmem_st8(tS + c + 8, hi2);
-          tmem_st8(tS + c + 16, lo);
-          tmem_st8(tS + c + 24, lo2);
+          tmem_st8(tS + c + 8, lo);
         }
         l_run += psum;
         tmem_wait_st();
@@ -374,15 +405,16 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
         mbar_arrive(&p_full);
       }
       if (!ok) break;
-      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 132, abort);
-      ok = __all_sync(0xffffffffu, ok);
+      const float l_total = l_run + exchange(l_run);
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 132, abort));
       if (!ok) break;
       tc_fence_after();
-      T* none = nullptr;
       const bool row_ok = row < N;
       const int64_t grow = static_cast<int64_t>(bh) * N + row;
-      store_row_from_tmem<T, D>(tO, 1.f / l_run, row_ok ? out + grow * D : none);
-      if (row_ok) lse[grow] = m_used + logf(l_run);
+      T* dst = row_ok ? out + grow * D : nullptr;
+      store_cols_from_tmem<T, D / 2>(tO, half * (D / 2), 1.f / l_total, dst);
+      if (row_ok && half == 0) lse[grow] = m_used + logf(l_total);
     }
   }
   tc_fence_before();
@@ -430,18 +462,22 @@ struct BwdPipeLayout {
   static constexpr uint32_t kBytes = kStats + 2 * 2 * 64 * 4;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;
 };
 
-// Row pass of the backward for N > 128, persistent and warp-specialized like the forward: an item is 128 query rows
-// of one slice (Q, dO double-buffered per item); the key tiles stream through a 2-stage ring in steps of 64 keys.
-// Per step: S = Q K^T and dP = dO V^T (M = 128 queries, N = 64 keys) into TMEM; the compute warps (thread t = query
-// row t) form dS = P (dP - D) with P = exp(fma(s, scale, -lse)), pack it to 16 bits over the S columns they have
-// read, and the MMA warp accumulates dQ += dS K with dS read from TMEM. D_i = <dO_i, O_i> is computed at the start of
-// each item (stored O) and written to `di` for the column pass. The reference's _bwd_dq_kernel + _rowdot_kernel
-// (triton_kernels.py:277-339, :171-181). TMEM: S [0, 64), dP [64, 128), dQ [128, 128 + D).
+// Row pass of the backward for N > 128, persistent and warp-specialized: an item is 128 query rows of one slice
+// (Q, dO double-buffered per item); the key tiles stream through a 2-stage ring in steps of 64 keys.
+//   warps 0-7  compute, two warpgroups: warp w owns TMEM lanes 32 (w % 4) .. + 31 (query rows) and key columns
+//              32 (w / 4) .. + 31 of each step, so each row's 64 keys are split between two threads;
+//   warp 8     TMA producer;  warp 9  MMA issuer.
+// Per step: S = Q K^T and dP = dO V^T (M = 128 queries, N = 64 keys) into TMEM; the compute warps form
+// dS = P (dP - D) with P = exp(fma(s, scale, -lse)), pack it to 16 bits over the S columns they have read (key k at
+// column 32 (k / 32) + (k % 32) / 2), and the MMA warp accumulates dQ += dS K with dS read from TMEM. D_i = <dO_i, O_i>
+// is computed at the start of each item from the stored O and written to `di` for the column pass. The reference's
+// _bwd_dq_kernel + _rowdot_kernel (triton_kernels.py:277-339, :171-181). TMEM: S [0, 64), dP [64, 128),
+// dQ [128, 128 + D).
 template <typename T, int D>
-__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
     tc_bwd_dq_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk64,
                           const __grid_constant__ CUtensorMap tv64, const __grid_constant__ CUtensorMap tdo,
                           const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
@@ -475,7 +511,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(&s_full, 1);
-    mbar_init(&p_full, 128);
+    mbar_init(&p_full, 256);
     mbar_init(&o_done, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -490,7 +526,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       uint32_t kv_use = 0;
       int64_t li = 0;
@@ -518,7 +554,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t tS = tmem, tDP = tmem + 64, tDQ = tmem + 128;
       uint32_t kv_use = 0, t = 0;
@@ -545,75 +581,71 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tDQ, tS + kk * 8, desc_mnmajor_r(sK(s), kk, L::kHalf64), kIdKM, (j > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tDQ, tS + (kk >> 1) * 32 + (kk & 1) * 8, desc_mnmajor_r(sK(s), kk, L::kHalf64), kIdKM,
+                   (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&o_done);
           mma_commit(&kv_empty[s]);
         }
       }
     }
   } else {
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tDP = tmem + 64 + lane_off, tDQ = tmem + 128 + lane_off;
+    const int half = warp >> 2, lrow = (warp & 3) * 32 + lane;  // key-column half, query row in the tile
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + half * 32, tDP = tmem + 64 + lane_off + half * 32;
     uint32_t t = 0;
     int64_t li = 0;
     bool ok = true;
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
       const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
       const int qb = static_cast<int>(li & 1);
-      const int row = qt * kTile + tid;
+      const int row = qt * kTile + lrow;
       const bool row_ok = row < N;
       const int64_t grow = static_cast<int64_t>(bh) * N + row;
       const float Li = row_ok ? lse[grow] : 0.f;
-      ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 261, abort);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 261, abort));
       if (!ok) break;
       float Di = 0.f;
       if (row_ok) {
-        Di = row_delta<T, D>(sDO(qb), tid, o + grow * D);
-        di_out[grow] = Di;
+        Di = row_delta<T, D>(sDO(qb), lrow, o + grow * D);
+        if (half == 0) di_out[grow] = Di;
       }
       for (int j = 0; j < n_ks; ++j, ++t) {
-        ok = mbar_wait_or_abort(&s_full, t & 1, 262, abort);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 262, abort));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 64; c += 32) {
-          uint32_t rs[32], rp[32];
-          tmem_ld32(tS + c, rs);
-          tmem_ld32(tDP + c, rp);
-          tmem_wait_ld();
-          // Query rows past N have zero Q / dO (TMA fill) and Li = Di = 0, so their dS is exactly 0 without a mask;
-          // keys past N (the last step only) are masked so exp(-Li) cannot reach dQ.
-          const int valid = N - j * 64;
-          uint32_t a[8], b8[8];
+        // Query rows past N have zero Q / dO (TMA fill) and Li = Di = 0, so their dS is exactly 0 without a mask;
+        // keys past N (the last step only) are masked so exp(-Li) cannot reach dQ.
+        const int valid = N - j * 64 - half * 32;
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
+        for (int sc = 0; sc < 32; sc += 16) {
+          uint32_t rs[16], rp[16];
+          tmem_ld16(tS + sc, rs);
+          tmem_ld16(tDP + sc, rp);
+          tmem_wait_ld();
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
             float ds[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               float p = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li));
-              if (valid < 64 && c + e + u >= valid) p = 0.f;
+              if (valid < 32 && sc + e + u >= valid) p = 0.f;
               ds[u] = p * (__uint_as_float(rp[e + u]) - Di);
             }
-            const uint32_t pk = pack2<T>(ds[0], ds[1]);
-            if (e < 16) a[e >> 1] = pk;
-            else b8[(e - 16) >> 1] = pk;
+            pk[e >> 1] = pack2<T>(ds[0], ds[1]);
           }
-          tmem_st8(tS + (c >> 1), a);
-          tmem_st8(tS + (c >> 1) + 8, b8);
+          tmem_st8(tS + (sc >> 1), pk);
         }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full);
       }
       if (!ok) break;
-      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 263, abort);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 263, abort));
       if (!ok) break;
       tc_fence_after();
-      T* none = nullptr;
-      store_row_from_tmem<T, D>(tDQ, scale, row_ok ? dq + grow * D : none);
+      T* dst = row_ok ? dq + grow * D : nullptr;
+      store_cols_from_tmem<T, D / 2>(tmem + 128 + lane_off, half * (D / 2), scale, dst);
     }
   }
   tc_fence_before();
@@ -622,13 +654,14 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
 }
 
 // Column pass of the backward for N > 128: an item is 128 keys of one slice (K, V double-buffered per item); the
-// query tiles stream through a 2-stage ring in steps of 64 queries. Per step: S^T = K Q^T and dP^T = V dO^T
-// (M = 128 keys, N = 64 queries) into TMEM; the compute warps (thread t = key t) form P^T and dS^T with the queries'
-// lse and D staged in shared memory, pack both to 16 bits over the columns they have read, and the MMA warp
-// accumulates dV += P^T dO and dK += dS^T Q with A read from TMEM. The reference's _bwd_col_kernel
-// (triton_kernels.py:184-274, two-kernel mode). TMEM: S^T [0, 64), dP^T [64, 128), dK [128, 128 + D), dV after dK.
+// query tiles stream through a 2-stage ring in steps of 64 queries, with each step's lse and D staged in shared memory
+// by the producer warp. Per step: S^T = K Q^T and dP^T = V dO^T (M = 128 keys, N = 64 queries) into TMEM; the two
+// compute warpgroups (warp w: keys 32 (w % 4) .., query columns 32 (w / 4) ..) form P^T and dS^T, pack both to 16 bits
+// over the columns they have read, and the MMA warp accumulates dV += P^T dO and dK += dS^T Q with A read from TMEM.
+// The reference's _bwd_col_kernel (triton_kernels.py:184-274, two-kernel mode).
+// TMEM: S^T [0, 64), dP^T [64, 128), dK [128, 128 + D), dV after dK.
 template <typename T, int D>
-__global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
+__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
     tc_bwd_dkdv_pipe_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                             const __grid_constant__ CUtensorMap tq64, const __grid_constant__ CUtensorMap tdo64,
                             const float* __restrict__ lse, const float* __restrict__ di, T* __restrict__ dk,
@@ -652,6 +685,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   auto sV = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig + L::kBig; };
   auto sQ = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
   auto sDO = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
+  float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [stage][lse 64 | D 64]
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -663,12 +697,11 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(&s_full, 1);
-    mbar_init(&p_full, 128);
+    mbar_init(&p_full, 256);
     mbar_init(&o_done, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
-  float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [stage][lse 64 | D 64]
   if (warp == 0) {
     tmem_alloc(&tmem_slot, kCols);
     tmem_relinquish();
@@ -679,7 +712,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // Lane 0 issues the TMA loads; all 32 lanes stage each query step's lse and D (64 + 64 floats) in shared memory.
     uint32_t q_use = 0;
     int64_t li = 0;
@@ -723,7 +756,7 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
         mbar_arrive(&q_full[s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t tS = tmem, tDP = tmem + 64, tDK = tmem + 128, tDV = tmem + 128 + D;
       uint32_t q_use = 0, t = 0;
@@ -749,8 +782,9 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            mma_ts(tDV, tS + kk * 8, desc_mnmajor_r(sDO(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
-            mma_ts(tDK, tDP + kk * 8, desc_mnmajor_r(sQ(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t col = (kk >> 1) * 32 + (kk & 1) * 8;
+            mma_ts(tDV, tS + col, desc_mnmajor_r(sDO(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tDK, tDP + col, desc_mnmajor_r(sQ(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&o_done);
           mma_commit(&q_empty[s]);
@@ -759,68 +793,56 @@ __global__ void __launch_bounds__(192, (D == 64) ? 2 : 1)
       }
     }
   } else {
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_off, tDP = tmem + 64 + lane_off;
-    const uint32_t tDK = tmem + 128 + lane_off, tDV = tmem + 128 + D + lane_off;
+    const int half = warp >> 2, lkey = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + half * 32, tDP = tmem + 64 + lane_off + half * 32;
     uint32_t t = 0;
     bool ok = true;
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
       const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-      const int64_t base = static_cast<int64_t>(bh) * N;
       for (int i = 0; i < n_qs; ++i, ++t) {
         const int s = static_cast<int>(t % NS);
-        ok = mbar_wait_or_abort(&q_full[s], (t / NS) & 1, 293, abort);  // this step's staged lse / D
-        ok = __all_sync(0xffffffffu, ok);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_full[s], (t / NS) & 1, 293, abort));
         if (!ok) break;
-        const float* st = stats + s * 128;
-        ok = mbar_wait_or_abort(&s_full, t & 1, 291, abort);
-        ok = __all_sync(0xffffffffu, ok);
+        const float* st = stats + s * 128 + half * 32;
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 291, abort));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 64; c += 32) {
-          uint32_t rs[32], rp[32];
-          tmem_ld32(tS + c, rs);
-          tmem_ld32(tDP + c, rp);
-          tmem_wait_ld();
-          uint32_t p0[8], p1[8], d0[8], d1[8];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
+        for (int sc = 0; sc < 32; sc += 16) {
+          uint32_t rs[16], rp[16];
+          tmem_ld16(tS + sc, rs);
+          tmem_ld16(tDP + sc, rp);
+          tmem_wait_ld();
+          uint32_t pp[8], pd[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
             float p[2], ds[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              const int qc = c + e + u;
+              const int qc = sc + e + u;
               p[u] = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -st[qc]));
               ds[u] = p[u] * (__uint_as_float(rp[e + u]) - st[64 + qc]);
             }
-            const uint32_t pp = pack2<T>(p[0], p[1]), pd = pack2<T>(ds[0], ds[1]);
-            if (e < 16) {
-              p0[e >> 1] = pp;
-              d0[e >> 1] = pd;
-            } else {
-              p1[(e - 16) >> 1] = pp;
-              d1[(e - 16) >> 1] = pd;
-            }
+            pp[e >> 1] = pack2<T>(p[0], p[1]);
+            pd[e >> 1] = pack2<T>(ds[0], ds[1]);
           }
-          tmem_st8(tS + (c >> 1), p0);
-          tmem_st8(tS + (c >> 1) + 8, p1);
-          tmem_st8(tDP + (c >> 1), d0);
-          tmem_st8(tDP + (c >> 1) + 8, d1);
+          tmem_st8(tS + (sc >> 1), pp);
+          tmem_st8(tDP + (sc >> 1), pd);
         }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full);
       }
       if (!ok) break;
-      ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 292, abort);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 292, abort));
       if (!ok) break;
       tc_fence_after();
-      const int key = kt * kTile + tid;
-      const int64_t gk = base + key;
-      T* none = nullptr;
-      store_row_from_tmem<T, D>(tDK, scale, key < N ? dk + gk * D : none);
-      store_row_from_tmem<T, D>(tDV, 1.f, key < N ? dv + gk * D : none);
+      const int key = kt * kTile + lkey;
+      const int64_t gk = static_cast<int64_t>(bh) * N + key;
+      // Warpgroup 0 writes dK, warpgroup 1 writes dV.
+      T* dst = key < N ? (half == 0 ? dk : dv) + gk * D : nullptr;
+      store_cols_from_tmem<T, D>(tmem + lane_off + (half == 0 ? 128 : 128 + D), 0, half == 0 ? scale : 1.f, dst);
     }
   }
   tc_fence_before();
