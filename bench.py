@@ -14,6 +14,7 @@ attention, torch CPU for the rest) timed on a bounded sample on this host.
 
 ``--impl reference`` times only that CPU path (rank 0) on the same config and prints its own line.
 ``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape).
+``--mode train`` times BASELINE config 2's training step (double backward, flat-bucket NCCL all-reduce, AdamW).
 """
 
 from __future__ import annotations
@@ -360,6 +361,98 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------------------------- training
+
+
+TRAIN_ROWS, TRAIN_BOARD, TRAIN_MICROSTEPS, TRAIN_GRADED = 768, 9, 16, 7
+
+
+def sudoku_like_tokens(n: int, gen: torch.Generator) -> torch.Tensor:
+    """Synthetic stand-in for Sudoku-Extreme boards (the dataset is not available): 81 cells, 0 (blank) with
+    p = 0.7, otherwise uniform in 1..9. Labels are uniform in 1..9."""
+    blank = torch.rand(n, 81, generator=gen) < 0.7
+    digits = torch.randint(1, 10, (n, 81), generator=gen)
+    return torch.where(blank, torch.zeros_like(digits), digits).to(torch.int32), torch.randint(1, 10, (n, 81), generator=gen)
+
+
+def run_train(args) -> None:
+    """BASELINE config 2 on each rank (weak scaling): 768 rows, L = 81, 16 microsteps per segment of which the last
+    7 carry a graph (create_graph=True, so the backward runs the attention's double backward), cross-entropy of the
+    decoded endpoint, backward, one flat-bucket NCCL all-reduce of all gradients, AdamW step."""
+    from ebr_b200 import _native, fused_attn, runtime
+    from ebr_b200.build import build
+    from ebr_b200.energy import EnergyConfig, EnergyReasoner, train_step_loss
+
+    rank, world, local = runtime.init_distributed()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if rank == 0:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.manual_seed(0)
+    cfg = EnergyConfig(board_height=TRAIN_BOARD, board_width=TRAIN_BOARD, vocab_size=10)
+    model = EnergyReasoner(cfg).to(device)
+    runtime.broadcast_model(model)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    gen = torch.Generator().manual_seed(2000 + rank)
+    tok, labels = sudoku_like_tokens(TRAIN_ROWS, gen)
+    tok, labels = tok.to(device), labels.to(device)
+    z0 = model.fresh_states(TRAIN_ROWS, device)
+    params = [p for p in model.parameters() if p.requires_grad]
+
+    def step():
+        x = model.input_embeddings(tok)
+        loss = train_step_loss(model, z0, x, labels, prefix=TRAIN_MICROSTEPS - TRAIN_GRADED, graded=TRAIN_GRADED)
+        opt.zero_grad(set_to_none=True)
+        (loss / (TRAIN_ROWS * world)).backward()
+        runtime.allreduce_gradients(params)
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.device_status()
+    if world > 1:
+        torch.distributed.barrier()
+    launches0 = _native.launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with fused_attn.kernel_timer() as timer:
+        a.record()
+        for _ in range(args.steps):
+            loss = step()
+        b.record()
+        torch.cuda.synchronize()
+    ms = runtime.max_over_ranks(a.elapsed_time(b))
+    ops = timer.summary()
+    runtime.check_param_sync(model, rtol=1e-9)
+    value = world * TRAIN_ROWS * TRAIN_MICROSTEPS * args.steps / (ms / 1000.0)
+    if rank == 0:
+        line = {
+            "metric": "latent-descent training sample-steps/s (L=81, B=768)",
+            "value": round(value, 3),
+            "unit": "sample-steps/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "dtype": "bf16",
+            "data": "synthetic (seeded sudoku-like boards; Sudoku-Extreme is not available offline), random-init weights",
+            "config": {"workload": "cfg2 training step (16 microsteps, last 7 graded, double backward, AdamW)",
+                       "rows_per_gpu": TRAIN_ROWS, "seq_len": 81, "parallelism": f"dp{world} (one flat NCCL all-reduce)"},
+            "loss": float(loss.item()),
+            "gpu_launches": int(_native.launch_count() - launches0),
+            "attention_ms": {n: round(v["ms"], 3) for n, v in ops.items()},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 # --------------------------------------------------------------------------------------------------------- sweep
 
 
@@ -420,7 +513,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["descent", "sweep"], default="descent")
+    ap.add_argument("--mode", choices=["descent", "sweep", "train"], default="descent")
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
     ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd", help="sweep: which passes to time")
@@ -433,6 +526,8 @@ def main() -> None:
         run_reference(args)
     elif args.mode == "sweep":
         run_sweep(args)
+    elif args.mode == "train":
+        run_train(args)
     else:
         run_ours(args)
 
