@@ -314,7 +314,7 @@ def run_ours(args) -> None:
         tfile = ROOT / "profiles" / "traffic.json"
         if tfile.exists():
             t = json.loads(tfile.read_text()).get(dom_name)
-            if t:
+            if t and t.get("N") == N_ and t.get("D") == D_:
                 traffic = t["bytes_per_slice"] * B_ * H_
         roofline = {
             "bound": "tensor",
