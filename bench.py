@@ -143,7 +143,8 @@ def build_model(device, attention=None):
     from ebr_b200.energy import EnergyConfig, EnergyReasoner
 
     torch.manual_seed(0)
-    cfg = EnergyConfig(board_height=BOARD, board_width=BOARD, vocab_size=5, softplus=True)
+    layers = "eager" if torch.device(device).type == "cpu" else "fused"
+    cfg = EnergyConfig(board_height=BOARD, board_width=BOARD, vocab_size=5, softplus=True, layers=layers)
     return EnergyReasoner(cfg, attention=attention).to(device)
 
 

@@ -32,6 +32,18 @@ EXPORTED = (
     "ebr_attn_bwd_noalloc",
 )
 
+# include/ebr_layers.h: the fused kernels on either side of the attention.
+EXPORTED_LAYERS = (
+    "ebr_rope_split",
+    "ebr_rope_merge",
+    "ebr_add_rms_norm",
+    "ebr_rms_norm_bwd",
+    "ebr_swiglu_fwd",
+    "ebr_swiglu_bwd",
+    "ebr_descent_step",
+    "ebr_descent_step_scratch_floats",
+)
+
 
 class Operand(ctypes.Structure):
     """``ebr_operand``: a strided [B, H, N, D] operand (strides in elements, unit head-dim stride)."""
@@ -82,6 +94,18 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ebr_attn_launch_count.restype = ctypes.c_uint64
     for name in ("ebr_attn_fwd", "ebr_attn_bwd", "ebr_attn_bwd_bwd", "ebr_attn_uses_tensor_cores",
                  "ebr_attn_device_status"):  # fmt: skip
+        getattr(lib, name).restype = ctypes.c_int
+    dbl, fp = ctypes.c_double, ctypes.c_void_p
+    lib.ebr_rope_split.argtypes = dims + [vp, i64, i64, fp, fp, fp, vp, vp, vp, vp]
+    lib.ebr_rope_merge.argtypes = dims + [op, op, op, fp, fp, fp, vp, vp]
+    lib.ebr_add_rms_norm.argtypes = [ctypes.c_int, i64, i64, dbl, vp, vp, vp, vp, fp, vp, dbl, vp]
+    lib.ebr_rms_norm_bwd.argtypes = [ctypes.c_int, i64, i64, vp, fp, vp, vp, vp]
+    lib.ebr_swiglu_fwd.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp]
+    lib.ebr_swiglu_bwd.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp, vp]
+    lib.ebr_descent_step.argtypes = [ctypes.c_int, i64, i64, dbl, dbl, vp, vp, vp, fp, sz, vp]
+    lib.ebr_descent_step_scratch_floats.argtypes = [i64, i64]
+    lib.ebr_descent_step_scratch_floats.restype = sz
+    for name in EXPORTED_LAYERS[:-1]:
         getattr(lib, name).restype = ctypes.c_int
 
 

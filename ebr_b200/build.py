@@ -41,7 +41,7 @@ def _nvcc() -> str:
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "ebr_attn.h"]
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "ebr_attn.h", ROOT / "include" / "ebr_layers.h"]
 
 
 def up_to_date() -> bool:

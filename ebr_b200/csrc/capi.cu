@@ -645,3 +645,6 @@ const char* ebr_attn_last_error(void) { return g_last_error; }
 uint64_t ebr_attn_launch_count(void) { return g_launch_count.load(); }
 
 }  // extern "C"
+
+// The fused kernels on either side of the attention (include/ebr_layers.h).
+#include "layers_capi.cuh"

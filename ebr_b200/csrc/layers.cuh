@@ -1,0 +1,378 @@
+// layers.cuh: the fused pointwise / row kernels on either side of the attention in the energy network (2D-RoPE split
+// and merge, residual + rms_norm and its backward, the SwiGLU activation and its backward, the descent step with its
+// sphere projection). All are HBM-bound: each reads its inputs once and writes its outputs once, 16 bytes per thread
+// access where the pointers and row lengths allow it (V elements of the I/O type), else one element per access.
+//
+// Rounding follows the reference's eager code operation by operation (multiplies and adds rounded separately with the
+// _rn intrinsics, so the compiler does not contract them into fused multiply-adds, and one rounding to the I/O type
+// where the eager code converts), so outputs equal the eager ones except where a row sum is taken in another order.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace ebr {
+namespace layers {
+
+constexpr int kThreads = 256;
+
+// ------------------------------------------------------------------------------------------------ arithmetic
+
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ double sub_rn(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(a, b); }
+__device__ __forceinline__ float rsqrt_c(float x) { return rsqrtf(x); }
+__device__ __forceinline__ double rsqrt_c(double x) { return rsqrt(x); }
+__device__ __forceinline__ float sqrt_c(float x) { return sqrtf(x); }
+__device__ __forceinline__ double sqrt_c(double x) { return sqrt(x); }
+__device__ __forceinline__ float exp_c(float x) { return expf(x); }
+__device__ __forceinline__ double exp_c(double x) { return exp(x); }
+
+// Round a compute-type value to the I/O type and back.
+template <typename T>
+__device__ __forceinline__ typename Elem<T>::C rnd(typename Elem<T>::C x) {
+  return static_cast<typename Elem<T>::C>(Elem<T>::to(x));
+}
+
+// V elements of T moved as one access (16 bytes when V * sizeof(T) == 16).
+template <typename T, int V>
+struct alignas(sizeof(T) * V) Pack {
+  T e[V];
+};
+
+template <typename T, int V>
+__device__ __forceinline__ void load_c(const T* p, typename Elem<T>::C (&out)[V]) {
+  const Pack<T, V> pk = *reinterpret_cast<const Pack<T, V>*>(p);
+#pragma unroll
+  for (int i = 0; i < V; ++i) out[i] = static_cast<typename Elem<T>::C>(pk.e[i]);
+}
+
+template <typename T, int V>
+__device__ __forceinline__ void store_c(T* p, const typename Elem<T>::C (&in)[V]) {
+  Pack<T, V> pk;
+#pragma unroll
+  for (int i = 0; i < V; ++i) pk.e[i] = Elem<T>::to(in[i]);
+  *reinterpret_cast<Pack<T, V>*>(p) = pk;
+}
+
+template <int V>
+__device__ __forceinline__ void load_table(const float* p, float (&out)[V]) {
+#pragma unroll
+  for (int i = 0; i < V; ++i) out[i] = __ldg(p + i);
+}
+
+template <typename C>
+__device__ __forceinline__ C warp_sum(C v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ int64_t grid_stride() { return static_cast<int64_t>(gridDim.x) * blockDim.x; }
+__device__ __forceinline__ int64_t global_tid() { return static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; }
+
+// ------------------------------------------------------------------------------------------------ 2D RoPE split
+
+// quarter_swap's source index for element d of a head row of D = 4 Q elements: (a, b, c, d) -> (b, a, d, c).
+__device__ __forceinline__ int swap_index(int d, int Q) { return ((d / Q) ^ 1) * Q + (d % Q); }
+
+// One thread per V-element chunk of one head row of one of q / k / v of one token; the chunk index runs fastest, then
+// the head, then q / k / v, then the token, so a warp reads a contiguous stretch of the qkv row. Chunks never straddle
+// a quarter (Q % V == 0), so a chunk's quarter_swap partner is the contiguous chunk at swap_index(d0).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) rope_split_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sn,
+                                                              int64_t N, int H, int D, int64_t total,
+                                                              const float* __restrict__ cos_t,
+                                                              const float* __restrict__ sin_t,
+                                                              const float* __restrict__ qscale, T* __restrict__ q,
+                                                              T* __restrict__ k, T* __restrict__ v) {
+  using C = typename Elem<T>::C;
+  const int cpr = D / V, Q = D / 4;
+  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
+    const int c = static_cast<int>(i % cpr);
+    int64_t r = i / cpr;
+    const int h = static_cast<int>(r % H);
+    r /= H;
+    const int part = static_cast<int>(r % 3);
+    const int64_t tok = r / 3;
+    const int64_t b = tok / N, n = tok - b * N;
+    const int d0 = c * V;
+    const T* row = qkv + b * sb + n * sn + static_cast<int64_t>(part * H + h) * D;
+    T* dst = (part == 0 ? q : part == 1 ? k : v) + ((b * H + h) * N + n) * D + d0;
+    C own[V];
+    load_c<T, V>(row + d0, own);
+    if (part == 2) {
+      store_c<T, V>(dst, own);
+      continue;
+    }
+    C partner[V];
+    float cs[V], sn_[V];
+    load_c<T, V>(row + swap_index(d0, Q), partner);
+    load_table<V>(cos_t + n * D + d0, cs);
+    load_table<V>(sin_t + n * D + d0, sn_);
+    C out[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      out[e] = rnd<T>(add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sn_[e]))));
+      if (part == 0 && qscale) out[e] = mul_rn(out[e], static_cast<C>(__ldg(qscale + h)));
+    }
+    store_c<T, V>(dst, out);
+  }
+}
+
+// The adjoint, one thread per V-element chunk of the dqkv row (same index order, so the writes are contiguous):
+// g' = g * cos + quarter_swap(g * sin) for dq (after its qscale rounding) and dk; dv copied.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) rope_merge_kernel(ebr_operand dq, ebr_operand dk, ebr_operand dv,
+                                                              int64_t N, int H, int D, int64_t total,
+                                                              const float* __restrict__ cos_t,
+                                                              const float* __restrict__ sin_t,
+                                                              const float* __restrict__ qscale, T* __restrict__ out) {
+  using C = typename Elem<T>::C;
+  const int cpr = D / V, Q = D / 4;
+  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
+    const int c = static_cast<int>(i % cpr);
+    int64_t r = i / cpr;
+    const int h = static_cast<int>(r % H);
+    r /= H;
+    const int part = static_cast<int>(r % 3);
+    const int64_t tok = r / 3;
+    const int64_t b = tok / N, n = tok - b * N;
+    const int d0 = c * V;
+    const ebr_operand& op = part == 0 ? dq : part == 1 ? dk : dv;
+    const T* row = static_cast<const T*>(op.data) + b * op.stride_b + h * op.stride_h + n * op.stride_n;
+    T* dst = out + tok * (3 * static_cast<int64_t>(H) * D) + static_cast<int64_t>(part * H + h) * D + d0;
+    C own[V];
+    load_c<T, V>(row + d0, own);
+    if (part == 2) {
+      store_c<T, V>(dst, own);
+      continue;
+    }
+    const int p0 = swap_index(d0, Q);
+    C partner[V];
+    float cs[V], sp[V];
+    load_c<T, V>(row + p0, partner);
+    load_table<V>(cos_t + n * D + d0, cs);
+    load_table<V>(sin_t + n * D + p0, sp);
+    if (part == 0 && qscale) {
+      const C s = static_cast<C>(__ldg(qscale + h));
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        own[e] = rnd<T>(mul_rn(own[e], s));
+        partner[e] = rnd<T>(mul_rn(partner[e], s));
+      }
+    }
+    C res[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e)
+      res[e] = add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sp[e])));
+    store_c<T, V>(dst, res);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ residual + rms_norm
+
+// One warp per row of C elements, two passes over the row (the second hits L1 / L2): the sum of squares of
+// s = round(x + a), then y = round(s * rstd) (+ round(post * post_scale), rounded again).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) add_rms_norm_kernel(int64_t rows, int C_, float eps,
+                                                                const T* __restrict__ x, const T* __restrict__ a,
+                                                                T* __restrict__ sum_out, T* __restrict__ y,
+                                                                float* __restrict__ rstd_out,
+                                                                const T* __restrict__ post, float post_scale) {
+  using C = typename Elem<T>::C;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = grid_stride() >> 5;
+  for (int64_t row = global_tid() >> 5; row < rows; row += warps) {
+    const int64_t base = row * C_;
+    C ss = 0;
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V];
+      load_c<T, V>(x + base + c, xs);
+      if (a) {
+        C as[V];
+        load_c<T, V>(a + base + c, as);
+#pragma unroll
+        for (int e = 0; e < V; ++e) xs[e] = rnd<T>(add_rn(xs[e], as[e]));
+        if (sum_out) store_c<T, V>(sum_out + base + c, xs);
+      }
+#pragma unroll
+      for (int e = 0; e < V; ++e) ss += xs[e] * xs[e];
+    }
+    ss = warp_sum(ss);
+    const C r = rsqrt_c(add_rn(div_rn(ss, static_cast<C>(C_)), static_cast<C>(eps)));
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V];
+      load_c<T, V>(x + base + c, xs);
+      if (a) {
+        C as[V];
+        load_c<T, V>(a + base + c, as);
+#pragma unroll
+        for (int e = 0; e < V; ++e) xs[e] = rnd<T>(add_rn(xs[e], as[e]));
+      }
+      C out[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) out[e] = mul_rn(xs[e], r);
+      if (post) {
+        C ps[V];
+        load_c<T, V>(post + base + c, ps);
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+          out[e] = add_rn(rnd<T>(out[e]), rnd<T>(mul_rn(ps[e], static_cast<C>(post_scale))));
+      }
+      store_c<T, V>(y + base + c, out);
+    }
+    if (rstd_out && lane == 0) rstd_out[row] = static_cast<float>(r);
+  }
+}
+
+// gs = round(rstd * (g - xh * mean(g * xh))), xh = s * rstd; one warp per row, two passes.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) rms_norm_bwd_kernel(int64_t rows, int C_, const T* __restrict__ s,
+                                                                const float* __restrict__ rstd,
+                                                                const T* __restrict__ gy, T* __restrict__ gs) {
+  using C = typename Elem<T>::C;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = grid_stride() >> 5;
+  for (int64_t row = global_tid() >> 5; row < rows; row += warps) {
+    const int64_t base = row * C_;
+    const C r = static_cast<C>(rstd[row]);
+    C dot = 0;
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V], gs_[V];
+      load_c<T, V>(s + base + c, xs);
+      load_c<T, V>(gy + base + c, gs_);
+#pragma unroll
+      for (int e = 0; e < V; ++e) dot += gs_[e] * (xs[e] * r);
+    }
+    const C mean = warp_sum(dot) / static_cast<C>(C_);
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V], g[V], out[V];
+      load_c<T, V>(s + base + c, xs);
+      load_c<T, V>(gy + base + c, g);
+#pragma unroll
+      for (int e = 0; e < V; ++e) out[e] = r * (g[e] - (xs[e] * r) * mean);
+      store_c<T, V>(gs + base + c, out);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ SwiGLU
+
+template <typename C>
+__device__ __forceinline__ C silu_c(C x) {
+  return x / (C(1) + exp_c(-x));
+}
+
+// out[r, j] = round(round(silu(h[r, j])) * h[r, I + j]); one thread per V-element chunk.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) swiglu_fwd_kernel(int64_t rows, int64_t I, const T* __restrict__ h,
+                                                              T* __restrict__ out) {
+  using C = typename Elem<T>::C;
+  const int64_t cpr = I / V, total = rows * cpr;
+  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
+    const int64_t r = i / cpr, j = (i - r * cpr) * V;
+    C g[V], u[V], o[V];
+    load_c<T, V>(h + r * 2 * I + j, g);
+    load_c<T, V>(h + r * 2 * I + I + j, u);
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = mul_rn(rnd<T>(silu_c(g[e])), u[e]);
+    store_c<T, V>(out + r * I + j, o);
+  }
+}
+
+// gh[r, j] = silu'(gate) * round(gout * up), gh[r, I + j] = round(gout * round(silu(gate))).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) swiglu_bwd_kernel(int64_t rows, int64_t I, const T* __restrict__ h,
+                                                              const T* __restrict__ gout, T* __restrict__ gh) {
+  using C = typename Elem<T>::C;
+  const int64_t cpr = I / V, total = rows * cpr;
+  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
+    const int64_t r = i / cpr, j = (i - r * cpr) * V;
+    C g[V], u[V], go[V], dg[V], du[V];
+    load_c<T, V>(h + r * 2 * I + j, g);
+    load_c<T, V>(h + r * 2 * I + I + j, u);
+    load_c<T, V>(gout + r * I + j, go);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const C sg = C(1) / (C(1) + exp_c(-g[e]));
+      const C act = rnd<T>(silu_c(g[e]));
+      du[e] = mul_rn(go[e], act);
+      const C da = rnd<T>(mul_rn(go[e], u[e]));
+      dg[e] = da * sg * (C(1) + g[e] * (C(1) - sg));
+    }
+    store_c<T, V>(gh + r * 2 * I + j, dg);
+    store_c<T, V>(gh + r * 2 * I + I + j, du);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ descent step
+
+constexpr int kStepChunk = kThreads * 32;  // elements of one row handled by one block
+
+// Block (chunk, row): u = round(v - round(alpha * g)) into z_next, and the block's sum of u^2 into partial.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) descent_step_kernel(int64_t row_elems, int chunks, double alpha,
+                                                                const T* __restrict__ v, const T* __restrict__ g,
+                                                                T* __restrict__ z_next, float* __restrict__ partial) {
+  using C = typename Elem<T>::C;
+  __shared__ float red[kThreads / 32];
+  const int64_t row = blockIdx.y;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kStepChunk;
+  const int64_t hi = min(lo + kStepChunk, row_elems);
+  const int64_t base = row * row_elems;
+  float ss = 0.f;
+  for (int64_t c = lo + threadIdx.x * V; c < hi; c += kThreads * V) {
+    C vs[V], gs[V], u[V];
+    load_c<T, V>(v + base + c, vs);
+    load_c<T, V>(g + base + c, gs);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      u[e] = rnd<T>(sub_rn(vs[e], rnd<T>(mul_rn(static_cast<C>(alpha), gs[e]))));
+      ss += static_cast<float>(u[e] * u[e]);
+    }
+    store_c<T, V>(z_next + base + c, u);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+    partial[row * chunks + blockIdx.x] = t;
+  }
+}
+
+// Block (chunk, row): rms of the row from its partial sums (every block adds them in the same order), then
+// z_next = round(u / max(rms, eps)) in place.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) sphere_kernel(int64_t row_elems, int chunks, float eps,
+                                                          T* __restrict__ z_next, const float* __restrict__ partial) {
+  using C = typename Elem<T>::C;
+  __shared__ float rms_s;
+  const int64_t row = blockIdx.y;
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < chunks; ++i) t += partial[row * chunks + i];
+    rms_s = fmaxf(sqrtf(__fdiv_rn(t, static_cast<float>(row_elems))), eps);
+  }
+  __syncthreads();
+  const C rms = static_cast<C>(rms_s);
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kStepChunk;
+  const int64_t hi = min(lo + kStepChunk, row_elems);
+  const int64_t base = row * row_elems;
+  for (int64_t c = lo + threadIdx.x * V; c < hi; c += kThreads * V) {
+    C u[V];
+    load_c<T, V>(z_next + base + c, u);
+#pragma unroll
+    for (int e = 0; e < V; ++e) u[e] = div_rn(u[e], rms);
+    store_c<T, V>(z_next + base + c, u);
+  }
+}
+
+}  // namespace layers
+}  // namespace ebr

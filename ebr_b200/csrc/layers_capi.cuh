@@ -1,0 +1,275 @@
+// layers_capi.cuh: the C ABI of include/ebr_layers.h (included at the end of capi.cu, which owns the error state,
+// the device check and the launch counter). Validates arguments, picks the 16-byte vector width when the pointers and
+// row lengths allow it, and launches the kernels of layers.cuh on the caller's stream.
+#pragma once
+
+#include <algorithm>
+#include <initializer_list>
+#include <type_traits>
+
+#include "../../include/ebr_layers.h"
+#include "layers.cuh"
+
+namespace {
+
+using ebr::layers::kThreads;
+
+// Grid for a grid-stride kernel over `work` thread-items.
+dim3 flat_grid(int device, int64_t work) {
+  const int64_t want = (work + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count(device)) * 16;
+  return dim3(static_cast<unsigned>(std::max<int64_t>(1, std::min(want, cap))));
+}
+
+template <typename T>
+constexpr int vec_width() {
+  return static_cast<int>(16 / sizeof(T));
+}
+
+bool all_aligned16(std::initializer_list<const void*> ps) {
+  for (const void* p : ps)
+    if (p && !aligned16(p)) return false;
+  return true;
+}
+
+int check_layer_dtype(int dtype, bool allow_f64) {
+  if (dtype == EBR_FLOAT32 || dtype == EBR_FLOAT16 || dtype == EBR_BFLOAT16) return EBR_OK;
+  if (dtype == EBR_FLOAT64 && allow_f64) return EBR_OK;
+  return set_error(EBR_ERR_DTYPE, "unsupported dtype for this layer kernel%s%s");
+}
+
+// Run fn.template operator()<T>() for the I/O type of `dtype`.
+template <typename Fn>
+int with_type(int dtype, Fn&& fn) {
+  switch (dtype) {
+    case EBR_FLOAT32: return fn(static_cast<float*>(nullptr));
+    case EBR_FLOAT16: return fn(static_cast<__half*>(nullptr));
+    case EBR_BFLOAT16: return fn(static_cast<__nv_bfloat16*>(nullptr));
+    case EBR_FLOAT64: return fn(static_cast<double*>(nullptr));
+    default: return set_error(EBR_ERR_DTYPE, "unknown dtype%s%s");
+  }
+}
+
+int check_rope_shape(int64_t B, int64_t N, int64_t H, int64_t D) {
+  if (B < 0 || N < 0 || H < 0) return set_error(EBR_ERR_SHAPE, "negative size%s%s");
+  if (D < 4 || D % 4 != 0 || D > 4096) return set_error(EBR_ERR_SHAPE, "head dim must be a multiple of 4 in [4, 4096]%s%s");
+  if (H > (1 << 20) || N > (int64_t{1} << 31) || B > (int64_t{1} << 31))
+    return set_error(EBR_ERR_SHAPE, "size too large%s%s");
+  return EBR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ebr_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const void* qkv, int64_t stride_b,
+                   int64_t stride_n, const float* cos_table, const float* sin_table, const float* qscale, void* q,
+                   void* k, void* v, void* stream) {
+  int rc = check_layer_dtype(dtype, true);
+  if (rc == EBR_OK) rc = check_rope_shape(B, N, H, D);
+  if (rc != EBR_OK) return rc;
+  if (B * N * H == 0) return EBR_OK;
+  if (!qkv || !cos_table || !sin_table || !q || !k || !v) return set_error(EBR_ERR_NULL, "rope_split: NULL pointer%s%s");
+  if (stride_b < 0 || stride_n < 0) return set_error(EBR_ERR_STRIDE, "rope_split: negative stride%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    const bool vec = (D / 4) % V == 0 && stride_b % V == 0 && stride_n % V == 0 &&
+                     all_aligned16({qkv, q, k, v});
+    const T* src = static_cast<const T*>(qkv);
+    if (vec) {
+      const int64_t total = B * N * 3 * H * (D / V);
+      ebr::layers::rope_split_kernel<T, V><<<flat_grid(device, total), kThreads, 0, st>>>(
+          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+          static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v));
+    } else {
+      const int64_t total = B * N * 3 * H * D;
+      ebr::layers::rope_split_kernel<T, 1><<<flat_grid(device, total), kThreads, 0, st>>>(
+          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+          static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v));
+    }
+    return check_launch("rope_split");
+  });
+}
+
+int ebr_rope_merge(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const ebr_operand* dq,
+                   const ebr_operand* dk, const ebr_operand* dv, const float* cos_table, const float* sin_table,
+                   const float* qscale, void* dqkv, void* stream) {
+  int rc = check_layer_dtype(dtype, true);
+  if (rc == EBR_OK) rc = check_rope_shape(B, N, H, D);
+  if (rc == EBR_OK) rc = check_operand(dq, "dq");
+  if (rc == EBR_OK) rc = check_operand(dk, "dk");
+  if (rc == EBR_OK) rc = check_operand(dv, "dv");
+  if (rc != EBR_OK) return rc;
+  if (B * N * H == 0) return EBR_OK;
+  if (!cos_table || !sin_table || !dqkv) return set_error(EBR_ERR_NULL, "rope_merge: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    bool vec = (D / 4) % V == 0 && aligned16(dqkv);
+    for (const ebr_operand* op : {dq, dk, dv})
+      vec = vec && aligned16(op->data) && op->stride_b % V == 0 && op->stride_h % V == 0 && op->stride_n % V == 0;
+    const int Vr = vec ? V : 1;
+    const int64_t total = B * N * 3 * H * (D / Vr);
+    if (vec)
+      ebr::layers::rope_merge_kernel<T, V><<<flat_grid(device, total), kThreads, 0, st>>>(
+          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+          static_cast<T*>(dqkv));
+    else
+      ebr::layers::rope_merge_kernel<T, 1><<<flat_grid(device, total), kThreads, 0, st>>>(
+          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+          static_cast<T*>(dqkv));
+    return check_launch("rope_merge");
+  });
+}
+
+int ebr_add_rms_norm(int dtype, int64_t rows, int64_t C, double eps, const void* x, const void* a, void* sum_out,
+                     void* y, float* rstd_out, const void* post, double post_scale, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || C < 1 || C > (1 << 20)) return set_error(EBR_ERR_SHAPE, "add_rms_norm: bad rows / row length%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!x || !y) return set_error(EBR_ERR_NULL, "add_rms_norm: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    const bool vec = C % V == 0 && all_aligned16({x, a, sum_out, y, post});
+    const dim3 grid = flat_grid(device, rows * 32);
+    if (vec)
+      ebr::layers::add_rms_norm_kernel<T, V><<<grid, kThreads, 0, st>>>(
+          rows, static_cast<int>(C), static_cast<float>(eps), static_cast<const T*>(x), static_cast<const T*>(a),
+          static_cast<T*>(sum_out), static_cast<T*>(y), rstd_out, static_cast<const T*>(post),
+          static_cast<float>(post_scale));
+    else
+      ebr::layers::add_rms_norm_kernel<T, 1><<<grid, kThreads, 0, st>>>(
+          rows, static_cast<int>(C), static_cast<float>(eps), static_cast<const T*>(x), static_cast<const T*>(a),
+          static_cast<T*>(sum_out), static_cast<T*>(y), rstd_out, static_cast<const T*>(post),
+          static_cast<float>(post_scale));
+    return check_launch("add_rms_norm");
+  });
+}
+
+int ebr_rms_norm_bwd(int dtype, int64_t rows, int64_t C, const void* s, const float* rstd, const void* gy, void* gs,
+                     void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || C < 1 || C > (1 << 20)) return set_error(EBR_ERR_SHAPE, "rms_norm_bwd: bad rows / row length%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!s || !rstd || !gy || !gs) return set_error(EBR_ERR_NULL, "rms_norm_bwd: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    const bool vec = C % V == 0 && all_aligned16({s, gy, gs});
+    const dim3 grid = flat_grid(device, rows * 32);
+    if (vec)
+      ebr::layers::rms_norm_bwd_kernel<T, V><<<grid, kThreads, 0, st>>>(
+          rows, static_cast<int>(C), static_cast<const T*>(s), rstd, static_cast<const T*>(gy), static_cast<T*>(gs));
+    else
+      ebr::layers::rms_norm_bwd_kernel<T, 1><<<grid, kThreads, 0, st>>>(
+          rows, static_cast<int>(C), static_cast<const T*>(s), rstd, static_cast<const T*>(gy), static_cast<T*>(gs));
+    return check_launch("rms_norm_bwd");
+  });
+}
+
+int ebr_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* h, void* out, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || I < 1) return set_error(EBR_ERR_SHAPE, "swiglu: bad rows / width%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!h || !out) return set_error(EBR_ERR_NULL, "swiglu: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    if (I % V == 0 && all_aligned16({h, out}))
+      ebr::layers::swiglu_fwd_kernel<T, V><<<flat_grid(device, rows * (I / V)), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<T*>(out));
+    else
+      ebr::layers::swiglu_fwd_kernel<T, 1><<<flat_grid(device, rows * I), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<T*>(out));
+    return check_launch("swiglu_fwd");
+  });
+}
+
+int ebr_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, void* gh, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || I < 1) return set_error(EBR_ERR_SHAPE, "swiglu_bwd: bad rows / width%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!h || !gout || !gh) return set_error(EBR_ERR_NULL, "swiglu_bwd: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    if (I % V == 0 && all_aligned16({h, gout, gh}))
+      ebr::layers::swiglu_bwd_kernel<T, V><<<flat_grid(device, rows * (I / V)), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<const T*>(gout), static_cast<T*>(gh));
+    else
+      ebr::layers::swiglu_bwd_kernel<T, 1><<<flat_grid(device, rows * I), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<const T*>(gout), static_cast<T*>(gh));
+    return check_launch("swiglu_bwd");
+  });
+}
+
+size_t ebr_descent_step_scratch_floats(int64_t rows, int64_t row_elems) {
+  if (rows <= 0 || row_elems <= 0) return 0;
+  const int64_t chunks = (row_elems + ebr::layers::kStepChunk - 1) / ebr::layers::kStepChunk;
+  return static_cast<size_t>(rows * chunks);
+}
+
+int ebr_descent_step(int dtype, int64_t rows, int64_t row_elems, double alpha, double eps, const void* v,
+                     const void* g, void* z_next, float* partial, size_t partial_floats, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || row_elems < 1 || rows > 65535) return set_error(EBR_ERR_SHAPE, "descent_step: bad rows / row length%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!v || !g || !z_next) return set_error(EBR_ERR_NULL, "descent_step: NULL pointer%s%s");
+  if (!partial || partial_floats < ebr_descent_step_scratch_floats(rows, row_elems))
+    return set_error(EBR_ERR_SCRATCH, "descent_step: partial-sum scratch missing or too small%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int chunks = static_cast<int>((row_elems + ebr::layers::kStepChunk - 1) / ebr::layers::kStepChunk);
+  const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(rows));
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    const bool vec = row_elems % V == 0 && all_aligned16({v, g, z_next});
+    if (vec) {
+      ebr::layers::descent_step_kernel<T, V><<<grid, kThreads, 0, st>>>(
+          row_elems, chunks, alpha, static_cast<const T*>(v), static_cast<const T*>(g), static_cast<T*>(z_next),
+          partial);
+      rc = check_launch("descent_step");
+      if (rc != EBR_OK) return rc;
+      ebr::layers::sphere_kernel<T, V><<<grid, kThreads, 0, st>>>(row_elems, chunks, static_cast<float>(eps),
+                                                                  static_cast<T*>(z_next), partial);
+    } else {
+      ebr::layers::descent_step_kernel<T, 1><<<grid, kThreads, 0, st>>>(
+          row_elems, chunks, alpha, static_cast<const T*>(v), static_cast<const T*>(g), static_cast<T*>(z_next),
+          partial);
+      rc = check_launch("descent_step");
+      if (rc != EBR_OK) return rc;
+      ebr::layers::sphere_kernel<T, 1><<<grid, kThreads, 0, st>>>(row_elems, chunks, static_cast<float>(eps),
+                                                                  static_cast<T*>(z_next), partial);
+    }
+    return check_launch("sphere");
+  });
+}
+
+}  // extern "C"

@@ -16,11 +16,19 @@ loops do:
 
 The attention is ``ebr_b200.fused_attn.fused_attention`` unless a caller injects another callable with the same
 signature (the CPU baseline of the benchmark injects the oracle there); there is no backend registry or fallback.
+
+``EnergyConfig.layers`` picks how the layers around the attention run: ``"fused"`` (CUDA: the kernels of
+``ebr_b200.layers`` -- the 2D-RoPE split / merge, residual + rms_norm, the SwiGLU activation, and the pointwise ops of
+inference microsteps) or ``"eager"`` (plain torch ops, the reference's ``rope_impl: eager`` code; the CPU model and
+the parity yardstick). As in the reference (``models/attention.py:215-242``), the per-head temperature is folded into
+the RoPE split only outside the graded window, where log_logit_scale needs no gradient.
 """
 
 from __future__ import annotations
 
+import contextlib
 import math
+import threading
 from dataclasses import dataclass
 from typing import Callable
 
@@ -28,6 +36,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from ebr_b200 import layers as fl
 from ebr_b200.fused_attn import fused_attention
 
 RMS_NORM_EPS = 1e-5
@@ -38,6 +47,25 @@ AttentionFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
 def _fused(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     return fused_attention(q, k, v, scale=q.shape[-1] ** -0.5)
+
+
+_window = threading.local()
+
+
+@contextlib.contextmanager
+def second_order_window(enabled: bool):
+    """Mark the energy evaluations inside as graded (their dE/dz is differentiated again), thread-locally
+    (``models/attention.py:22-37``)."""
+    prev = getattr(_window, "graded", False)
+    _window.graded = enabled
+    try:
+        yield
+    finally:
+        _window.graded = prev
+
+
+def second_order_required() -> bool:
+    return getattr(_window, "graded", False)
 
 
 # ------------------------------------------------------------------------------------------------------------ layers
@@ -89,14 +117,17 @@ class CastedEmbedding(nn.Module):
 
 
 class SwiGLU(nn.Module):
-    def __init__(self, hidden: int, expansion: float) -> None:
+    def __init__(self, hidden: int, expansion: float, fused: bool = False) -> None:
         super().__init__()
         inter = round(expansion * hidden * 2 / 3)
         inter = -(inter // -256) * 256
         self.gate_up = CastedLinear(hidden, 2 * inter, bias=False)
         self.down = CastedLinear(inter, hidden, bias=False)
+        self.fused = fused
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            return self.down(fl.swiglu_act(self.gate_up(x)))
         gate, up = self.gate_up(x).chunk(2, dim=-1)
         return self.down(F.silu(gate) * up)
 
@@ -122,6 +153,10 @@ class Rope2D(nn.Module):
         self.register_buffer("sin_h", rows.sin(), persistent=False)
         self.register_buffer("cos_w", cols.cos(), persistent=False)
         self.register_buffer("sin_w", cols.sin(), persistent=False)
+        # The same angles as [height * width, D] tables for the fused split (sign of rotate_half folded into sin).
+        cos_t, sin_t = fl.rotary_tables(self.cos_h, self.sin_h, self.cos_w, self.sin_w)
+        self.register_buffer("cos_table", cos_t, persistent=False)
+        self.register_buffer("sin_table", sin_t, persistent=False)
 
     def apply(self, q: torch.Tensor, k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """q, k: [B, N, heads, D] with N = height * width."""
@@ -143,33 +178,49 @@ class Rope2D(nn.Module):
 
 
 class EnergyAttention(nn.Module):
-    def __init__(self, hidden: int, heads: int, attention: AttentionFn | None = None) -> None:
+    def __init__(self, hidden: int, heads: int, attention: AttentionFn | None = None, fused: bool = False) -> None:
         super().__init__()
         self.heads, self.head_dim = heads, hidden // heads
         self.qkv = CastedLinear(hidden, 3 * hidden, bias=False)
         self.o = CastedLinear(hidden, hidden, bias=False)
         self.log_logit_scale = nn.Parameter(torch.zeros(heads))
         self.attention = attention or _fused
+        self.fused = fused
 
     def forward(self, rope: Rope2D, x: torch.Tensor) -> torch.Tensor:
         b, n, _ = x.shape
         h, d = self.heads, self.head_dim
-        q, k, v = self.qkv(x).split([h * d] * 3, dim=-1)
-        q, k, v = q.view(b, n, h, d), k.view(b, n, h, d), v.view(b, n, h, d)
-        q, k = rope.apply(q, k)
-        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-        q = q * self.log_logit_scale.exp().to(q.dtype).view(1, -1, 1, 1)
+        temperature_applied = False
+        if self.fused:
+            # One kernel: split + 2D RoPE + head-major layout (+ the temperature outside the graded window).
+            qscale = None
+            if not second_order_required():
+                qscale = self.log_logit_scale.detach().exp().to(x.dtype)
+                temperature_applied = True
+            q, k, v = fl.rope_split(self.qkv(x), rope.cos_table, rope.sin_table, h, qscale)
+        else:
+            q, k, v = self.qkv(x).split([h * d] * 3, dim=-1)
+            q, k, v = q.view(b, n, h, d), k.view(b, n, h, d), v.view(b, n, h, d)
+            q, k = rope.apply(q, k)
+            q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        if not temperature_applied:
+            q = q * self.log_logit_scale.exp().to(q.dtype).view(1, -1, 1, 1)
         y = self.attention(q, k, v)
         return self.o(y.transpose(1, 2).reshape(b, n, h * d))
 
 
 class Block(nn.Module):
-    def __init__(self, hidden: int, heads: int, expansion: float, attention: AttentionFn | None = None) -> None:
+    def __init__(self, hidden: int, heads: int, expansion: float, attention: AttentionFn | None = None,
+                 fused: bool = False) -> None:  # fmt: skip
         super().__init__()
-        self.attn = EnergyAttention(hidden, heads, attention)
-        self.mlp = SwiGLU(hidden, expansion)
+        self.attn = EnergyAttention(hidden, heads, attention, fused)
+        self.mlp = SwiGLU(hidden, expansion, fused)
+        self.fused = fused
 
     def forward(self, rope: Rope2D, x: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            x = fl.add_rms_norm(x, self.attn(rope, x), RMS_NORM_EPS)
+            return fl.add_rms_norm(x, self.mlp(x), RMS_NORM_EPS)
         x = rms_norm(x + self.attn(rope, x))
         return rms_norm(x + self.mlp(x))
 
@@ -178,9 +229,9 @@ class ScalarEnergy(nn.Module):
     """E(z, x): blocks over z + x, then the sum over cells of a per-cell scalar head. Returns [B] float32."""
 
     def __init__(self, hidden: int, heads: int, layers: int, expansion: float, softplus: bool,
-                 attention: AttentionFn | None = None) -> None:  # fmt: skip
+                 attention: AttentionFn | None = None, fused: bool = False) -> None:  # fmt: skip
         super().__init__()
-        self.blocks = nn.ModuleList(Block(hidden, heads, expansion, attention) for _ in range(layers))
+        self.blocks = nn.ModuleList(Block(hidden, heads, expansion, attention, fused) for _ in range(layers))
         self.head_hidden = CastedLinear(hidden, hidden, bias=True)
         self.head_out = CastedLinear(hidden, 1, bias=False)
         self.softplus = softplus
@@ -220,6 +271,7 @@ class EnergyConfig:
     step_size: float = 250.0
     noise_scale: float = 0.05
     init_std: float = 1.0
+    layers: str = "fused"  # "fused" (CUDA kernels around the attention) or "eager" (torch ops; CPU)
 
     @property
     def seq_len(self) -> int:
@@ -236,8 +288,11 @@ class EnergyReasoner(nn.Module):
         self.embed = CastedEmbedding(cfg.vocab_size, cfg.hidden_size, 1.0 / self.embed_scale, cfg.forward_dtype)
         self.lm_head = CastedLinear(cfg.hidden_size, cfg.vocab_size, bias=False)
         self.rope = Rope2D(cfg.hidden_size // cfg.num_heads, cfg.board_height, cfg.board_width)
+        if cfg.layers not in ("fused", "eager"):
+            raise ValueError(f"EnergyConfig.layers must be 'fused' or 'eager', got {cfg.layers!r}")
+        self.fused = cfg.layers == "fused"
         self.energy = ScalarEnergy(cfg.hidden_size, cfg.num_heads, cfg.num_layers, cfg.expansion, cfg.softplus,
-                                   attention)  # fmt: skip
+                                   attention, self.fused)  # fmt: skip
 
     def input_embeddings(self, tokens: torch.Tensor) -> torch.Tensor:
         return self.embed_scale * self.embed(tokens.to(torch.int32))
@@ -253,7 +308,7 @@ class EnergyReasoner(nn.Module):
 
     def energy_and_grad(self, v: torch.Tensor, x: torch.Tensor, create_graph: bool):
         """E(v, x) per row and dE/dv (``_energy_gradient``, ``models/energy.py:345-350``)."""
-        with torch.enable_grad():
+        with torch.enable_grad(), second_order_window(create_graph):
             if not v.requires_grad:
                 v = v.detach().requires_grad_(True)
             e = self.energy(v, x, self.rope)
@@ -264,14 +319,24 @@ class EnergyReasoner(nn.Module):
                   sigma: float | None = None, alpha: float | torch.Tensor | None = None):  # fmt: skip
         """One descent microstep from ``z``; returns (z_next, E(v) per row)."""
         cfg = self.cfg
-        v = rms_norm(z)
         sigma = cfg.noise_scale if sigma is None else sigma
+        step = cfg.step_size if alpha is None else alpha
+        if self.fused and not graded and not torch.is_tensor(step):
+            # Inference microstep: v = rms_norm(z) + noise and z' = sphere(v - alpha g) as fused kernels.
+            if noise is not None:
+                v = fl.noisy_point(z, noise, 1.0, RMS_NORM_EPS)
+            elif sigma:
+                v = fl.noisy_point(z, torch.randn_like(z), float(sigma), RMS_NORM_EPS)
+            else:
+                v = fl.noisy_point(z, None, 0.0, RMS_NORM_EPS)
+            e, g, v = self.energy_and_grad(v, x, create_graph=False)
+            return fl.step_and_project(v.detach(), g, float(step), RMS_NORM_EPS), e.detach()
+        v = rms_norm(z)
         if noise is not None:
             v = v + noise.to(v.dtype)
         elif sigma:
             v = v + torch.randn_like(v) * sigma
         e, g, v = self.energy_and_grad(v, x, create_graph=graded)
-        step = cfg.step_size if alpha is None else alpha
         z_next = sphere(v - step * g)
         return (z_next, e) if graded else (z_next.detach(), e.detach())
 

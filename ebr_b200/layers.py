@@ -1,0 +1,367 @@
+"""Fused kernels on either side of the attention in the energy network (``include/ebr_layers.h``).
+
+* 2D-RoPE split / merge: the reference's ``rope_impl: fused`` path (``models/fused_attn/rope_split.py``): custom ops
+  ``ebr_fused::rope_split(qkv, cos, sin, qscale, heads) -> (q, k, v)`` and
+  ``ebr_fused::rope_merge(dq, dk, dv, cos, sin, qscale) -> dqkv`` with the reference's schemas and fake kernels
+  (``rope_split.py:75-103``), the two autograd Functions that are each other's adjoint, so every derivative order is
+  exact (``:110-150``), and ``rope_split(qkv, cos, sin, heads, qscale=None)`` (``:161-178``). ``rotary_tables`` builds
+  the ``[H * W, D]`` cos / sign-folded sin tables of ``RotaryTable2D`` (``models/layers.py:143-172``).
+* ``add_rms_norm(x, a)``: rms_norm(x + a) of the post-norm block (``models/layers.py:37-42``), one kernel forward and
+  one backward.
+* ``swiglu_act(h)``: ``silu(gate) * up`` of ``SwiGLU`` (``models/layers.py:82-84``), one kernel each way.
+* ``noisy_point`` / ``step_and_project``: the pointwise ops of an inference microstep, ``v = rms_norm(z) + noise``
+  and ``z' = sphere(v - alpha g)`` (``models/energy.py:219-241``), one and two kernels.
+
+The row kernels' backwards run the fused kernel when no higher-order graph is being built; under ``create_graph``
+(graded microsteps) they evaluate the same formula with differentiable torch ops, so the double backward of training
+differentiates through them. Every op is CUDA-only: a CPU tensor is an error (the CPU model uses the eager layers).
+"""
+
+# No ``from __future__ import annotations``: custom_op schema inference needs real type objects.
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from ebr_b200 import _native
+
+Tensor = torch.Tensor
+
+_DTYPES = {
+    torch.float32: _native.FLOAT32,
+    torch.float16: _native.FLOAT16,
+    torch.bfloat16: _native.BFLOAT16,
+    torch.float64: _native.FLOAT64,
+}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(t: Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} runs only on CUDA (sm_100a) tensors, got device {t.device}; there is no CPU path")
+    if t.dtype not in _DTYPES:
+        raise TypeError(f"{what}: unsupported dtype {t.dtype}")
+
+
+def _ptr(t: Optional[Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------------------------------- 2D RoPE
+
+
+def quarter_swap(x: Tensor) -> Tensor:
+    """``(a, b, c, d) -> (b, a, d, c)`` over the quarters of the last dim (rotate_half of each half, without sign)."""
+    shape = x.shape
+    return x.reshape(*shape[:-1], 2, 2, shape[-1] // 4).flip(-2).reshape(shape)
+
+
+def rotary_tables(cos_h: Tensor, sin_h: Tensor, cos_w: Tensor, sin_w: Tensor) -> Tuple[Tensor, Tensor]:
+    """``[H * W, D]`` float32 tables from the per-row / per-column ``[H, D/2]`` / ``[W, D/2]`` RoPE tables: cell
+    ``i * W + j`` has row ``i``'s angles in the first half of D and column ``j``'s in the second, and the sign of
+    rotate_half is folded into sin, so ``t' = t * cos + quarter_swap(t) * sin`` (``models/layers.py:143-172``)."""
+    height, width, half = cos_h.shape[0], cos_w.shape[0], cos_h.shape[1]
+    dim = 2 * half
+    rows = torch.arange(height, device=cos_h.device).repeat_interleave(width)
+    cols = torch.arange(width, device=cos_h.device).repeat(height)
+    cos = torch.cat((cos_h[rows], cos_w[cols]), dim=-1)
+    sin = torch.cat((sin_h[rows], sin_w[cols]), dim=-1)
+    sign = torch.ones(dim, device=cos_h.device)
+    sign[: dim // 4] = -1.0
+    sign[dim // 2 : dim // 2 + dim // 4] = -1.0
+    return cos.to(torch.float32).contiguous(), (sin * sign).to(torch.float32).contiguous()
+
+
+def _qscale_arg(qscale: Tensor):
+    if qscale is None or qscale.numel() == 0:
+        return None, None
+    qs = qscale.detach().to(torch.float32).contiguous()
+    return qs, qs.data_ptr()
+
+
+def _table(t: Tensor, dev) -> Tensor:
+    return t.to(device=dev, dtype=torch.float32).contiguous()
+
+
+@torch.library.custom_op("ebr_fused::rope_split", mutates_args=())
+def rope_split_op(qkv: Tensor, cos: Tensor, sin: Tensor, qscale: Tensor, heads: int) -> Tuple[Tensor, Tensor, Tensor]:
+    _require_cuda(qkv, "rope_split")
+    b, n, c3 = qkv.shape
+    d = c3 // (3 * heads)
+    if qkv.stride(-1) != 1:
+        qkv = qkv.contiguous()
+    q, k, v = (torch.empty((b, heads, n, d), device=qkv.device, dtype=qkv.dtype) for _ in range(3))
+    cos, sin = _table(cos, qkv.device), _table(sin, qkv.device)
+    qs, qs_ptr = _qscale_arg(qscale)
+    _native.check(
+        _native.lib().ebr_rope_split(_DTYPES[qkv.dtype], b, n, heads, d, qkv.data_ptr(), qkv.stride(0), qkv.stride(1),
+                                     cos.data_ptr(), sin.data_ptr(), qs_ptr, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                     _stream()),  # fmt: skip
+        "rope_split",
+    )
+    return q, k, v
+
+
+@rope_split_op.register_fake
+def _(qkv, cos, sin, qscale, heads):
+    b, n, c3 = qkv.shape
+    d = c3 // (3 * heads)
+    return tuple(qkv.new_empty((b, heads, n, d)) for _ in range(3))
+
+
+@torch.library.custom_op("ebr_fused::rope_merge", mutates_args=())
+def rope_merge_op(dq: Tensor, dk: Tensor, dv: Tensor, cos: Tensor, sin: Tensor, qscale: Tensor) -> Tensor:
+    _require_cuda(dq, "rope_merge")
+    dk, dv = dk.to(dq.dtype), dv.to(dq.dtype)
+    dq, dk, dv = (t if t.stride(-1) == 1 else t.contiguous() for t in (dq, dk, dv))
+    b, h, n, d = dq.shape
+    out = torch.empty((b, n, 3 * h * d), device=dq.device, dtype=dq.dtype)
+    cos, sin = _table(cos, dq.device), _table(sin, dq.device)
+    qs, qs_ptr = _qscale_arg(qscale)
+    ops = [_native.Operand(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)) for t in (dq, dk, dv)]
+    r = ctypes.byref
+    _native.check(
+        _native.lib().ebr_rope_merge(_DTYPES[dq.dtype], b, n, h, d, r(ops[0]), r(ops[1]), r(ops[2]), cos.data_ptr(),
+                                     sin.data_ptr(), qs_ptr, out.data_ptr(), _stream()),  # fmt: skip
+        "rope_merge",
+    )
+    return out
+
+
+@rope_merge_op.register_fake
+def _(dq, dk, dv, cos, sin, qscale):
+    b, h, n, d = dq.shape
+    return dq.new_empty((b, n, 3 * h * d))
+
+
+class _Split(torch.autograd.Function):
+    """Forward: the split; backward: the merge (its exact adjoint). ``rope_split.py:110-131``."""
+
+    @staticmethod
+    def forward(qkv, cos, sin, qscale, heads):
+        return torch.ops.ebr_fused.rope_split(qkv, cos, sin, qscale, heads)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        qkv, cos, sin, qscale, heads = inputs
+        ctx.save_for_backward(cos, sin, qscale)
+        ctx.heads = heads
+        ctx.shape = tuple(output[0].shape)
+
+    @staticmethod
+    def backward(ctx, gq, gk, gv):
+        cos, sin, qscale = ctx.saved_tensors
+        ref = next(g for g in (gq, gk, gv) if g is not None)
+        z = None
+        if gq is None or gk is None or gv is None:
+            z = torch.zeros(ctx.shape, dtype=ref.dtype, device=ref.device)
+        gq, gk, gv = (z if g is None else g for g in (gq, gk, gv))
+        return _Merge.apply(gq, gk, gv, cos, sin, qscale), None, None, None, None
+
+
+class _Merge(torch.autograd.Function):
+    """Forward: the merge; backward: the split. ``rope_split.py:134-150``."""
+
+    @staticmethod
+    def forward(dq, dk, dv, cos, sin, qscale):
+        return torch.ops.ebr_fused.rope_merge(dq, dk, dv, cos, sin, qscale)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        dq, dk, dv, cos, sin, qscale = inputs
+        ctx.save_for_backward(cos, sin, qscale)
+        ctx.heads = int(dq.shape[1])
+
+    @staticmethod
+    def backward(ctx, g):
+        cos, sin, qscale = ctx.saved_tensors
+        gq, gk, gv = _Split.apply(g, cos, sin, qscale, ctx.heads)
+        return gq, gk, gv, None, None, None
+
+
+def _split(qkv: Tensor, cos: Tensor, sin: Tensor, qscale: Tensor, heads: int):
+    return _Split.apply(qkv, cos, sin, qscale, heads)
+
+
+_split = torch._dynamo.allow_in_graph(_split)
+
+
+def rope_split(qkv: Tensor, cos: Tensor, sin: Tensor, heads: int,
+               qscale: Optional[Tensor] = None) -> Tuple[Tensor, Tensor, Tensor]:  # fmt: skip
+    """``[B, N, 3*H*D]`` -> rotated ``q``, ``k`` and ``v``, each ``[B, H, N, D]``; differentiable to every order.
+
+    ``qscale`` (optional, ``[H]``, no gradient): per-head temperature already rounded to the I/O type, folded into q as
+    ``round(round(R q) * t)``; the adjoint scales first (``rope_split.py:161-178``)."""
+    if qkv.dim() != 3 or qkv.shape[-1] % (3 * heads):
+        raise ValueError(f"rope_split expects [B, N, 3*H*D], got {tuple(qkv.shape)} for {heads} heads")
+    d = qkv.shape[-1] // (3 * heads)
+    if d % 4 or tuple(cos.shape) != (qkv.shape[1], d) or tuple(sin.shape) != (qkv.shape[1], d):
+        raise ValueError(f"rope_split: tables must be [N, D] with D % 4 == 0, got {tuple(cos.shape)} (D={d})")
+    if qscale is None:
+        qscale = qkv.new_zeros((0,), dtype=torch.float32)
+    return _split(qkv, cos, sin, qscale.detach(), heads)
+
+
+# ---------------------------------------------------------------------------------------------------- rms_norm
+
+
+def _rows(x: Tensor) -> Tuple[int, int]:
+    c = x.shape[-1]
+    return x.numel() // c if c else 0, c
+
+
+def _rms_norm_bwd_graph(x: Tensor, a: Optional[Tensor], gy: Tensor, eps: float) -> Tensor:
+    """The backward of rms_norm(x + a) as differentiable torch ops (for create_graph)."""
+    s = x if a is None else x + a
+    xf = s.to(torch.float32)
+    r = torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
+    xh = xf * r
+    g = gy.to(torch.float32)
+    return (r * (g - xh * (g * xh).mean(-1, keepdim=True))).to(x.dtype)
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, a: Optional[Tensor], eps: float) -> Tensor:
+        _require_cuda(x, "add_rms_norm")
+        x = x.contiguous()
+        a = None if a is None else a.to(x.dtype).contiguous()
+        rows, c = _rows(x)
+        y = torch.empty_like(x)
+        s = torch.empty_like(x) if a is not None else None
+        rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+        _native.check(
+            _native.lib().ebr_add_rms_norm(_DTYPES[x.dtype], rows, c, eps, x.data_ptr(), _ptr(a), _ptr(s),
+                                           y.data_ptr(), rstd.data_ptr(), None, 0.0, _stream()),  # fmt: skip
+            "add_rms_norm",
+        )
+        ctx.save_for_backward(x, a, x if s is None else s, rstd)
+        ctx.eps = eps
+        ctx.has_a = a is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, gy: Tensor):
+        x, a, s, rstd = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            gs = _rms_norm_bwd_graph(x, a, gy, ctx.eps)
+        else:
+            gy = gy.to(x.dtype).contiguous()
+            rows, c = _rows(x)
+            gs = torch.empty_like(x)
+            _native.check(
+                _native.lib().ebr_rms_norm_bwd(_DTYPES[x.dtype], rows, c, s.data_ptr(), rstd.data_ptr(),
+                                               gy.data_ptr(), gs.data_ptr(), _stream()),  # fmt: skip
+                "rms_norm_bwd",
+            )
+        return gs, (gs if ctx.has_a else None), None
+
+
+def add_rms_norm(x: Tensor, a: Optional[Tensor] = None, eps: float = 1e-5) -> Tensor:
+    """``rms_norm(x + a)`` (``a`` optional): the residual add rounded to the I/O type, then the row norm in float32
+    (``models/layers.py:37-42``). Differentiable; the double backward goes through torch ops."""
+    return _AddRMSNorm.apply(x, a, float(eps))
+
+
+# ---------------------------------------------------------------------------------------------------- SwiGLU
+
+
+class _SwiGLUAct(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h: Tensor) -> Tensor:
+        _require_cuda(h, "swiglu")
+        h = h.contiguous()
+        rows, c2 = _rows(h)
+        inter = c2 // 2
+        out = torch.empty((*h.shape[:-1], inter), device=h.device, dtype=h.dtype)
+        _native.check(
+            _native.lib().ebr_swiglu_fwd(_DTYPES[h.dtype], rows, inter, h.data_ptr(), out.data_ptr(), _stream()),
+            "swiglu_fwd",
+        )
+        ctx.save_for_backward(h)
+        return out
+
+    @staticmethod
+    def backward(ctx, gout: Tensor):
+        (h,) = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            # Differentiable torch ops (aten's silu_backward has no derivative of its own).
+            gate, up = h.chunk(2, dim=-1)
+            gf = gate.to(torch.float32)
+            sg = torch.sigmoid(gf)
+            ga = (gout * up).to(torch.float32)
+            gg = (ga * sg * (1.0 + gf * (1.0 - sg))).to(h.dtype)
+            return torch.cat([gg, gout * F.silu(gate)], dim=-1)
+        gout = gout.to(h.dtype).contiguous()
+        rows, c2 = _rows(h)
+        gh = torch.empty_like(h)
+        _native.check(
+            _native.lib().ebr_swiglu_bwd(_DTYPES[h.dtype], rows, c2 // 2, h.data_ptr(), gout.data_ptr(),
+                                         gh.data_ptr(), _stream()),  # fmt: skip
+            "swiglu_bwd",
+        )
+        return gh
+
+
+def swiglu_act(h: Tensor) -> Tensor:
+    """``silu(gate) * up`` for ``gate, up = h.chunk(2, -1)`` (``models/layers.py:82-84``)."""
+    if h.shape[-1] % 2:
+        raise ValueError(f"swiglu_act expects an even last dim, got {h.shape[-1]}")
+    return _SwiGLUAct.apply(h)
+
+
+# ---------------------------------------------------------------------------------------------------- descent step
+
+
+@torch.no_grad()
+def noisy_point(z: Tensor, noise: Optional[Tensor] = None, sigma: float = 1.0, eps: float = 1e-5) -> Tensor:
+    """``v = rms_norm(z) + round(noise * sigma)`` in one kernel (no autograd: inference microsteps). With ``noise``
+    None, ``v = rms_norm(z)`` (``models/energy.py:226-232``, ``:322-341``)."""
+    _require_cuda(z, "noisy_point")
+    z = z.contiguous()
+    rows, c = _rows(z)
+    v = torch.empty_like(z)
+    noise = None if noise is None else noise.to(z.dtype).contiguous()
+    _native.check(
+        _native.lib().ebr_add_rms_norm(_DTYPES[z.dtype], rows, c, eps, z.data_ptr(), None, None, v.data_ptr(), None,
+                                       _ptr(noise), float(sigma), _stream()),  # fmt: skip
+        "noisy_point",
+    )
+    return v
+
+
+@torch.no_grad()
+def step_and_project(v: Tensor, g: Tensor, alpha: float, eps: float = 1e-5) -> Tensor:
+    """``z' = sphere(v - alpha * g)``: each row (board) of ``v`` rescaled to unit RMS in float32 after the step, in
+    two kernels (``models/energy.py:219-241``; no autograd: inference microsteps)."""
+    _require_cuda(v, "step_and_project")
+    v, g = v.contiguous(), g.to(v.dtype).contiguous()
+    rows = v.shape[0]
+    row_elems = v.numel() // rows if rows else 0
+    z = torch.empty_like(v)
+    lib = _native.lib()
+    nfl = lib.ebr_descent_step_scratch_floats(rows, row_elems)
+    partial = torch.empty(max(int(nfl), 1), device=v.device, dtype=torch.float32)
+    _native.check(
+        lib.ebr_descent_step(_DTYPES[v.dtype], rows, row_elems, float(alpha), float(eps), v.data_ptr(), g.data_ptr(),
+                             z.data_ptr(), partial.data_ptr(), partial.numel(), _stream()),  # fmt: skip
+        "descent_step",
+    )
+    return z
+
+
+__all__ = [
+    "add_rms_norm",
+    "noisy_point",
+    "quarter_swap",
+    "rope_merge_op",
+    "rope_split",
+    "rope_split_op",
+    "rotary_tables",
+    "step_and_project",
+    "swiglu_act",
+]

@@ -1,0 +1,77 @@
+/* ebr_layers.h: C ABI of the fused kernels on either side of the attention in the energy network E(z; x).
+ *
+ * These are the callers of the attention path: the 2D-RoPE split of the qkv projection into head-major q / k / v and
+ * its exact adjoint (the reference's ebr_fused::rope_split / rope_merge, models/fused_attn/rope_split.py:31-172), the
+ * post-norm residual + rms_norm and the SwiGLU activation of each block (models/layers.py:37-42, :74-84,
+ * models/attention.py post-norm block), and the pointwise ops of one descent microstep, v = rms_norm(z) + noise and
+ * z' = sphere(v - alpha dE/dv) (models/energy.py:219-241).
+ *
+ * Conventions (as include/ebr_attn.h): device pointers, sizes in elements, the caller's stream as void*, nothing
+ * allocated, nothing trapped. Every function returns EBR_OK (0) or an ebr_status code; ebr_attn_last_error() holds
+ * the message. Arithmetic is in float32 (float64 for EBR_FLOAT64) with one rounding to the I/O type where the
+ * reference's eager code rounds, so the outputs match it bit for bit up to the order of the row sums.
+ */
+#ifndef EBR_LAYERS_H
+#define EBR_LAYERS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ebr_attn.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* q, k, v [B, H, N, D] (contiguous) from qkv [B, N, 3 H D] (token stride stride_n, batch stride stride_b, unit
+ * channel stride): t' = t * cos + quarter_swap(t) * sin for q and k in float32, rounded once; v copied. cos / sin:
+ * float32 [N, D] tables with the sign of rotate_half folded into sin (quarter_swap: (a, b, c, d) -> (b, a, d, c) over
+ * the quarters of D). qscale: NULL, or float32 [H] per-head temperature already rounded to the I/O type, applied as
+ * q = round(round(R q) * qscale[h]). D must be a multiple of 4.
+ * Replaces: ebr_fused::rope_split / rope_split_triton.rope_split (models/fused_attn/rope_split.py:77-82, ref_split
+ * :31-50). */
+int ebr_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const void* qkv, int64_t stride_b,
+                   int64_t stride_n, const float* cos_table, const float* sin_table, const float* qscale, void* q,
+                   void* k, void* v, void* stream);
+
+/* The adjoint: dqkv [B, N, 3 H D] (contiguous) from dq, dk, dv (strided [B, H, N, D] operands): dq is first scaled
+ * by qscale (if not NULL) and rounded, then g' = g * cos + quarter_swap(g * sin) for dq and dk, rounded once; dv
+ * copied. Replaces: ebr_fused::rope_merge (models/fused_attn/rope_split.py:91-96, ref_merge :53-67). */
+int ebr_rope_merge(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const ebr_operand* dq,
+                   const ebr_operand* dk, const ebr_operand* dv, const float* cos_table, const float* sin_table,
+                   const float* qscale, void* dqkv, void* stream);
+
+/* Residual + rms_norm over rows of C contiguous elements:
+ *   s = round(x + a)            (a may be NULL: s = x; sum_out may be NULL, else s is written there)
+ *   y = round(s * rsqrt(mean(s^2) + eps)),  rstd_out[row] = rsqrt(mean(s^2) + eps) (float32; may be NULL)
+ *   if post != NULL: y = round(y + round(post * post_scale))   (the descent point v = rms_norm(z) + noise * sigma)
+ * Replaces: rms_norm(x + sublayer(x)) of the post-norm block and the descent state normalisation
+ * (models/layers.py:37-42; models/energy.py:226-232, :322-341). */
+int ebr_add_rms_norm(int dtype, int64_t rows, int64_t C, double eps, const void* x, const void* a, void* sum_out,
+                     void* y, float* rstd_out, const void* post, double post_scale, void* stream);
+
+/* Backward of ebr_add_rms_norm (without post): gs = round(rstd * (gy - xh * mean(gy * xh))), xh = s * rstd; gs is
+ * the gradient of both x and a. */
+int ebr_rms_norm_bwd(int dtype, int64_t rows, int64_t C, const void* s, const float* rstd, const void* gy, void* gs,
+                     void* stream);
+
+/* SwiGLU activation over rows of 2 I: out[r, j] = round(round(silu(h[r, j])) * h[r, I + j]), out [rows, I].
+ * Replaces: F.silu(gate) * up after gate_up_proj(x).chunk(2) (models/layers.py:82-84). */
+int ebr_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* h, void* out, void* stream);
+
+/* Its backward: gh [rows, 2 I] = (silu'(gate) * round(gout * up), round(gout * round(silu(gate)))). */
+int ebr_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, void* gh, void* stream);
+
+/* One descent step and projection, z' = sphere(v - alpha * g) over rows of `row_elems` elements (a whole board:
+ * N * C): u = round(v - round(alpha * g)), z' = round(u / max(sqrt(mean(u^2)), eps)). `partial` is float32 scratch
+ * of ebr_descent_step_scratch_floats(rows, row_elems) elements (the caller allocates it). Replaces: _step_and_project
+ * and sphere (models/energy.py:219-241). */
+int ebr_descent_step(int dtype, int64_t rows, int64_t row_elems, double alpha, double eps, const void* v,
+                     const void* g, void* z_next, float* partial, size_t partial_floats, void* stream);
+size_t ebr_descent_step_scratch_floats(int64_t rows, int64_t row_elems);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EBR_LAYERS_H */

@@ -13,6 +13,7 @@ from ebr_b200 import _native
 from ebr_b200.build import OUT, build
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "ebr_attn.h"
+LAYERS_HEADER = HEADER.with_name("ebr_layers.h")
 
 
 @pytest.fixture(scope="module")
@@ -21,9 +22,9 @@ def lib():
     return _native.lib()
 
 
-def declared_functions() -> list[str]:
-    text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*|uint64_t)\s+(ebr_attn_\w+)\s*\(", text, re.M)))
+def declared_functions(header: Path = HEADER) -> list[str]:
+    text = header.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*|uint64_t)\s+(ebr_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_reference_entry_points():
@@ -35,8 +36,32 @@ def test_header_declares_the_reference_entry_points():
 
 def test_library_exports_every_declared_symbol(lib):
     assert OUT.exists()
-    for name in declared_functions():
+    for name in declared_functions() + declared_functions(LAYERS_HEADER):
         assert hasattr(lib, name), name
+    assert set(_native.EXPORTED_LAYERS) == set(declared_functions(LAYERS_HEADER))
+
+
+def test_layer_entry_points_reject_bad_arguments_before_device(lib):
+    r = ctypes.byref
+    op = _op()
+    t = 0x1000
+    # RoPE: head dim not a multiple of 4, unknown dtype, NULL tables
+    assert lib.ebr_rope_split(_native.BFLOAT16, 1, 4, 2, 6, t, 0, 36, t, t, None, t, t, t, None) == _native.ERR_SHAPE
+    assert lib.ebr_rope_split(9, 1, 4, 2, 8, t, 0, 48, t, t, None, t, t, t, None) == _native.ERR_DTYPE
+    assert lib.ebr_rope_split(_native.BFLOAT16, 1, 4, 2, 8, t, 0, 48, None, t, None, t, t, t, None) == _native.ERR_NULL
+    assert lib.ebr_rope_merge(_native.BFLOAT16, 1, 4, 2, 8, None, r(op), r(op), t, t, None, t, None) == _native.ERR_NULL
+    # row kernels: float64 is not a layer dtype; bad row length; NULL output
+    assert lib.ebr_add_rms_norm(_native.FLOAT64, 4, 8, 1e-5, t, None, None, t, None, None, 0.0, None) == _native.ERR_DTYPE
+    assert lib.ebr_add_rms_norm(_native.BFLOAT16, 4, 0, 1e-5, t, None, None, t, None, None, 0.0, None) == _native.ERR_SHAPE
+    assert lib.ebr_swiglu_fwd(_native.BFLOAT16, 4, 8, t, None, None) == _native.ERR_NULL
+    assert lib.ebr_rms_norm_bwd(_native.BFLOAT16, 4, 8, t, None, t, t, None) == _native.ERR_NULL
+    # descent step: scratch too small
+    need = lib.ebr_descent_step_scratch_floats(4, 460800)
+    assert need == 4 * ((460800 + 8191) // 8192)
+    assert lib.ebr_descent_step(_native.BFLOAT16, 4, 460800, 1.0, 1e-5, t, t, t, t, need - 1, None) == _native.ERR_SCRATCH
+    # empty problems are no-ops
+    assert lib.ebr_rope_split(_native.BFLOAT16, 0, 4, 2, 8, None, 0, 48, None, None, None, None, None, None, None) == 0
+    assert lib.ebr_add_rms_norm(_native.BFLOAT16, 0, 8, 1e-5, None, None, None, None, None, None, 0.0, None) == 0
 
 
 def _op(ptr=0x1000, sb=0, sh=0, sn=64):

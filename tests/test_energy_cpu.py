@@ -19,7 +19,7 @@ def math_attention(q, k, v):
 def _model(attention, dtype=torch.float64):
     torch.manual_seed(3)
     cfg = EnergyConfig(board_height=3, board_width=4, vocab_size=6, hidden_size=32, num_heads=2, num_layers=2,
-                       forward_dtype=dtype)  # fmt: skip
+                       forward_dtype=dtype, layers="eager")  # fmt: skip
     return EnergyReasoner(cfg, attention=attention).to(dtype)
 
 

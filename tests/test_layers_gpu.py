@@ -1,0 +1,324 @@
+"""The fused kernels around the attention (include/ebr_layers.h) on the B200, against the reference's eager code:
+
+* 2D-RoPE split / merge: bit-exact against the reference's dense ``ref_split`` / ``ref_merge`` restated in torch
+  (models/fused_attn/rope_split.py:31-67) and against the eager split + apply_rope + transpose path
+  (models/layers.py:115-131), in bf16 / fp16 / fp32 / fp64, with and without the per-head temperature, contiguous and
+  strided qkv; the merge is the split's adjoint (<split(x), y> = <x, merge(y)>) and autograd passes gradcheck and
+  gradgradcheck in float64;
+* residual + rms_norm, SwiGLU activation, the descent point and step: equal to the eager ops up to the order of the
+  row sums (at most one unit in the last place of the I/O type, on a small fraction of elements), first derivatives
+  within 1e-2 max-rel of float64 autograd, second derivatives (create_graph) matching the eager ops' own;
+* the energy network with fused layers against the same network with eager layers: dE/dz within the network's bf16
+  noise floor (the deviation that swapping fp32 for fp64 inside the attention already causes).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+DTYPES = [torch.bfloat16, torch.float16, torch.float32, torch.float64]
+
+
+def _tables(h=9, w=9, d=64):
+    from ebr_b200.energy import Rope2D
+
+    rope = Rope2D(d, h, w).to(DEV)
+    return rope, rope.cos_table, rope.sin_table
+
+
+def quarter_swap(x):
+    shape = x.shape
+    return x.reshape(*shape[:-1], 2, 2, shape[-1] // 4).flip(-2).reshape(shape)
+
+
+def ref_split(qkv, cos, sin, heads, qscale=None):
+    """The reference's dense split (models/fused_attn/rope_split.py:31-50), restated."""
+    b, n, c3 = qkv.shape
+    d = c3 // (3 * heads)
+    ct = torch.float64 if qkv.dtype == torch.float64 else torch.float32
+    x = qkv.view(b, n, 3, heads, d)
+    c, s = cos.to(ct)[None, :, None, :], sin.to(ct)[None, :, None, :]
+
+    def rot(t):
+        t = t.to(ct)
+        return (t * c + quarter_swap(t) * s).to(qkv.dtype)
+
+    q, k, v = rot(x[:, :, 0]), rot(x[:, :, 1]), x[:, :, 2]
+    if qscale is not None:
+        q = (q.to(ct) * qscale.to(ct).view(1, 1, -1, 1)).to(qkv.dtype)
+    return q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(), v.transpose(1, 2).contiguous()
+
+
+def ref_merge(dq, dk, dv, cos, sin, qscale=None):
+    """The reference's dense merge (models/fused_attn/rope_split.py:53-67), restated."""
+    b, h, n, d = dq.shape
+    ct = torch.float64 if dq.dtype == torch.float64 else torch.float32
+    c, s = cos.to(ct)[None, None], sin.to(ct)[None, None]
+
+    def adj(g):
+        g = g.to(ct)
+        return (g * c + quarter_swap(g * s)).to(dq.dtype)
+
+    if qscale is not None:
+        dq = (dq.to(ct) * qscale.to(ct).view(1, -1, 1, 1)).to(dq.dtype)
+    out = torch.stack([adj(dq), adj(dk), dv.to(dq.dtype)], dim=2)
+    return out.permute(0, 3, 2, 1, 4).reshape(b, n, 3 * h * d)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("with_scale", [False, True])
+def test_rope_split_and_merge_bit_exact(dtype, with_scale):
+    from ebr_b200.layers import rope_merge_op, rope_split_op
+
+    rope, cos, sin = _tables()
+    g = torch.Generator(device="cpu").manual_seed(3)
+    b, n, h, d = 3, 81, 8, 64
+    qkv = torch.randn(b, n, 3 * h * d, generator=g).to(DEV, dtype)
+    qs = (torch.rand(h, generator=g) + 0.5).to(dtype).to(DEV) if with_scale else None
+    empty = torch.zeros(0, device=DEV)
+    got = rope_split_op(qkv, cos, sin, qs if with_scale else empty, h)
+    for a, r in zip(got, ref_split(qkv, cos, sin, h, qs)):
+        assert torch.equal(a, r)
+    dq, dk, dv = (torch.randn(b, h, n, d, generator=g).to(DEV, dtype) for _ in range(3))
+    out = rope_merge_op(dq, dk, dv, cos, sin, qs if with_scale else empty)
+    assert torch.equal(out, ref_merge(dq, dk, dv, cos, sin, qs))
+
+
+def test_rope_split_matches_the_eager_apply_rope_path():
+    """The [N, D] tables with folded signs give exactly the eager split + apply_rope + transpose (+ temperature)."""
+    from ebr_b200.layers import rope_split
+
+    rope, cos, sin = _tables()
+    g = torch.Generator(device="cpu").manual_seed(4)
+    b, n, h, d = 2, 81, 8, 64
+    qkv = torch.randn(b, n, 3 * h * d, generator=g).to(DEV, torch.bfloat16)
+    temp = (torch.randn(h, generator=g) * 0.1).to(DEV).exp().to(torch.bfloat16)
+    q, k, v = qkv.split([h * d] * 3, dim=-1)
+    q, k = rope.apply(q.reshape(b, n, h, d), k.reshape(b, n, h, d))
+    q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.reshape(b, n, h, d).transpose(1, 2)
+    q = q * temp.view(1, -1, 1, 1)
+    fq, fk, fv = rope_split(qkv, cos, sin, h, temp)
+    assert torch.equal(fq, q) and torch.equal(fk, k) and torch.equal(fv, v)
+
+
+def test_rope_strided_qkv_and_odd_head_dim():
+    from ebr_b200.layers import rope_merge_op, rope_split_op
+
+    g = torch.Generator(device="cpu").manual_seed(5)
+    for d in (64, 20):  # vector path; D % 32 != 0 takes the one-element path
+        rope, cos, sin = _tables(3, 5, d)
+        b, n, h = 2, 15, 3
+        big = torch.randn(b, n, 3 * h * d + 8, generator=g).to(DEV, torch.bfloat16)
+        qkv = big[..., : 3 * h * d]  # token stride 3 h d + 8
+        empty = torch.zeros(0, device=DEV)
+        for a, r in zip(rope_split_op(qkv, cos, sin, empty, h), ref_split(qkv.contiguous(), cos, sin, h)):
+            assert torch.equal(a, r)
+        dq = torch.randn(b, n, h, d, generator=g).to(DEV, torch.bfloat16).transpose(1, 2)  # strided [B, H, N, D]
+        dk, dv = dq.contiguous(), dq * 2
+        assert torch.equal(rope_merge_op(dq, dk, dv, cos, sin, empty), ref_merge(dq, dk, dv, cos, sin))
+
+
+def test_rope_merge_is_the_adjoint_and_autograd_is_exact():
+    from ebr_b200.layers import rope_merge_op, rope_split, rope_split_op
+
+    rope, cos, sin = _tables(3, 4, 16)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    b, n, h, d = 2, 12, 2, 16
+    qkv = torch.randn(b, n, 3 * h * d, generator=g, dtype=torch.float64).to(DEV)
+    ys = [torch.randn(b, h, n, d, generator=g, dtype=torch.float64).to(DEV) for _ in range(3)]
+    empty = torch.zeros(0, device=DEV)
+    lhs = sum((a * y).sum() for a, y in zip(rope_split_op(qkv, cos, sin, empty, h), ys))
+    rhs = (qkv * rope_merge_op(*ys, cos, sin, empty)).sum()
+    assert abs(float(lhs - rhs)) <= 1e-10 * abs(float(lhs))
+    x = qkv.clone().requires_grad_(True)
+    fn = lambda t: rope_split(t, cos, sin, h)
+    assert torch.autograd.gradcheck(fn, (x,), eps=1e-6, atol=1e-8)
+    assert torch.autograd.gradgradcheck(fn, (x,), eps=1e-6, atol=1e-8)
+
+
+def _check_rounding(a, r):
+    """16-bit outputs: at most one ulp apart on under 2% of the elements (a row sum in another order can move a
+    rounding); float32: a few ulps (no final rounding hides the sum-order difference)."""
+    ulps, frac = _ulp_diff(a, r)
+    if a.dtype in (torch.bfloat16, torch.float16):
+        assert ulps <= 1.0 and frac < 0.02, (ulps, frac)
+    else:
+        assert ulps <= 8.0, ulps
+
+
+def _ulp_diff(a, r):
+    """Largest difference in units of the I/O type's last place, and the fraction of unequal elements."""
+    eps = torch.finfo(a.dtype).eps
+    diff = (a.double() - r.double()).abs()
+    scale = r.double().abs().clamp_min(torch.finfo(a.dtype).tiny)
+    return float((diff / (scale * eps)).max()), float((a != r).double().mean())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_add_rms_norm_forward_and_backward(dtype):
+    from ebr_b200.energy import rms_norm
+    from ebr_b200.layers import add_rms_norm
+
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(4, 81, 512, generator=g).to(DEV, dtype)
+    a = torch.randn(4, 81, 512, generator=g).to(DEV, dtype)
+    gy = torch.randn(4, 81, 512, generator=g).to(DEV, dtype)
+    y = add_rms_norm(x, a)
+    _check_rounding(y, rms_norm(x + a))
+    # first derivative against float64 autograd of the same function on the rounded sum
+    xr, ar = x.clone().requires_grad_(True), a.clone().requires_grad_(True)
+    (gx, ga) = torch.autograd.grad(add_rms_norm(xr, ar), (xr, ar), gy)
+    s64 = (x + a).double().requires_grad_(True)
+    (g64,) = torch.autograd.grad(s64 * torch.rsqrt(s64.square().mean(-1, keepdim=True) + 1e-5), s64, gy.double())
+    rel = float((gx.double() - g64).abs().max() / g64.abs().max())
+    assert rel < 1e-2 and torch.equal(gx, ga), rel
+
+
+def test_add_rms_norm_second_order_matches_eager():
+    """Under create_graph the backward is built from torch ops: d/dx <dy/dx gy, u> equals the eager ops' own."""
+    from ebr_b200.energy import rms_norm
+    from ebr_b200.layers import add_rms_norm
+
+    g = torch.Generator(device="cpu").manual_seed(8)
+    x0 = torch.randn(3, 17, 256, generator=g).to(DEV)
+    a0 = torch.randn(3, 17, 256, generator=g).to(DEV)
+    gy, u = (torch.randn(3, 17, 256, generator=g).to(DEV) for _ in range(2))
+
+    def hvp(fn):
+        x, a = x0.clone().requires_grad_(True), a0.clone().requires_grad_(True)
+        (gx,) = torch.autograd.grad(fn(x, a), x, gy, create_graph=True)
+        return torch.autograd.grad((gx * u).sum(), (x, a))
+
+    for f, r in zip(hvp(add_rms_norm), hvp(lambda x, a: rms_norm(x + a))):
+        assert float((f - r).abs().max() / r.abs().max()) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swiglu_forward_backward_and_second_order(dtype):
+    from ebr_b200.layers import swiglu_act
+
+    g = torch.Generator(device="cpu").manual_seed(9)
+    h = (torch.randn(5, 81, 2 * 1536, generator=g) * 2).to(DEV, dtype)
+    go = torch.randn(5, 81, 1536, generator=g).to(DEV, dtype)
+    eager = lambda t: F.silu(t.chunk(2, -1)[0]) * t.chunk(2, -1)[1]
+    _check_rounding(swiglu_act(h), eager(h))
+    hf, he = h.clone().requires_grad_(True), h.clone().requires_grad_(True)
+    (gf,) = torch.autograd.grad(swiglu_act(hf), hf, go)
+    (ge,) = torch.autograd.grad(eager(he), he, go)
+    assert float((gf.double() - ge.double()).abs().max() / ge.double().abs().max()) < 1e-2
+    # create_graph: second derivative equals the eager ops'
+    u = torch.randn_like(h)
+    out = []
+    for fn in (swiglu_act, eager):
+        t = h.float().clone().requires_grad_(True)
+        (gt,) = torch.autograd.grad(fn(t), t, go.float(), create_graph=True)
+        out.append(torch.autograd.grad((gt * u.float()).sum(), t)[0])
+    assert float((out[0] - out[1]).abs().max() / out[1].abs().max()) < 1e-5
+
+
+def test_descent_point_and_step_match_eager():
+    from ebr_b200.energy import rms_norm, sphere
+    from ebr_b200.layers import noisy_point, step_and_project
+
+    g = torch.Generator(device="cpu").manual_seed(10)
+    z = torch.randn(6, 900, 512, generator=g).to(DEV, torch.bfloat16)
+    noise = torch.randn(6, 900, 512, generator=g).to(DEV, torch.bfloat16)
+    ulps, frac = _ulp_diff(noisy_point(z, noise, 0.05), rms_norm(z) + noise * 0.05)
+    assert ulps <= 1.0 and frac < 0.02, (ulps, frac)
+    ulps, frac = _ulp_diff(noisy_point(z, None, 0.0), rms_norm(z))
+    assert ulps <= 1.0 and frac < 0.02, (ulps, frac)
+    v = rms_norm(z)
+    grad = torch.randn(6, 900, 512, generator=g).to(DEV, torch.bfloat16) * 1e-3
+    ulps, frac = _ulp_diff(step_and_project(v, grad, 250.0), sphere(v - 250.0 * grad))
+    assert ulps <= 1.0 and frac < 0.02, (ulps, frac)
+
+
+def test_energy_network_fused_layers_within_noise_floor():
+    """dE/dz and one inference microstep of the cfg2 network with fused layers vs eager layers (same fused
+    attention): within 1.25x the deviation that fp32 -> fp64 inside the attention causes, plus 2e-3."""
+    from ebr_b200.energy import EnergyConfig, EnergyReasoner, rms_norm
+
+    def make(layers, attention=None):
+        torch.manual_seed(0)
+        cfg = EnergyConfig(board_height=9, board_width=9, vocab_size=10, layers=layers)
+        return EnergyReasoner(cfg, attention=attention).to(DEV)
+
+    def math64(q, k, v):
+        s = torch.matmul(q.double(), k.double().transpose(-1, -2)) * q.shape[-1] ** -0.5
+        return torch.matmul(s.softmax(-1), v.double()).to(q.dtype)
+
+    def math32(q, k, v):
+        s = torch.matmul(q.float(), k.float().transpose(-1, -2)) * q.shape[-1] ** -0.5
+        return torch.matmul(s.softmax(-1), v.float()).to(q.dtype)
+
+    fused, eager = make("fused"), make("eager")
+    m32, m64 = make("eager", math32), make("eager", math64)
+    for m in (eager, m32, m64):
+        m.load_state_dict(fused.state_dict())
+    g = torch.Generator().manual_seed(1)
+    tok = torch.randint(0, 10, (32, 81), generator=g).to(DEV)
+    x = fused.input_embeddings(tok)
+    z = fused.fresh_states(32, DEV)
+    v = rms_norm(z)
+    gf, ge, g32, g64 = (m.energy_and_grad(v, x, create_graph=False)[1] for m in (fused, eager, m32, m64))
+    rel = lambda a, r: float((a.float() - r.float()).norm() / r.float().norm())
+    floor = rel(g32, g64)
+    assert rel(gf, ge) <= 1.25 * floor + 2e-3, (rel(gf, ge), floor)
+    zf, _ = fused.microstep(z, x, graded=False, sigma=0.0)
+    ze, _ = eager.microstep(z, x, graded=False, sigma=0.0)
+    z32, _ = m32.microstep(z, x, graded=False, sigma=0.0)
+    z64, _ = m64.microstep(z, x, graded=False, sigma=0.0)
+    assert rel(zf, ze) <= 1.25 * rel(z32, z64) + 2e-3, (rel(zf, ze), rel(z32, z64))
+
+
+def test_training_segment_with_fused_layers():
+    """One graded microstep (create_graph, so the double backward runs through the fused layers' graph backwards)
+    and the decode loss: finite parameter gradients, and their deviation from the eager-layer model's (same fused
+    attention) within the network's noise floor, taken as the deviation between fp32 and fp64 math attention in
+    the eager-layer model (norm-rel, times 1.25, plus 2e-3), or 2e-2."""
+    from ebr_b200.energy import EnergyConfig, EnergyReasoner, train_step_loss
+
+    def math(dt):
+        def fn(q, k, v):
+            s = torch.matmul(q.to(dt), k.to(dt).transpose(-1, -2)) * q.shape[-1] ** -0.5
+            return torch.matmul(s.softmax(-1), v.to(dt)).to(q.dtype)
+
+        return fn
+
+    def make(layers, attention=None):
+        torch.manual_seed(0)
+        cfg = EnergyConfig(board_height=9, board_width=9, vocab_size=10, layers=layers)
+        return EnergyReasoner(cfg, attention=attention).to(DEV)
+
+    models = [make("fused"), make("eager"), make("eager", math(torch.float32)), make("eager", math(torch.float64))]
+    for m in models[1:]:
+        m.load_state_dict(models[0].state_dict())
+    g = torch.Generator().manual_seed(2)
+    tok = torch.randint(0, 10, (8, 81), generator=g).to(DEV)
+    labels = torch.randint(0, 10, (8, 81), generator=g).to(DEV)
+    grads = []
+    for m in models:
+        torch.manual_seed(5)
+        x = m.input_embeddings(tok)
+        z = m.fresh_states(8, DEV)
+        loss = train_step_loss(m, z, x, labels, prefix=0, graded=1)
+        grads.append(torch.autograd.grad(loss, list(m.parameters()), allow_unused=True))
+
+    def rel(ga, gb):
+        num = den = 0.0
+        for a, b in zip(ga, gb):
+            if a is None or b is None:
+                assert a is None and b is None
+                continue
+            assert torch.isfinite(a).all()
+            num += float((a.double() - b.double()).square().sum())
+            den += float(b.double().square().sum())
+        return (num / den) ** 0.5
+
+    ours, floor = rel(grads[0], grads[1]), rel(grads[2], grads[3])
+    assert ours <= max(2e-2, 1.25 * floor + 2e-3), (ours, floor)
