@@ -11,6 +11,7 @@
 #include "../../include/ebr_attn.h"
 #include "simt.cuh"
 #include "tc_attn.cuh"
+#include "tc_fwd.cuh"
 
 namespace {
 
@@ -224,6 +225,28 @@ int launch_tc_fwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, d
                                                                  static_cast<int>(H), static_cast<int>(N),
                                                                  static_cast<float>(scale));
   return check_launch("tc_fwd_pipe_kernel");
+}
+
+template <typename T, int D>
+int launch_tc_fwd_pair(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                       const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
+  using L = FwdPairLayout<D>;
+  CUtensorMap tq, tk, tv;  // Q in 128-row boxes, K / V in 64-row boxes (kKeyTile)
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D, kKeyTile) ||
+      make_tile_map(&tv, v, dtype, B, H, N, D, kKeyTile))
+    return kNoTensorMap;
+  const void* fn = reinterpret_cast<const void*>(tc_fwd_pair_kernel<T, D>);
+  int s = prepare_tc_kernel(fn, device, L::kSmem, L::kTmemCols, L::kThreads);
+  if (s) return s;
+  const int64_t n_qt = (N + kTile - 1) / kTile;
+  const int64_t items = B * H * ((n_qt + 1) / 2);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  tc_fwd_pair_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, static_cast<T*>(o),
+                                                                 static_cast<float*>(lse), static_cast<int>(B * H),
+                                                                 static_cast<int>(H), static_cast<int>(N),
+                                                                 static_cast<float>(scale));
+  return check_launch("tc_fwd_pair_kernel");
 }
 
 // ------------------------------------------------------------------------------------------------ backward
@@ -446,12 +469,23 @@ int ebr_attn_fwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double s
   if ((s = check_device(&device))) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (tc_eligible(dtype, D, {q, k, v}, B, H, N) && aligned16(o)) {
-    if (dtype == EBR_BFLOAT16)
-      s = D == 64 ? launch_tc_fwd_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                  : launch_tc_fwd_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
-    else
-      s = D == 64 ? launch_tc_fwd_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                  : launch_tc_fwd_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+    // N > 128: two query tiles per CTA in ping-pong; N <= 128 (one tile per slice): two CTAs per SM.
+    const bool pair = N > kTile;
+    if (dtype == EBR_BFLOAT16) {
+      if (pair)
+        s = D == 64 ? launch_tc_fwd_pair<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_pair<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+      else
+        s = D == 64 ? launch_tc_fwd_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+    } else {
+      if (pair)
+        s = D == 64 ? launch_tc_fwd_pair<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_pair<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+      else
+        s = D == 64 ? launch_tc_fwd_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+    }
     if (s != kNoTensorMap) return s;
   }
   switch (dtype) {

@@ -80,97 +80,145 @@ __device__ __forceinline__ int64_t global_tid() { return static_cast<int64_t>(bl
 // quarter_swap's source index for element d of a head row of D = 4 Q elements: (a, b, c, d) -> (b, a, d, c).
 __device__ __forceinline__ int swap_index(int d, int Q) { return ((d / Q) ^ 1) * Q + (d % Q); }
 
-// One thread per V-element chunk of one head row of one of q / k / v of one token; the chunk index runs fastest, then
-// the head, then q / k / v, then the token, so a warp reads a contiguous stretch of the qkv row. Chunks never straddle
-// a quarter (Q % V == 0), so a chunk's quarter_swap partner is the contiguous chunk at swap_index(d0).
-template <typename T, int V>
-__global__ void __launch_bounds__(kThreads) rope_split_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sn,
-                                                              int64_t N, int H, int D, int64_t total,
-                                                              const float* __restrict__ cos_t,
-                                                              const float* __restrict__ sin_t,
-                                                              const float* __restrict__ qscale, T* __restrict__ q,
-                                                              T* __restrict__ k, T* __restrict__ v) {
-  using C = typename Elem<T>::C;
-  const int cpr = D / V, Q = D / 4;
-  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
-    const int c = static_cast<int>(i % cpr);
-    int64_t r = i / cpr;
-    const int h = static_cast<int>(r % H);
-    r /= H;
-    const int part = static_cast<int>(r % 3);
-    const int64_t tok = r / 3;
-    const int64_t b = tok / N, n = tok - b * N;
-    const int d0 = c * V;
-    const T* row = qkv + b * sb + n * sn + static_cast<int64_t>(part * H + h) * D;
-    T* dst = (part == 0 ? q : part == 1 ? k : v) + ((b * H + h) * N + n) * D + d0;
-    C own[V];
-    load_c<T, V>(row + d0, own);
-    if (part == 2) {
-      store_c<T, V>(dst, own);
-      continue;
-    }
-    C partner[V];
-    float cs[V], sn_[V];
-    load_c<T, V>(row + swap_index(d0, Q), partner);
-    load_table<V>(cos_t + n * D + d0, cs);
-    load_table<V>(sin_t + n * D + d0, sn_);
-    C out[V];
+template <int V>
+__device__ __forceinline__ void load_table_v(const float* p, float (&out)[V]) {
+  if constexpr (V % 4 == 0) {
 #pragma unroll
-    for (int e = 0; e < V; ++e) {
-      out[e] = rnd<T>(add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sn_[e]))));
-      if (part == 0 && qscale) out[e] = mul_rn(out[e], static_cast<C>(__ldg(qscale + h)));
+    for (int i = 0; i < V; i += 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p + i));
+      out[i] = t.x;
+      out[i + 1] = t.y;
+      out[i + 2] = t.z;
+      out[i + 3] = t.w;
     }
-    store_c<T, V>(dst, out);
+  } else {
+    load_table<V>(p, out);
   }
 }
 
-// The adjoint, one thread per V-element chunk of the dqkv row (same index order, so the writes are contiguous):
-// g' = g * cos + quarter_swap(g * sin) for dq (after its qscale rounding) and dk; dv copied.
+// A token's qkv row is 3 H D / V "slots" of V elements (slot = (part * H + h) * (D / V) + chunk, part 0 / 1 / 2 for
+// q / k / v). A block is one token's slots wide (blockDim.x >= slots: each thread keeps one slot for every token it
+// visits) and walks tokens blockIdx.x, blockIdx.x + gridDim.x, ...; a warp reads a contiguous stretch of the row.
+// Chunks never straddle a quarter of D (Q % V == 0), so a chunk's quarter_swap partner is the contiguous chunk at
+// swap_index(d0). The tables are float32 [N, D] rows (16-byte aligned when D % 4 == 0).
+struct RopeSlot {
+  int part, h, d0;
+};
+
+__device__ __forceinline__ RopeSlot rope_slot(int slot, int H, int cpr, int V) {
+  const int c = slot % cpr, r = slot / cpr;
+  return RopeSlot{r / H, r % H, c * V};
+}
+
 template <typename T, int V>
-__global__ void __launch_bounds__(kThreads) rope_merge_kernel(ebr_operand dq, ebr_operand dk, ebr_operand dv,
-                                                              int64_t N, int H, int D, int64_t total,
-                                                              const float* __restrict__ cos_t,
-                                                              const float* __restrict__ sin_t,
-                                                              const float* __restrict__ qscale, T* __restrict__ out) {
+__device__ __forceinline__ void rope_split_one(const T* __restrict__ qkv, int64_t sb, int64_t sn, int64_t b,
+                                               int64_t n, int64_t N, int H, int D, RopeSlot sl,
+                                               const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                               const float* __restrict__ qscale, T* __restrict__ q,
+                                               T* __restrict__ k, T* __restrict__ v) {
   using C = typename Elem<T>::C;
-  const int cpr = D / V, Q = D / 4;
-  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
-    const int c = static_cast<int>(i % cpr);
-    int64_t r = i / cpr;
-    const int h = static_cast<int>(r % H);
-    r /= H;
-    const int part = static_cast<int>(r % 3);
-    const int64_t tok = r / 3;
-    const int64_t b = tok / N, n = tok - b * N;
-    const int d0 = c * V;
-    const ebr_operand& op = part == 0 ? dq : part == 1 ? dk : dv;
-    const T* row = static_cast<const T*>(op.data) + b * op.stride_b + h * op.stride_h + n * op.stride_n;
-    T* dst = out + tok * (3 * static_cast<int64_t>(H) * D) + static_cast<int64_t>(part * H + h) * D + d0;
-    C own[V];
-    load_c<T, V>(row + d0, own);
-    if (part == 2) {
-      store_c<T, V>(dst, own);
-      continue;
-    }
-    const int p0 = swap_index(d0, Q);
-    C partner[V];
-    float cs[V], sp[V];
-    load_c<T, V>(row + p0, partner);
-    load_table<V>(cos_t + n * D + d0, cs);
-    load_table<V>(sin_t + n * D + p0, sp);
-    if (part == 0 && qscale) {
-      const C s = static_cast<C>(__ldg(qscale + h));
+  const T* row = qkv + b * sb + n * sn + static_cast<int64_t>(sl.part * H + sl.h) * D;
+  T* dst = (sl.part == 0 ? q : sl.part == 1 ? k : v) + ((b * H + sl.h) * N + n) * D + sl.d0;
+  C own[V];
+  load_c<T, V>(row + sl.d0, own);
+  if (sl.part == 2) {
+    store_c<T, V>(dst, own);
+    return;
+  }
+  C partner[V];
+  float cs[V], sn_[V];
+  load_c<T, V>(row + swap_index(sl.d0, D / 4), partner);
+  load_table_v<V>(cos_t + n * D + sl.d0, cs);
+  load_table_v<V>(sin_t + n * D + sl.d0, sn_);
+  C out[V];
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        own[e] = rnd<T>(mul_rn(own[e], s));
-        partner[e] = rnd<T>(mul_rn(partner[e], s));
-      }
+  for (int e = 0; e < V; ++e) {
+    out[e] = rnd<T>(add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sn_[e]))));
+    if (sl.part == 0 && qscale) out[e] = mul_rn(out[e], static_cast<C>(__ldg(qscale + sl.h)));
+  }
+  store_c<T, V>(dst, out);
+}
+
+template <typename T, int V>
+__global__ void rope_split_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sn, int64_t N, int H, int D,
+                                  int64_t tokens, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                  const float* __restrict__ qscale, T* __restrict__ q, T* __restrict__ k,
+                                  T* __restrict__ v) {
+  const int cpr = D / V, slots = 3 * H * cpr;
+  if (static_cast<int>(blockDim.x) >= slots) {
+    if (static_cast<int>(threadIdx.x) >= slots) return;
+    const RopeSlot sl = rope_slot(threadIdx.x, H, cpr, V);
+    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+      const int64_t b = tok / N;
+      rope_split_one<T, V>(qkv, sb, sn, b, tok - b * N, N, H, D, sl, cos_t, sin_t, qscale, q, k, v);
     }
-    C res[V];
+  } else {
+    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+      const int64_t b = tok / N;
+      for (int s = threadIdx.x; s < slots; s += blockDim.x)
+        rope_split_one<T, V>(qkv, sb, sn, b, tok - b * N, N, H, D, rope_slot(s, H, cpr, V), cos_t, sin_t, qscale,
+                             q, k, v);
+    }
+  }
+}
+
+// The adjoint, same slots and token walk (so the dqkv writes are contiguous): g' = g * cos + quarter_swap(g * sin)
+// for dq (after its qscale rounding) and dk; dv copied.
+template <typename T, int V>
+__device__ __forceinline__ void rope_merge_one(const ebr_operand& dq, const ebr_operand& dk, const ebr_operand& dv,
+                                               int64_t tok, int64_t b, int64_t n, int H, int D, RopeSlot sl,
+                                               const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                               const float* __restrict__ qscale, T* __restrict__ out) {
+  using C = typename Elem<T>::C;
+  const ebr_operand& op = sl.part == 0 ? dq : sl.part == 1 ? dk : dv;
+  const T* row = static_cast<const T*>(op.data) + b * op.stride_b + sl.h * op.stride_h + n * op.stride_n;
+  T* dst = out + tok * (3 * static_cast<int64_t>(H) * D) + static_cast<int64_t>(sl.part * H + sl.h) * D + sl.d0;
+  C own[V];
+  load_c<T, V>(row + sl.d0, own);
+  if (sl.part == 2) {
+    store_c<T, V>(dst, own);
+    return;
+  }
+  const int p0 = swap_index(sl.d0, D / 4);
+  C partner[V];
+  float cs[V], sp[V];
+  load_c<T, V>(row + p0, partner);
+  load_table_v<V>(cos_t + n * D + sl.d0, cs);
+  load_table_v<V>(sin_t + n * D + p0, sp);
+  if (sl.part == 0 && qscale) {
+    const C s = static_cast<C>(__ldg(qscale + sl.h));
 #pragma unroll
-    for (int e = 0; e < V; ++e)
-      res[e] = add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sp[e])));
-    store_c<T, V>(dst, res);
+    for (int e = 0; e < V; ++e) {
+      own[e] = rnd<T>(mul_rn(own[e], s));
+      partner[e] = rnd<T>(mul_rn(partner[e], s));
+    }
+  }
+  C res[V];
+#pragma unroll
+  for (int e = 0; e < V; ++e)
+    res[e] = add_rn(mul_rn(own[e], static_cast<C>(cs[e])), mul_rn(partner[e], static_cast<C>(sp[e])));
+  store_c<T, V>(dst, res);
+}
+
+template <typename T, int V>
+__global__ void rope_merge_kernel(ebr_operand dq, ebr_operand dk, ebr_operand dv, int64_t N, int H, int D,
+                                  int64_t tokens, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                  const float* __restrict__ qscale, T* __restrict__ out) {
+  const int cpr = D / V, slots = 3 * H * cpr;
+  if (static_cast<int>(blockDim.x) >= slots) {
+    if (static_cast<int>(threadIdx.x) >= slots) return;
+    const RopeSlot sl = rope_slot(threadIdx.x, H, cpr, V);
+    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+      const int64_t b = tok / N;
+      rope_merge_one<T, V>(dq, dk, dv, tok, b, tok - b * N, H, D, sl, cos_t, sin_t, qscale, out);
+    }
+  } else {
+    for (int64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x) {
+      const int64_t b = tok / N;
+      for (int s = threadIdx.x; s < slots; s += blockDim.x)
+        rope_merge_one<T, V>(dq, dk, dv, tok, b, tok - b * N, H, D, rope_slot(s, H, cpr, V), cos_t, sin_t, qscale,
+                             out);
+    }
   }
 }
 

@@ -50,6 +50,19 @@ int with_type(int dtype, Fn&& fn) {
   }
 }
 
+// RoPE launch shape: one token's slots per block (rounded up to whole warps, at most 1024 threads; wider rows loop),
+// enough blocks to fill the SMs, each walking tokens with a stride of the grid.
+struct RopeGrid {
+  dim3 blocks, threads;
+};
+
+RopeGrid rope_grid(int device, int64_t slots, int64_t tokens) {
+  const int threads = static_cast<int>(std::min<int64_t>(1024, (slots + 31) / 32 * 32));
+  const int64_t per_sm = std::max<int64_t>(1, 2048 / threads);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(tokens, per_sm * sm_count(device) * 4));
+  return RopeGrid{dim3(static_cast<unsigned>(blocks)), dim3(static_cast<unsigned>(threads))};
+}
+
 int check_rope_shape(int64_t B, int64_t N, int64_t H, int64_t D) {
   if (B < 0 || N < 0 || H < 0) return set_error(EBR_ERR_SHAPE, "negative size%s%s");
   if (D < 4 || D % 4 != 0 || D > 4096) return set_error(EBR_ERR_SHAPE, "head dim must be a multiple of 4 in [4, 4096]%s%s");
@@ -78,17 +91,18 @@ int ebr_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const 
     using T = std::remove_pointer_t<decltype(tag)>;
     constexpr int V = vec_width<T>();
     const bool vec = (D / 4) % V == 0 && stride_b % V == 0 && stride_n % V == 0 &&
-                     all_aligned16({qkv, q, k, v});
+                     all_aligned16({qkv, q, k, v, cos_table, sin_table});
     const T* src = static_cast<const T*>(qkv);
+    const int64_t tokens = B * N;
     if (vec) {
-      const int64_t total = B * N * 3 * H * (D / V);
-      ebr::layers::rope_split_kernel<T, V><<<flat_grid(device, total), kThreads, 0, st>>>(
-          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+      const RopeGrid g = rope_grid(device, 3 * H * (D / V), tokens);
+      ebr::layers::rope_split_kernel<T, V><<<g.blocks, g.threads, 0, st>>>(
+          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), tokens, cos_table, sin_table, qscale,
           static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v));
     } else {
-      const int64_t total = B * N * 3 * H * D;
-      ebr::layers::rope_split_kernel<T, 1><<<flat_grid(device, total), kThreads, 0, st>>>(
-          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+      const RopeGrid g = rope_grid(device, 3 * H * D, tokens);
+      ebr::layers::rope_split_kernel<T, 1><<<g.blocks, g.threads, 0, st>>>(
+          src, stride_b, stride_n, N, static_cast<int>(H), static_cast<int>(D), tokens, cos_table, sin_table, qscale,
           static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v));
     }
     return check_launch("rope_split");
@@ -112,18 +126,19 @@ int ebr_rope_merge(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const 
   return with_type(dtype, [&](auto* tag) -> int {
     using T = std::remove_pointer_t<decltype(tag)>;
     constexpr int V = vec_width<T>();
-    bool vec = (D / 4) % V == 0 && aligned16(dqkv);
+    bool vec = (D / 4) % V == 0 && all_aligned16({dqkv, cos_table, sin_table});
     for (const ebr_operand* op : {dq, dk, dv})
       vec = vec && aligned16(op->data) && op->stride_b % V == 0 && op->stride_h % V == 0 && op->stride_n % V == 0;
     const int Vr = vec ? V : 1;
-    const int64_t total = B * N * 3 * H * (D / Vr);
+    const int64_t tokens = B * N;
+    const RopeGrid g = rope_grid(device, 3 * H * (D / Vr), tokens);
     if (vec)
-      ebr::layers::rope_merge_kernel<T, V><<<flat_grid(device, total), kThreads, 0, st>>>(
-          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+      ebr::layers::rope_merge_kernel<T, V><<<g.blocks, g.threads, 0, st>>>(
+          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), tokens, cos_table, sin_table, qscale,
           static_cast<T*>(dqkv));
     else
-      ebr::layers::rope_merge_kernel<T, 1><<<flat_grid(device, total), kThreads, 0, st>>>(
-          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), total, cos_table, sin_table, qscale,
+      ebr::layers::rope_merge_kernel<T, 1><<<g.blocks, g.threads, 0, st>>>(
+          *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), tokens, cos_table, sin_table, qscale,
           static_cast<T*>(dqkv));
     return check_launch("rope_merge");
   });
