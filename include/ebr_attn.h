@@ -21,8 +21,9 @@
  *   - A cotangent with data == NULL is zero (triton_kernels.py:868-873 expands a zero row instead).
  *
  * Ownership: the library never allocates device memory. The caller allocates outputs and the scratch buffer whose
- * size ebr_attn_*_scratch_bytes() reports (zero for most shapes), and passes a CUDA stream (cudaStream_t, NULL =
- * legacy default stream). Calls are asynchronous on that stream and reentrant.
+ * size ebr_attn_*_scratch_bytes() reports (the row scalars of the two-pass kernels: B * H * N fp32 values, fp64 for
+ * float64, three sets for the double backward), and passes a CUDA stream (cudaStream_t, NULL = legacy default
+ * stream). Calls are asynchronous on that stream and reentrant.
  *
  * Errors: every entry point returns EBR_OK or an ebr_status code and never traps. Argument errors are detected on the
  * host before any launch. Device-side waits are bounded; a wait that runs out sets a device error word that
