@@ -11,6 +11,7 @@
 #include "../../include/ebr_attn.h"
 #include "simt.cuh"
 #include "tc_attn.cuh"
+#include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
 
 namespace {
@@ -290,32 +291,33 @@ template <typename T, int D>
 int launch_tc_bwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
                        const ebr_operand* dout, void* dq, void* dk, void* dv, void* scratch, cudaStream_t st) {
-  using L = BwdPipeLayout<D>;
   CUtensorMap tq, tk, tv, tdo, tq64, tk64, tv64, tdo64;
   if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
       make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D) ||
       make_tile_map(&tq64, q, dtype, B, H, N, D, 64) || make_tile_map(&tk64, k, dtype, B, H, N, D, 64) ||
       make_tile_map(&tv64, v, dtype, B, H, N, D, 64) || make_tile_map(&tdo64, dout, dtype, B, H, N, D, 64))
     return kNoTensorMap;
-  const void* fq = reinterpret_cast<const void*>(tc_bwd_dq_pipe_kernel<T, D>);
-  const void* fk = reinterpret_cast<const void*>(tc_bwd_dkdv_pipe_kernel<T, D>);
-  int s = prepare_tc_kernel(fq, device, L::kSmem, 256, L::kThreads);
+  using LR = BwdRowLayout<D>;
+  using LC = BwdColLayout<D>;
+  const void* fq = reinterpret_cast<const void*>(tc_bwd_dq_split_kernel<T, D>);
+  const void* fk = reinterpret_cast<const void*>(tc_bwd_dkdv_split_kernel<T, D>);
+  int s = prepare_tc_kernel(fq, device, LR::kSmem, LR::kTmemCols, LR::kThreads);
   if (s) return s;
-  s = prepare_tc_kernel(fk, device, L::kSmem, D == 64 ? 256 : 512, L::kThreads);
+  s = prepare_tc_kernel(fk, device, LC::kSmem, LC::kTmemCols, LC::kThreads);
   if (s) return s;
-  const int64_t items = B * H * ((N + kTile - 1) / kTile);
-  const int64_t cap = static_cast<int64_t>(L::kCtasPerSm) * sm_count(device);
+  const int64_t items = B * H * ((N + kTile - 1) / kTile);  // 128-row query tiles (row pass) = key tiles (column)
+  const int64_t cap = sm_count(device);
   const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
   float* di = static_cast<float*>(scratch);
   const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
-  tc_bwd_dq_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+  tc_bwd_dq_split_kernel<T, D><<<grid, LR::kThreads, LR::kSmem, st>>>(
       tq, tk64, tv64, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), di, static_cast<T*>(dq), BH, Hi,
       Ni, static_cast<float>(scale));
-  if ((s = check_launch("tc_bwd_dq_pipe_kernel"))) return s;
-  tc_bwd_dkdv_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+  if ((s = check_launch("tc_bwd_dq_split_kernel"))) return s;
+  tc_bwd_dkdv_split_kernel<T, D><<<grid, LC::kThreads, LC::kSmem, st>>>(
       tk, tv, tq64, tdo64, static_cast<const float*>(lse), di, static_cast<T*>(dk), static_cast<T*>(dv), BH, Hi, Ni,
       static_cast<float>(scale));
-  return check_launch("tc_bwd_dkdv_pipe_kernel");
+  return check_launch("tc_bwd_dkdv_split_kernel");
 }
 
 // ------------------------------------------------------------------------------------------------ double backward
