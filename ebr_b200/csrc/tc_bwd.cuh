@@ -218,23 +218,33 @@ __global__ void __launch_bounds__(352, 1)
         // keys past N (the last step only) are masked so exp(-Li) cannot reach dQ.
         const int valid = N - j * 64;
         const int nch = valid > 32 ? 2 : 1;
+        // The second 32 keys' scores are requested before the first 32 are turned into dS, so that load's latency
+        // hides behind the exponentials.
+        uint32_t rs[2][32], rp[2][32];
+        tmem_ld32(tS, rs[0]);
+        tmem_ld32(tDP, rp[0]);
+        tmem_wait_ld_regs(rs[0]);
+        tmem_wait_ld_regs(rp[0]);
+        if (nch > 1) {
+          tmem_ld32(tS + 32, rs[1]);
+          tmem_ld32(tDP + 32, rp[1]);
+        }
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
           if (c < nch) {
-            uint32_t rs[32], rp[32];
-            tmem_ld32(tS + 32 * c, rs);
-            tmem_ld32(tDP + 32 * c, rp);
-            tmem_wait_ld_regs(rs);
-            tmem_wait_ld_regs(rp);
+            if (c == 1) {
+              tmem_wait_ld_regs(rs[1]);
+              tmem_wait_ld_regs(rp[1]);
+            }
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
               float ds[2];
 #pragma unroll
               for (int u = 0; u < 2; ++u) {
-                float p = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li));
+                float p = exp_nat(fmaf(__uint_as_float(rs[c][e + u]), scale, -Li));
                 if (valid < 64 && 32 * c + e + u >= valid) p = 0.f;
-                ds[u] = p * (__uint_as_float(rp[e + u]) - Di);
+                ds[u] = p * (__uint_as_float(rp[c][e + u]) - Di);
               }
               pk[e >> 1] = pack2<T>(ds[0], ds[1]);
             }
@@ -474,13 +484,20 @@ __global__ void __launch_bounds__(352, 1)
         tc_fence_after();
         // The stage's lse / D were written before q_full completed, and S^T was computed after it.
         const float* st = stats + s * 128;
+        // The second 32 queries' scores are requested before the first 32 are processed (latency hidden).
+        uint32_t rs[2][32], rp[2][32];
+        tmem_ld32(tS, rs[0]);
+        tmem_ld32(tDP, rp[0]);
+        tmem_wait_ld_regs(rs[0]);
+        tmem_wait_ld_regs(rp[0]);
+        tmem_ld32(tS + 32, rs[1]);
+        tmem_ld32(tDP + 32, rp[1]);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          uint32_t rs[32], rp[32];
-          tmem_ld32(tS + 32 * c, rs);
-          tmem_ld32(tDP + 32 * c, rp);
-          tmem_wait_ld_regs(rs);
-          tmem_wait_ld_regs(rp);
+          if (c == 1) {
+            tmem_wait_ld_regs(rs[1]);
+            tmem_wait_ld_regs(rp[1]);
+          }
           uint32_t pp[16], pd[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -488,8 +505,8 @@ __global__ void __launch_bounds__(352, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int qc = 32 * c + e + u;
-              p[u] = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -st[qc]));
-              ds[u] = p[u] * (__uint_as_float(rp[e + u]) - st[64 + qc]);
+              p[u] = exp_nat(fmaf(__uint_as_float(rs[c][e + u]), scale, -st[qc]));
+              ds[u] = p[u] * (__uint_as_float(rp[c][e + u]) - st[64 + qc]);
             }
             pp[e >> 1] = pack2<T>(p[0], p[1]);
             pd[e >> 1] = pack2<T>(ds[0], ds[1]);
