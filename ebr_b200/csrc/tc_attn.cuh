@@ -439,7 +439,7 @@ __device__ __forceinline__ float row_delta(const unsigned char* sDO, int row, co
   return di;
 }
 
-// ================================================================================================ backward (pipelined)
+// ================================================================================================ tile descriptors for 64- and 128-row tiles
 
 // Descriptors for tiles of `rows` rows (64 or 128): the 64-column halves of a D = 128 tile are rows * 128 B apart.
 __device__ __forceinline__ uint64_t desc_kmajor_r(const unsigned char* tile, int kk, uint32_t half_bytes) {
@@ -447,407 +447,6 @@ __device__ __forceinline__ uint64_t desc_kmajor_r(const unsigned char* tile, int
 }
 __device__ __forceinline__ uint64_t desc_mnmajor_r(const unsigned char* tile, int kk, uint32_t half_bytes) {
   return sw128_desc(smem_u32(tile) + kk * 2048u, half_bytes, 1024u);
-}
-
-template <int D>
-struct BwdPipeLayout {
-  static constexpr uint32_t kHalf64 = 64u * 128u;              // [64 x 64] 16-bit tile
-  static constexpr uint32_t kBig = (D / 64) * kHalfBytes;      // [128 x D] tile
-  static constexpr uint32_t kSmall = (D / 64) * kHalf64;       // [64 x D] tile
-  static constexpr int kStages = 2;
-  // Big-tile pair (double-buffered per item): buffer b holds tiles at kBigPair + b * 2 kBig and + kBig.
-  static constexpr uint32_t kBigPair = 0;
-  static constexpr uint32_t kRing = 4 * kBig;                  // stage s: small tiles at kRing + s * 2 kSmall, + kSmall
-  static constexpr uint32_t kStats = kRing + kStages * 2 * kSmall;  // [2][2][64] floats (column-pass row scalars)
-  static constexpr uint32_t kBytes = kStats + 2 * 2 * 64 * 4;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kThreads = 320;
-};
-
-// Row pass of the backward for N > 128, persistent and warp-specialized: an item is 128 query rows of one slice
-// (Q, dO double-buffered per item); the key tiles stream through a 2-stage ring in steps of 64 keys.
-//   warps 0-7  compute, two warpgroups: warp w owns TMEM lanes 32 (w % 4) .. + 31 (query rows) and key columns
-//              32 (w / 4) .. + 31 of each step, so each row's 64 keys are split between two threads;
-//   warp 8     TMA producer;  warp 9  MMA issuer.
-// Per step: S = Q K^T and dP = dO V^T (M = 128 queries, N = 64 keys) into TMEM; the compute warps form
-// dS = P (dP - D) with P = exp(fma(s, scale, -lse)), pack it to 16 bits over the S columns they have read (key k at
-// column 32 (k / 32) + (k % 32) / 2), and the MMA warp accumulates dQ += dS K with dS read from TMEM. D_i = <dO_i, O_i>
-// is computed at the start of each item from the stored O and written to `di` for the column pass. The reference's
-// _bwd_dq_kernel + _rowdot_kernel (triton_kernels.py:277-339, :171-181). TMEM: S [0, 64), dP [64, 128),
-// dQ [128, 128 + D).
-template <typename T, int D>
-__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
-    tc_bwd_dq_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk64,
-                          const __grid_constant__ CUtensorMap tv64, const __grid_constant__ CUtensorMap tdo,
-                          const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
-                          T* __restrict__ dq, int BH, int H, int N, float scale) {
-  using L = BwdPipeLayout<D>;
-  constexpr int NS = L::kStages;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_qt = (N + kTile - 1) / kTile, n_ks = (N + 63) / 64;
-  const int64_t items = static_cast<int64_t>(BH) * n_qt;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 64);
-  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
-  auto sQ = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig; };
-  auto sDO = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig + L::kBig; };
-  auto sK = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
-  auto sV = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
-
-  if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 256);
-    mbar_init(&o_done, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, 256);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort = &abort_flag;
-
-  if (warp == 8) {
-    if (lane == 0) {
-      uint32_t kv_use = 0;
-      int64_t li = 0;
-      bool ok = true;
-      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-        const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
-        const int b = bh / H, h = bh - (bh / H) * H;
-        const int qb = static_cast<int>(li & 1);
-        ok = mbar_wait_or_abort(&q_empty[qb], ((li >> 1) & 1) ^ 1, 241, abort);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&q_full[qb], 2 * L::kBig);
-        for (int hh = 0; hh < D / 64; ++hh) {
-          tma_load_4d(sQ(qb) + hh * kHalfBytes, &tq, &q_full[qb], hh * 64, qt * kTile, h, b);
-          tma_load_4d(sDO(qb) + hh * kHalfBytes, &tdo, &q_full[qb], hh * 64, qt * kTile, h, b);
-        }
-        for (int j = 0; j < n_ks; ++j, ++kv_use) {
-          const int s = static_cast<int>(kv_use % NS);
-          ok = mbar_wait_or_abort(&kv_empty[s], ((kv_use / NS) & 1) ^ 1, 242, abort);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::kSmall);
-          for (int hh = 0; hh < D / 64; ++hh) {
-            tma_load_4d(sK(s) + hh * L::kHalf64, &tk64, &kv_full[s], hh * 64, j * 64, h, b);
-            tma_load_4d(sV(s) + hh * L::kHalf64, &tv64, &kv_full[s], hh * 64, j * 64, h, b);
-          }
-        }
-      }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      const uint32_t tS = tmem, tDP = tmem + 64, tDQ = tmem + 128;
-      uint32_t kv_use = 0, t = 0;
-      int64_t li = 0;
-      bool ok = true;
-      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-        const int qb = static_cast<int>(li & 1);
-        ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 251, abort);
-        for (int j = 0; j < n_ks && ok; ++j, ++kv_use, ++t) {
-          const int s = static_cast<int>(kv_use % NS);
-          ok = mbar_wait_or_abort(&kv_full[s], (kv_use / NS) & 1, 252, abort);
-          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 253, abort);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            mma_ss(tS, desc_kmajor(sQ(qb), kk), desc_kmajor_r(sK(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
-            mma_ss(tDP, desc_kmajor(sDO(qb), kk), desc_kmajor_r(sV(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full);
-          if (j == n_ks - 1) mma_commit(&q_empty[qb]);
-          ok = mbar_wait_or_abort(&p_full, t & 1, 254, abort);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tDQ, tS + (kk >> 1) * 32 + (kk & 1) * 8, desc_mnmajor_r(sK(s), kk, L::kHalf64), kIdKM,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&o_done);
-          mma_commit(&kv_empty[s]);
-        }
-      }
-    }
-  } else {
-    const int half = warp >> 2, lrow = (warp & 3) * 32 + lane;  // key-column half, query row in the tile
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + half * 32, tDP = tmem + 64 + lane_off + half * 32;
-    uint32_t t = 0;
-    int64_t li = 0;
-    bool ok = true;
-    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-      const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
-      const int qb = static_cast<int>(li & 1);
-      const int row = qt * kTile + lrow;
-      const bool row_ok = row < N;
-      const int64_t grow = static_cast<int64_t>(bh) * N + row;
-      const float Li = row_ok ? lse[grow] : 0.f;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 261, abort));
-      if (!ok) break;
-      float Di = 0.f;
-      if (row_ok) {
-        Di = row_delta<T, D>(sDO(qb), lrow, o + grow * D);
-        if (half == 0) di_out[grow] = Di;
-      }
-      for (int j = 0; j < n_ks; ++j, ++t) {
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 262, abort));
-        if (!ok) break;
-        tc_fence_after();
-        // Query rows past N have zero Q / dO (TMA fill) and Li = Di = 0, so their dS is exactly 0 without a mask;
-        // keys past N (the last step only) are masked so exp(-Li) cannot reach dQ.
-        const int valid = N - j * 64 - half * 32;
-#pragma unroll
-        for (int sc = 0; sc < 32; sc += 16) {
-          uint32_t rs[16], rp[16];
-          tmem_ld16(tS + sc, rs);
-          tmem_ld16(tDP + sc, rp);
-          tmem_wait_ld();
-          uint32_t pk[8];
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            float ds[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              float p = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li));
-              if (valid < 32 && sc + e + u >= valid) p = 0.f;
-              ds[u] = p * (__uint_as_float(rp[e + u]) - Di);
-            }
-            pk[e >> 1] = pack2<T>(ds[0], ds[1]);
-          }
-          tmem_st8(tS + (sc >> 1), pk);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full);
-      }
-      if (!ok) break;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 263, abort));
-      if (!ok) break;
-      tc_fence_after();
-      T* dst = row_ok ? dq + grow * D : nullptr;
-      store_cols_from_tmem<T, D / 2>(tmem + 128 + lane_off, half * (D / 2), scale, dst);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
-}
-
-// Column pass of the backward for N > 128: an item is 128 keys of one slice (K, V double-buffered per item); the
-// query tiles stream through a 2-stage ring in steps of 64 queries, with each step's lse and D staged in shared memory
-// by the producer warp. Per step: S^T = K Q^T and dP^T = V dO^T (M = 128 keys, N = 64 queries) into TMEM; the two
-// compute warpgroups (warp w: keys 32 (w % 4) .., query columns 32 (w / 4) ..) form P^T and dS^T, pack both to 16 bits
-// over the columns they have read, and the MMA warp accumulates dV += P^T dO and dK += dS^T Q with A read from TMEM.
-// The reference's _bwd_col_kernel (triton_kernels.py:184-274, two-kernel mode).
-// TMEM: S^T [0, 64), dP^T [64, 128), dK [128, 128 + D), dV after dK.
-template <typename T, int D>
-__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
-    tc_bwd_dkdv_pipe_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                            const __grid_constant__ CUtensorMap tq64, const __grid_constant__ CUtensorMap tdo64,
-                            const float* __restrict__ lse, const float* __restrict__ di, T* __restrict__ dk,
-                            T* __restrict__ dv, int BH, int H, int N, float scale) {
-  using L = BwdPipeLayout<D>;
-  constexpr int NS = L::kStages;
-  constexpr uint32_t kCols = (D == 64) ? 256 : 512;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  __shared__ uint64_t k_full[2], k_empty[2], q_full[NS], q_empty[NS], s_full, p_full, o_done;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_kt = (N + kTile - 1) / kTile, n_qs = (N + 63) / 64;
-  const int64_t items = static_cast<int64_t>(BH) * n_kt;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 64);
-  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
-  auto sK = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig; };
-  auto sV = [&](int b) { return smem + L::kBigPair + b * 2 * L::kBig + L::kBig; };
-  auto sQ = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
-  auto sDO = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
-  float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [stage][lse 64 | D 64]
-
-  if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&q_full[i], 33);  // the TMA transaction arrive + one arrive per producer lane after its lse / D writes
-      mbar_init(&q_empty[i], 1);
-    }
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 256);
-    mbar_init(&o_done, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, kCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort = &abort_flag;
-
-  if (warp == 8) {
-    // Lane 0 issues the TMA loads; all 32 lanes stage each query step's lse and D (64 + 64 floats) in shared memory.
-    uint32_t q_use = 0;
-    int64_t li = 0;
-    bool ok = true;
-    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-      const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-      const int b = bh / H, h = bh - (bh / H) * H;
-      const int64_t base = static_cast<int64_t>(bh) * N;
-      const int kb = static_cast<int>(li & 1);
-      if (lane == 0) {
-        ok = mbar_wait_or_abort(&k_empty[kb], ((li >> 1) & 1) ^ 1, 271, abort);
-        if (ok) {
-          mbar_arrive_expect_tx(&k_full[kb], 2 * L::kBig);
-          for (int hh = 0; hh < D / 64; ++hh) {
-            tma_load_4d(sK(kb) + hh * kHalfBytes, &tk, &k_full[kb], hh * 64, kt * kTile, h, b);
-            tma_load_4d(sV(kb) + hh * kHalfBytes, &tv, &k_full[kb], hh * 64, kt * kTile, h, b);
-          }
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      for (int i = 0; i < n_qs && ok; ++i, ++q_use) {
-        const int s = static_cast<int>(q_use % NS);
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_empty[s], ((q_use / NS) & 1) ^ 1, 272, abort));
-        if (!ok) break;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&q_full[s], 2 * L::kSmall);
-          for (int hh = 0; hh < D / 64; ++hh) {
-            tma_load_4d(sQ(s) + hh * L::kHalf64, &tq64, &q_full[s], hh * 64, i * 64, h, b);
-            tma_load_4d(sDO(s) + hh * L::kHalf64, &tdo64, &q_full[s], hh * 64, i * 64, h, b);
-          }
-        }
-        // Queries past N get lse = D = 0: with their zero Q / dO rows this makes P^T = 1 and dS^T = 0 there, and
-        // dO = 0 keeps them out of dV, so the compute warps need no mask.
-        float* st = stats + s * 128;
-#pragma unroll
-        for (int k2 = lane; k2 < 64; k2 += 32) {
-          const int qi = i * 64 + k2;
-          st[k2] = qi < N ? lse[base + qi] : 0.f;
-          st[64 + k2] = qi < N ? di[base + qi] : 0.f;
-        }
-        mbar_arrive(&q_full[s]);
-      }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      const uint32_t tS = tmem, tDP = tmem + 64, tDK = tmem + 128, tDV = tmem + 128 + D;
-      uint32_t q_use = 0, t = 0;
-      int64_t li = 0;
-      bool ok = true;
-      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-        const int kb = static_cast<int>(li & 1);
-        ok = mbar_wait_or_abort(&k_full[kb], (li >> 1) & 1, 281, abort);
-        for (int i = 0; i < n_qs && ok; ++i, ++q_use, ++t) {
-          const int s = static_cast<int>(q_use % NS);
-          ok = mbar_wait_or_abort(&q_full[s], (q_use / NS) & 1, 282, abort);
-          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 283, abort);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            mma_ss(tS, desc_kmajor(sK(kb), kk), desc_kmajor_r(sQ(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
-            mma_ss(tDP, desc_kmajor(sV(kb), kk), desc_kmajor_r(sDO(s), kk, L::kHalf64), kIdNN, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full);
-          ok = mbar_wait_or_abort(&p_full, t & 1, 284, abort);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t col = (kk >> 1) * 32 + (kk & 1) * 8;
-            mma_ts(tDV, tS + col, desc_mnmajor_r(sDO(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
-            mma_ts(tDK, tDP + col, desc_mnmajor_r(sQ(s), kk, L::kHalf64), kIdKM, (i > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(&o_done);
-          mma_commit(&q_empty[s]);
-          if (i == n_qs - 1) mma_commit(&k_empty[kb]);
-        }
-      }
-    }
-  } else {
-    const int half = warp >> 2, lkey = (warp & 3) * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + half * 32, tDP = tmem + 64 + lane_off + half * 32;
-    uint32_t t = 0;
-    bool ok = true;
-    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-      for (int i = 0; i < n_qs; ++i, ++t) {
-        const int s = static_cast<int>(t % NS);
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_full[s], (t / NS) & 1, 293, abort));
-        if (!ok) break;
-        const float* st = stats + s * 128 + half * 32;
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 291, abort));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int sc = 0; sc < 32; sc += 16) {
-          uint32_t rs[16], rp[16];
-          tmem_ld16(tS + sc, rs);
-          tmem_ld16(tDP + sc, rp);
-          tmem_wait_ld();
-          uint32_t pp[8], pd[8];
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            float p[2], ds[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int qc = sc + e + u;
-              p[u] = exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -st[qc]));
-              ds[u] = p[u] * (__uint_as_float(rp[e + u]) - st[64 + qc]);
-            }
-            pp[e >> 1] = pack2<T>(p[0], p[1]);
-            pd[e >> 1] = pack2<T>(ds[0], ds[1]);
-          }
-          tmem_st8(tS + (sc >> 1), pp);
-          tmem_st8(tDP + (sc >> 1), pd);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full);
-      }
-      if (!ok) break;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 292, abort));
-      if (!ok) break;
-      tc_fence_after();
-      const int key = kt * kTile + lkey;
-      const int64_t gk = static_cast<int64_t>(bh) * N + key;
-      // Warpgroup 0 writes dK, warpgroup 1 writes dV.
-      T* dst = key < N ? (half == 0 ? dk : dv) + gk * D : nullptr;
-      store_cols_from_tmem<T, D>(tmem + lane_off + (half == 0 ? 128 : 128 + D), 0, half == 0 ? scale : 1.f, dst);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
 // ================================================================================================ double backward (pipelined)
