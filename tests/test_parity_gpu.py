@@ -100,6 +100,14 @@ SHAPES_16 = [
     (1, 2, 256, 64),
     (1, 1, 300, 128),
     (1, 1, 900, 64),
+    # N > 128 edges of the paired forward and the multi-buffered backward: a second query tile of one row and a last
+    # key step of one key (129), an odd tile count with a ragged 64-key step of more than 32 keys (191), exact
+    # multiples of 64 and 128 (320, 384 at D = 128), several items per CTA across the grid (1000 keys, 16 slices).
+    (1, 2, 129, 64),
+    (1, 2, 191, 128),
+    (2, 1, 320, 64),
+    (1, 2, 384, 128),
+    (2, 8, 1000, 64),
 ]
 
 
