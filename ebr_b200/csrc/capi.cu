@@ -11,6 +11,7 @@
 #include "../../include/ebr_attn.h"
 #include "simt.cuh"
 #include "tc_attn.cuh"
+#include "tc_bob.cuh"
 #include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
 
@@ -396,6 +397,63 @@ int launch_tc_bob_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, d
   return check_launch("tc_bob_col_pipe_kernel");
 }
 
+// D = 64: the statistics pass and the two output passes of tc_bob.cuh.
+template <typename T>
+int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                        const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
+                        void* hq, void* hk, void* hv, void* hdo, void* scratch, cudaStream_t st) {
+  constexpr int D = 64;
+  using LR = BobSplitLayout<false>;
+  using LC = BobSplitLayout<true>;
+  const bool has[3] = {gq && gq->data, gk && gk->data, gv && gv->data};
+  const uint32_t flags = (has[0] ? 1u : 0u) | (has[1] ? 2u : 0u) | (has[2] ? 4u : 0u);
+  CUtensorMap tq, tdo, tgq, tk, tv, tgk, tgv, tq64, tdo64, tgq64, tk64, tv64, tgk64, tgv64;
+  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D) ||
+      make_tile_map(&tk, k, dtype, B, H, N, D) || make_tile_map(&tv, v, dtype, B, H, N, D) ||
+      make_tile_map(&tq64, q, dtype, B, H, N, D, 64) || make_tile_map(&tdo64, dout, dtype, B, H, N, D, 64) ||
+      make_tile_map(&tk64, k, dtype, B, H, N, D, 64) || make_tile_map(&tv64, v, dtype, B, H, N, D, 64))
+    return kNoTensorMap;
+  // An absent cotangent's maps are never read (its loads and products are skipped); any valid map fills the slot.
+  const ebr_operand* gs[3] = {gq, gk, gv};
+  CUtensorMap* big[3] = {&tgq, &tgk, &tgv};
+  CUtensorMap* small[3] = {&tgq64, &tgk64, &tgv64};
+  for (int i = 0; i < 3; ++i) {
+    if (!has[i]) {
+      *big[i] = tq;
+      *small[i] = tq64;
+    } else if (make_tile_map(big[i], gs[i], dtype, B, H, N, D) || make_tile_map(small[i], gs[i], dtype, B, H, N, D, 64)) {
+      return kNoTensorMap;
+    }
+  }
+  const void* f0 = reinterpret_cast<const void*>(tc_bob_stats_kernel<T>);
+  const void* f1 = reinterpret_cast<const void*>(tc_bob_out_kernel<T, false>);
+  const void* f2 = reinterpret_cast<const void*>(tc_bob_out_kernel<T, true>);
+  int s = prepare_tc_kernel(f0, device, LR::kSmem, LR::kTmemCols, LR::kThreads);
+  if (s || (s = prepare_tc_kernel(f1, device, LR::kSmem, LR::kTmemCols, LR::kThreads)) ||
+      (s = prepare_tc_kernel(f2, device, LC::kSmem, LC::kTmemCols, LC::kThreads)))
+    return s;
+  const int64_t items = B * H * ((N + kTile - 1) / kTile);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  float* stats = static_cast<float*>(scratch);
+  const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
+  const float sc = static_cast<float>(scale);
+  const float* lsef = static_cast<const float*>(lse);
+  tc_bob_stats_kernel<T><<<grid, LR::kThreads, LR::kSmem, st>>>(tq, tdo, tgq, tk64, tv64, tgk64, tgv64,
+                                                                 static_cast<const T*>(o), lsef, stats, BH, Hi, Ni, sc,
+                                                                 flags);
+  if ((s = check_launch("tc_bob_stats_kernel"))) return s;
+  tc_bob_out_kernel<T, false><<<grid, LR::kThreads, LR::kSmem, st>>>(tq, tdo, tgq, tq, tk64, tv64, tgk64, tgv64, lsef,
+                                                                     stats, static_cast<T*>(hq), static_cast<T*>(hdo),
+                                                                     BH, Hi, Ni, sc, flags);
+  if ((s = check_launch("tc_bob_out_kernel<rows>"))) return s;
+  tc_bob_out_kernel<T, true><<<grid, LC::kThreads, LC::kSmem, st>>>(tk, tv, tgk, tgv, tq64, tdo64, tgq64, tq64, lsef,
+                                                                    stats, static_cast<T*>(hk), static_cast<T*>(hv),
+                                                                    BH, Hi, Ni, sc, flags);
+  return check_launch("tc_bob_out_kernel<cols>");
+}
+
 template <typename T>
 int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
                          const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
@@ -594,13 +652,13 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
     return set_error(EBR_ERR_SCRATCH, "scratch missing or too small%s%s");
   if (outs_ok && tc_eligible(dtype, D, {q, k, v, dout, gq, gk, gv}, B, H, N)) {
     if (dtype == EBR_BFLOAT16)
-      s = D == 64 ? launch_tc_bob_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk,
-                                                           gv, hq, hk, hv, hdout, scratch, st)
+      s = D == 64 ? launch_tc_bob_split<__nv_bfloat16>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk,
+                                                        gv, hq, hk, hv, hdout, scratch, st)
                   : launch_tc_bob_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq,
                                                             gk, gv, hq, hk, hv, hdout, scratch, st);
     else
-      s = D == 64 ? launch_tc_bob_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv,
-                                                   hq, hk, hv, hdout, scratch, st)
+      s = D == 64 ? launch_tc_bob_split<__half>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq,
+                                                hk, hv, hdout, scratch, st)
                   : launch_tc_bob_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv,
                                                     hq, hk, hv, hdout, scratch, st);
     if (s != kNoTensorMap) return s;

@@ -1,0 +1,565 @@
+// tc_bob.cuh: the tensor-core double backward for N > 128 at D = 64, with the score products of one step overlapping
+// the pointwise work of the previous one.
+//
+// Three passes, as in the reference's _bob_row_kernel / _bob_col_kernel (triton_kernels.py:347-551) restated with the
+// closed form of reference.py:80-90: a row pass for the per-row statistics D, E, T; a row pass for hQ and hdO; a
+// column pass for hK and hV. Per 64-key (or 64-query) step the MMA warp forms four score tiles of M = 128, N = 64 --
+// S = Q K^T, dP = dO V^T, G = gQ K^T + Q gK^T, R = dO gV^T (their transposes in the column pass) -- and the output
+// passes accumulate from 16-bit tiles the compute warps derive from them.
+//
+// Roles (320 threads, one persistent CTA per SM):
+//   warps 0-7  compute: warp w owns TMEM lanes [32 (w % 4), 32 (w % 4) + 32) -- one query (key) row per thread -- and
+//              warpgroup w / 4 the columns [32 (w / 4), 32 (w / 4) + 32) of every step, so both warpgroups work on
+//              the same step and a row's sums are split in two halves, added at the end of the item;
+//   warp 8     TMA producer: the item's 128-row tiles (two buffers), the streamed 64-row tiles (a three-stage ring)
+//              and, in the column pass, each step's lse / D / E / T;
+//   warp 9     MMA issuer (one thread).
+// Tensor memory (512 columns):
+//   statistics pass: two score buffers of 256 columns (S, dP, G, R at +0, +64, +128, +192); step g uses buffer g % 2,
+//     so the products of step g + 1 run while the compute warps read step g;
+//   output passes: one score buffer [0, 256), the 16-bit tiles [256, 384) (four of 32 columns: 64 keys as pairs), the
+//     two accumulators in [384, 448) and [448, 512). A step's scores are released as soon as the compute warps have
+//     loaded them, so the tensor pipe runs the next step's score products, then this step's accumulating products
+//     (issued once the 16-bit tiles are written), while the compute warps work.
+#pragma once
+
+#include "tc_attn.cuh"
+
+namespace ebr {
+
+template <bool kCol>
+struct BobSplitLayout {
+  static constexpr uint32_t kBig = kHalfBytes;   // [128 x 64] 16-bit tile
+  static constexpr uint32_t kSmall = 64u * 128u;  // [64 x 64] 16-bit tile
+  static constexpr int kItemBufs = 2;
+  static constexpr int kStages = 3;
+  static constexpr int kItemTiles = kCol ? 4 : 3;  // row passes: Q, dO, gQ; column pass: K, V, gK, gV
+  static constexpr int kRingTiles = kCol ? 3 : 4;  // row passes: K, V, gK, gV; column pass: Q, dO, gQ
+  static constexpr uint32_t kItemBytes = kItemTiles * kBig;
+  static constexpr uint32_t kStageBytes = kRingTiles * kSmall;
+  static constexpr uint32_t kRing = kItemBufs * kItemBytes;
+  // Row passes: the second warpgroup's partial row sums, [2 slots][4 sums][128 rows] floats.
+  // Column pass: each stage's per-query (lse, D, E, T), [stage][64 queries][4] floats.
+  static constexpr uint32_t kAux = kRing + kStages * kStageBytes;
+  static constexpr uint32_t kAuxBytes = kCol ? kStages * 64 * 4 * 4 : 2 * 4 * 128 * 4;
+  static constexpr uint32_t kBytes = kAux + kAuxBytes;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kThreads = 320;
+};
+
+// The score products of one step (M = 128, N = 64, K = 64), all K-major: a* are the 128-row item tiles, b* the 64-row
+// ring tiles (row passes: a = Q, dO, gQ and b = K, V, gK, gV; column pass: a = K, V, gK, gV and b = Q, dO, gQ). The
+// caller maps them so that S = a0 b0^T, dP = a1 b1^T, G = ag0 bg0^T + ag1 bg1^T, R = ar br^T.
+__device__ __forceinline__ void bob_scores(uint32_t t0, const unsigned char* aS, const unsigned char* bS,
+                                           const unsigned char* aP, const unsigned char* bP,
+                                           const unsigned char* aG0, const unsigned char* bG0,
+                                           const unsigned char* aG1, const unsigned char* bG1,
+                                           const unsigned char* aR, const unsigned char* bR, bool g0, bool g1, bool r,
+                                           uint32_t idesc) {
+  constexpr uint32_t kSmall = 64u * 128u;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint32_t acc = kk > 0 ? 1u : 0u;
+    mma_ss(t0, desc_kmajor(aS, kk), desc_kmajor_r(bS, kk, kSmall), idesc, acc);
+    mma_ss(t0 + 64, desc_kmajor(aP, kk), desc_kmajor_r(bP, kk, kSmall), idesc, acc);
+    if (g0) mma_ss(t0 + 128, desc_kmajor(aG0, kk), desc_kmajor_r(bG0, kk, kSmall), idesc, acc);
+    if (g1) mma_ss(t0 + 128, desc_kmajor(aG1, kk), desc_kmajor_r(bG1, kk, kSmall), idesc, (g0 || kk > 0) ? 1u : 0u);
+    if (r) mma_ss(t0 + 192, desc_kmajor(aR, kk), desc_kmajor_r(bR, kk, kSmall), idesc, acc);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ statistics pass
+
+// Per query row: D = <dO, O>, E = sum_j P G (G scaled), T = sum_j P (dP - D) G - E sum_j P dP + sum_j P R, written to
+// `stats` ([3][B H N]). An item is 128 query rows of one slice; the keys stream in 64-key steps.
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+    tc_bob_stats_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                        const __grid_constant__ CUtensorMap tgq, const __grid_constant__ CUtensorMap tk64,
+                        const __grid_constant__ CUtensorMap tv64, const __grid_constant__ CUtensorMap tgk64,
+                        const __grid_constant__ CUtensorMap tgv64, const T* __restrict__ o,
+                        const float* __restrict__ lse, float* __restrict__ stats, int BH, int H, int N, float scale,
+                        uint32_t flags) {
+  using L = BobSplitLayout<false>;
+  constexpr int NS = L::kStages, NI = L::kItemBufs;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t it_full[NI], it_empty[NI], rg_full[NS], rg_empty[NS], s_full[2], s_free[2], part_full[2],
+      part_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_qt = (N + kTile - 1) / kTile, n_ks = (N + 63) / 64;
+  const int64_t items = static_cast<int64_t>(BH) * n_qt;
+  const int64_t rows_total = static_cast<int64_t>(BH) * N;
+  const bool has_gq = flags & 1u, has_gk = flags & 2u, has_gv = flags & 4u;
+  auto item = [&](int b, int i) { return smem + b * L::kItemBytes + i * L::kBig; };                // 0 Q 1 dO 2 gQ
+  auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };  // 0 K 1 V 2 gK 3 gV
+  float* part = reinterpret_cast<float*>(smem + L::kAux);
+
+  if (tid == 0) {
+    for (int i = 0; i < NI; ++i) {
+      mbar_init(&it_full[i], 1);
+      mbar_init(&it_empty[i], 1 + 256);  // the MMA warp's commit + every compute thread once it has read dO
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&rg_full[i], 1);
+      mbar_init(&rg_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 256);
+      mbar_init(&part_full[i], 128);
+      mbar_init(&part_empty[i], 128);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      const uint32_t item_bytes = (2u + (has_gq ? 1u : 0u)) * L::kBig;
+      const uint32_t ring_bytes = (2u + (has_gk ? 1u : 0u) + (has_gv ? 1u : 0u)) * L::kSmall;
+      int64_t li = 0;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
+        const int b = bh / H, h = bh - (bh / H) * H;
+        const int ib = static_cast<int>(li % NI);
+        ok = mbar_wait_or_abort(&it_empty[ib], (static_cast<uint32_t>(li / NI) & 1) ^ 1, 511, abort);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&it_full[ib], item_bytes);
+        tma_load_4d(item(ib, 0), &tq, &it_full[ib], 0, qt * kTile, h, b);
+        tma_load_4d(item(ib, 1), &tdo, &it_full[ib], 0, qt * kTile, h, b);
+        if (has_gq) tma_load_4d(item(ib, 2), &tgq, &it_full[ib], 0, qt * kTile, h, b);
+        for (int j = 0; j < n_ks && ok; ++j, ++g) {
+          const int s = static_cast<int>(g % NS);
+          ok = mbar_wait_or_abort(&rg_empty[s], ((g / NS) & 1) ^ 1, 512, abort);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&rg_full[s], ring_bytes);
+          tma_load_4d(ring(s, 0), &tk64, &rg_full[s], 0, j * 64, h, b);
+          tma_load_4d(ring(s, 1), &tv64, &rg_full[s], 0, j * 64, h, b);
+          if (has_gk) tma_load_4d(ring(s, 2), &tgk64, &rg_full[s], 0, j * 64, h, b);
+          if (has_gv) tma_load_4d(ring(s, 3), &tgv64, &rg_full[s], 0, j * 64, h, b);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdNN = idesc_f16(is_bf16<T>(), 0, 0, 128, 64);
+      uint32_t g = 0;
+      bool ok = true;
+      int64_t li = 0;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int ib = static_cast<int>(li % NI);
+        ok = mbar_wait_or_abort(&it_full[ib], static_cast<uint32_t>(li / NI) & 1, 521, abort);
+        for (int j = 0; j < n_ks && ok; ++j, ++g) {
+          const int s = static_cast<int>(g % NS), b = static_cast<int>(g & 1);
+          // Buffer b is free once the compute warps have read its previous step (the first use passes at once).
+          ok = mbar_wait_or_abort(&s_free[b], ((g >> 1) & 1) ^ 1, 522, abort);
+          if (ok) ok = mbar_wait_or_abort(&rg_full[s], (g / NS) & 1, 523, abort);
+          if (!ok) break;
+          tc_fence_after();
+          bob_scores(tmem + 256 * b, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 2), ring(s, 0),
+                     item(ib, 0), ring(s, 2), item(ib, 1), ring(s, 3), has_gq, has_gk, has_gv, kIdNN);
+          mma_commit(&s_full[b]);
+          mma_commit(&rg_empty[s]);
+          if (j == n_ks - 1) mma_commit(&it_empty[ib]);
+        }
+      }
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------------- compute warps
+    const int w = warp >> 2, wq = warp & 3, lrow = wq * 32 + lane, col0 = 32 * w;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    uint32_t g = 0;
+    bool ok = true;
+    int64_t li = 0;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+      const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
+      const int ib = static_cast<int>(li % NI);
+      const int row = qt * kTile + lrow;
+      const bool row_ok = row < N;
+      const int64_t grow = static_cast<int64_t>(bh) * N + row;
+      const float Li = row_ok ? lse[grow] : 0.f;
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&it_full[ib], static_cast<uint32_t>(li / NI) & 1, 531, abort));
+      if (!ok) break;
+      const float Di = row_ok ? row_delta<T, 64>(item(ib, 1), lrow, o + grow * 64) : 0.f;
+      mbar_arrive(&it_empty[ib]);
+      float e_ = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+      for (int j = 0; j < n_ks; ++j, ++g) {
+        const int b = static_cast<int>(g & 1);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[b], (g >> 1) & 1, 532, abort));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t t0 = tmem + lane_off + 256 * b + col0;
+        uint32_t rs[32], rp[32], rg[32], rr[32];
+        tmem_ld32(t0, rs);
+        tmem_ld32(t0 + 64, rp);
+        if (has_gq || has_gk) tmem_ld32(t0 + 128, rg);
+        if (has_gv) tmem_ld32(t0 + 192, rr);
+        tmem_wait_ld_regs(rs);
+        tmem_wait_ld_regs(rp);
+        if (has_gq || has_gk) tmem_wait_ld_regs(rg);
+        if (has_gv) tmem_wait_ld_regs(rr);
+        tc_fence_before();
+        mbar_arrive(&s_free[b]);
+        const int valid = N - j * 64 - col0;  // keys of this half that exist
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          float p = exp_nat(fmaf(__uint_as_float(rs[u]), scale, -Li));
+          if (u >= valid) p = 0.f;
+          const float gg = (has_gq || has_gk) ? __uint_as_float(rg[u]) * scale : 0.f;
+          const float dp = __uint_as_float(rp[u]);
+          e_ += p * gg;
+          c1 += p * (dp - Di) * gg;
+          c2 += p * dp;
+          if (has_gv) c3 += p * __uint_as_float(rr[u]);
+        }
+      }
+      if (!ok) break;
+      // The two halves of each row meet in shared memory (slot li % 2): warpgroup 1 writes, warpgroup 0 adds.
+      const int slot = static_cast<int>(li & 1);
+      const uint32_t use = static_cast<uint32_t>(li >> 1) & 1;
+      float* ps = part + slot * 512;
+      if (w == 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&part_empty[slot], use ^ 1, 533, abort));
+        if (!ok) break;
+        ps[lrow] = e_;
+        ps[128 + lrow] = c1;
+        ps[256 + lrow] = c2;
+        ps[384 + lrow] = c3;
+        mbar_arrive(&part_full[slot]);
+      } else {
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&part_full[slot], use, 534, abort));
+        if (!ok) break;
+        e_ += ps[lrow];
+        c1 += ps[128 + lrow];
+        c2 += ps[256 + lrow];
+        c3 += ps[384 + lrow];
+        mbar_arrive(&part_empty[slot]);
+        if (row_ok) {
+          stats[grow] = Di;
+          stats[rows_total + grow] = e_;
+          stats[2 * rows_total + grow] = c1 - e_ * c2 + c3;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// ------------------------------------------------------------------------------------------------ output passes
+
+// Row pass: hQ = scale (gS K + dS gK) and hdO = A V + P gV, with dS = P (dP - D), A = P (G - E), gS = P (gp - T),
+// gp = (dP - D) G - E dP + R from the statistics pass. Column pass (kCol): hK = scale (gS^T Q + dS^T gQ) and
+// hV = A^T dO over the transposed tiles, with each query's lse / D / E / T staged per step. An item is 128 query
+// (key) rows of one slice; the other side streams in 64-row steps.
+template <typename T, bool kCol>
+__global__ void __launch_bounds__(320, 1)
+    tc_bob_out_kernel(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap ta1,
+                      const __grid_constant__ CUtensorMap ta2, const __grid_constant__ CUtensorMap ta3,
+                      const __grid_constant__ CUtensorMap tb0, const __grid_constant__ CUtensorMap tb1,
+                      const __grid_constant__ CUtensorMap tb2, const __grid_constant__ CUtensorMap tb3,
+                      const float* __restrict__ lse, const float* __restrict__ stats, T* __restrict__ out0,
+                      T* __restrict__ out1, int BH, int H, int N, float scale, uint32_t flags) {
+  using L = BobSplitLayout<kCol>;
+  constexpr int NS = L::kStages, NI = L::kItemBufs;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t it_full[NI], it_empty[NI], rg_full[NS], rg_empty[NS], s_full, s_free, p_full, pk_free, o_done,
+      acc_free;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_it = (N + kTile - 1) / kTile, n_st = (N + 63) / 64;
+  const int64_t items = static_cast<int64_t>(BH) * n_it;
+  const int64_t rows_total = static_cast<int64_t>(BH) * N;
+  const bool has_gq = flags & 1u, has_gk = flags & 2u, has_gv = flags & 4u;
+  // Which optional tiles exist: row pass items (Q, dO, gQ) and ring (K, V, gK, gV); column pass items (K, V, gK, gV)
+  // and ring (Q, dO, gQ).
+  const bool item_has[4] = {true, true, kCol ? has_gk : has_gq, kCol ? has_gv : false};
+  const bool ring_has[4] = {true, true, kCol ? has_gq : has_gk, kCol ? false : has_gv};
+  auto item = [&](int b, int i) { return smem + b * L::kItemBytes + i * L::kBig; };
+  auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };
+  float* stg = reinterpret_cast<float*>(smem + L::kAux);  // column pass: [stage][64][lse, D, E, T]
+
+  if (tid == 0) {
+    for (int i = 0; i < NI; ++i) {
+      mbar_init(&it_full[i], 1);
+      mbar_init(&it_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&rg_full[i], kCol ? 33 : 1);  // column pass: + one arrive per producer lane after its stats writes
+      mbar_init(&rg_empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_free, 256);
+    mbar_init(&p_full, 256);
+    mbar_init(&pk_free, 1);
+    mbar_init(&o_done, 1);
+    mbar_init(&acc_free, 256);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- producer (lane 0: TMA; column pass: all lanes
+    // also stage the step's per-query statistics)
+    uint32_t g = 0;
+    bool ok = true;
+    uint32_t item_bytes = 0, ring_bytes = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i < L::kItemTiles && item_has[i]) item_bytes += L::kBig;
+      if (i < L::kRingTiles && ring_has[i]) ring_bytes += L::kSmall;
+    }
+    const CUtensorMap* amap[4] = {&ta0, &ta1, &ta2, &ta3};
+    const CUtensorMap* bmap[4] = {&tb0, &tb1, &tb2, &tb3};
+    int64_t li = 0;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+      const int bh = static_cast<int>(it / n_it), t = static_cast<int>(it - static_cast<int64_t>(bh) * n_it);
+      const int b = bh / H, h = bh - (bh / H) * H;
+      const int64_t base = static_cast<int64_t>(bh) * N;
+      const int ib = static_cast<int>(li % NI);
+      if (lane == 0) {
+        ok = mbar_wait_or_abort(&it_empty[ib], (static_cast<uint32_t>(li / NI) & 1) ^ 1, 541, abort);
+        if (ok) {
+          mbar_arrive_expect_tx(&it_full[ib], item_bytes);
+#pragma unroll
+          for (int i = 0; i < L::kItemTiles; ++i)
+            if (item_has[i]) tma_load_4d(item(ib, i), amap[i], &it_full[ib], 0, t * kTile, h, b);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int j = 0; j < n_st && ok; ++j, ++g) {
+        const int s = static_cast<int>(g % NS);
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&rg_empty[s], ((g / NS) & 1) ^ 1, 542, abort));
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&rg_full[s], ring_bytes);
+#pragma unroll
+          for (int i = 0; i < L::kRingTiles; ++i)
+            if (ring_has[i]) tma_load_4d(ring(s, i), bmap[i], &rg_full[s], 0, j * 64, h, b);
+        }
+        if (kCol) {
+          // Queries past N get lse = D = E = T = 0: with their zero Q / dO / gQ rows every derived value is 0.
+          float4* st = reinterpret_cast<float4*>(stg) + s * 64;
+#pragma unroll
+          for (int k2 = lane; k2 < 64; k2 += 32) {
+            const int qi = j * 64 + k2;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qi < N) {
+              v.x = lse[base + qi];
+              v.y = stats[base + qi];
+              v.z = stats[rows_total + base + qi];
+              v.w = stats[2 * rows_total + base + qi];
+            }
+            st[k2] = v;
+          }
+          mbar_arrive(&rg_full[s]);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdNN = idesc_f16(is_bf16<T>(), 0, 0, 128, 64);
+      constexpr uint32_t kIdKM = idesc_f16(is_bf16<T>(), 0, 1, 128, 64);
+      const uint32_t tPk = tmem + 256, tAcc0 = tmem + 384, tAcc1 = tmem + 448;
+      uint32_t g = 0;
+      bool ok = true;
+      // The accumulating products of step g are issued after the score products of step g + 1: the step waiting for
+      // them (its index, ring stage, position in its item, item) is held here.
+      bool pend = false;
+      uint32_t pg = 0;
+      int ps = 0, pj = 0;
+      bool plast = false;
+      int64_t pli = 0;
+      auto accumulate = [&]() -> bool {
+        if (!mbar_wait_or_abort(&p_full, pg & 1, 553, abort)) return false;
+        // The first step of an item overwrites the accumulators: the previous item's must have been stored.
+        if (pj == 0 && pli > 0 && !mbar_wait_or_abort(&acc_free, static_cast<uint32_t>(pli - 1) & 1, 554, abort))
+          return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc0 = (pj > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t a = tPk + kk * 8;
+          if (!kCol) {
+            // hQ += gS K (+ dS gK); hdO += A V (+ P gV)
+            mma_ts(tAcc0, a, desc_mnmajor_r(ring(ps, 0), kk, L::kSmall), kIdKM, acc0);
+            if (has_gk) mma_ts(tAcc0, a + 32, desc_mnmajor_r(ring(ps, 2), kk, L::kSmall), kIdKM, 1u);
+            mma_ts(tAcc1, a + 64, desc_mnmajor_r(ring(ps, 1), kk, L::kSmall), kIdKM, acc0);
+            if (has_gv) mma_ts(tAcc1, a + 96, desc_mnmajor_r(ring(ps, 3), kk, L::kSmall), kIdKM, 1u);
+          } else {
+            // hK += gS^T Q (+ dS^T gQ); hV += A^T dO
+            mma_ts(tAcc0, a, desc_mnmajor_r(ring(ps, 0), kk, L::kSmall), kIdKM, acc0);
+            if (has_gq) mma_ts(tAcc0, a + 32, desc_mnmajor_r(ring(ps, 2), kk, L::kSmall), kIdKM, 1u);
+            mma_ts(tAcc1, a + 64, desc_mnmajor_r(ring(ps, 1), kk, L::kSmall), kIdKM, acc0);
+          }
+        }
+        mma_commit(&pk_free);
+        mma_commit(&rg_empty[ps]);
+        if (plast) mma_commit(&o_done);
+        return true;
+      };
+      int64_t li = 0;
+      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+        const int ib = static_cast<int>(li % NI);
+        ok = mbar_wait_or_abort(&it_full[ib], static_cast<uint32_t>(li / NI) & 1, 551, abort);
+        for (int j = 0; j < n_st && ok; ++j, ++g) {
+          const int s = static_cast<int>(g % NS);
+          ok = mbar_wait_or_abort(&rg_full[s], (g / NS) & 1, 552, abort);
+          // The score buffer is free once the compute warps have loaded the previous step.
+          if (ok) ok = mbar_wait_or_abort(&s_free, (g & 1) ^ 1, 555, abort);
+          if (!ok) break;
+          tc_fence_after();
+          if (!kCol)
+            bob_scores(tmem, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 2), ring(s, 0), item(ib, 0),
+                       ring(s, 2), item(ib, 1), ring(s, 3), has_gq, has_gk, has_gv, kIdNN);
+          else
+            bob_scores(tmem, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 0), ring(s, 2), item(ib, 2),
+                       ring(s, 0), item(ib, 3), ring(s, 1), has_gq, has_gk, has_gv, kIdNN);
+          mma_commit(&s_full);
+          if (j == n_st - 1) mma_commit(&it_empty[ib]);
+          if (pend) ok = accumulate();
+          pend = true;
+          pg = g;
+          ps = s;
+          pj = j;
+          plast = j == n_st - 1;
+          pli = li;
+        }
+      }
+      if (ok && pend) accumulate();
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------------- compute warps
+    const int w = warp >> 2, wq = warp & 3, lrow = wq * 32 + lane, col0 = 32 * w;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t t0 = tmem + lane_off + col0;              // this thread's 32 score columns
+    const uint32_t tp = tmem + lane_off + 256 + (col0 >> 1);  // its 16 columns of each 16-bit tile
+    uint32_t g = 0;
+    bool ok = true;
+    int64_t li = 0;
+    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
+      const int bh = static_cast<int>(it / n_it), t = static_cast<int>(it - static_cast<int64_t>(bh) * n_it);
+      const int row = t * kTile + lrow;
+      const bool row_ok = row < N;
+      const int64_t grow = static_cast<int64_t>(bh) * N + row;
+      // Row pass: this row's statistics (rows past N: 0, and their zero Q / dO / gQ make every product 0 but P V).
+      float Li = 0.f, Di = 0.f, Ei = 0.f, Ti = 0.f;
+      if (!kCol && row_ok) {
+        Li = lse[grow];
+        Di = stats[grow];
+        Ei = stats[rows_total + grow];
+        Ti = stats[2 * rows_total + grow];
+      }
+      for (int j = 0; j < n_st; ++j, ++g) {
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, g & 1, 561, abort));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t rs[32], rp[32], rg[32], rr[32];
+        const bool load_g = has_gq || has_gk, load_r = has_gv;
+        tmem_ld32(t0, rs);
+        tmem_ld32(t0 + 64, rp);
+        if (load_g) tmem_ld32(t0 + 128, rg);
+        if (load_r) tmem_ld32(t0 + 192, rr);
+        tmem_wait_ld_regs(rs);
+        tmem_wait_ld_regs(rp);
+        if (load_g) tmem_wait_ld_regs(rg);
+        if (load_r) tmem_wait_ld_regs(rr);
+        tc_fence_before();
+        mbar_arrive(&s_free);
+        // The previous step's accumulating products must have read the 16-bit tiles before they are rewritten.
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&pk_free, (g & 1) ^ 1, 562, abort));
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = kCol ? 64 : N - j * 64 - col0;  // row pass: keys of this half that exist
+        const float4* st = reinterpret_cast<const float4*>(stg) + (g % NS) * 64 + col0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 16) {
+          uint32_t pgs[8], pds[8], pa[8], pp[8];
+#pragma unroll
+          for (int u = 0; u < 16; u += 2) {
+            float v_gs[2], v_ds[2], v_a[2], v_p[2];
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              const int e = c + u + x;
+              float Lr = Li, Dr = Di, Er = Ei, Tr = Ti;
+              if (kCol) {
+                const float4 q4 = st[e];
+                Lr = q4.x;
+                Dr = q4.y;
+                Er = q4.z;
+                Tr = q4.w;
+              }
+              float p = exp_nat(fmaf(__uint_as_float(rs[e]), scale, -Lr));
+              if (!kCol && e >= valid) p = 0.f;
+              const float gg = load_g ? __uint_as_float(rg[e]) * scale : 0.f;
+              const float dp = __uint_as_float(rp[e]);
+              const float r = load_r ? __uint_as_float(rr[e]) : 0.f;
+              const float gp = (dp - Dr) * gg - Er * dp + r;
+              v_p[x] = p;
+              v_ds[x] = p * (dp - Dr);
+              v_a[x] = p * (gg - Er);
+              v_gs[x] = p * (gp - Tr);
+            }
+            pgs[u >> 1] = pack2<T>(v_gs[0], v_gs[1]);
+            pds[u >> 1] = pack2<T>(v_ds[0], v_ds[1]);
+            pa[u >> 1] = pack2<T>(v_a[0], v_a[1]);
+            pp[u >> 1] = pack2<T>(v_p[0], v_p[1]);
+          }
+          tmem_st8(tp + (c >> 1), pgs);
+          tmem_st8(tp + 32 + (c >> 1), pds);
+          tmem_st8(tp + 64 + (c >> 1), pa);
+          if (!kCol) tmem_st8(tp + 96 + (c >> 1), pp);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full);
+      }
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, static_cast<uint32_t>(li) & 1, 563, abort));
+      if (!ok) break;
+      tc_fence_after();
+      // Warpgroup 0 stores the first output (hQ / hK, times scale), warpgroup 1 the second (hdO / hV).
+      T* dst = row_ok ? (w == 0 ? out0 : out1) + grow * 64 : nullptr;
+      store_cols_from_tmem<T, 64>(tmem + lane_off + (w == 0 ? 384 : 448), 0, w == 0 ? scale : 1.f, dst);
+      tc_fence_before();
+      mbar_arrive(&acc_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+}  // namespace ebr
