@@ -444,11 +444,11 @@ int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, 
                                                                  static_cast<const T*>(o), lsef, stats, BH, Hi, Ni, sc,
                                                                  flags);
   if ((s = check_launch("tc_bob_stats_kernel"))) return s;
-  tc_bob_out_kernel<T, false><<<grid, LR::kThreads, LR::kSmem, st>>>(tq, tdo, tgq, tq, tk64, tv64, tgk64, tgv64, lsef,
+  tc_bob_out_kernel<T, false><<<grid, LR::kThreads, LR::kSmem, st>>>(tq, tdo, tgq, tq, tk64, tgk64, tv64, tgv64, lsef,
                                                                      stats, static_cast<T*>(hq), static_cast<T*>(hdo),
                                                                      BH, Hi, Ni, sc, flags);
   if ((s = check_launch("tc_bob_out_kernel<rows>"))) return s;
-  tc_bob_out_kernel<T, true><<<grid, LC::kThreads, LC::kSmem, st>>>(tk, tv, tgk, tgv, tq64, tdo64, tgq64, tq64, lsef,
+  tc_bob_out_kernel<T, true><<<grid, LC::kThreads, LC::kSmem, st>>>(tk, tv, tgk, tgv, tq64, tgq64, tdo64, tq64, lsef,
                                                                     stats, static_cast<T*>(hk), static_cast<T*>(hv),
                                                                     BH, Hi, Ni, sc, flags);
   return check_launch("tc_bob_out_kernel<cols>");

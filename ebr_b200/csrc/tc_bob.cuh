@@ -14,8 +14,12 @@
 //   warp 8     TMA producer: the item's 128-row tiles (two buffers), the streamed 64-row tiles (a three-stage ring)
 //              and, in the column pass, each step's lse / D / E / T;
 //   warp 9     MMA issuer (one thread).
+// Score products that share an operand run as one N = 128 product over two adjacent ring tiles: Q [K; gK]^T gives S
+// and Q gK^T side by side, gQ K^T accumulates onto the second half (G), dO [V; gV]^T gives dP and R (the column pass:
+// K [Q; gQ]^T, then gK Q^T onto G^T; V dO^T and gV dO^T). This reads each 128-row operand from shared memory once
+// instead of twice, which is what limits the N = 64 products.
 // Tensor memory (512 columns):
-//   statistics pass: two score buffers of 256 columns (S, dP, G, R at +0, +64, +128, +192); step g uses buffer g % 2,
+//   statistics pass: two score buffers of 256 columns (S, G, dP, R at +0, +64, +128, +192); step g uses buffer g % 2,
 //     so the products of step g + 1 run while the compute warps read step g;
 //   output passes: one score buffer [0, 256), the 16-bit tiles [256, 384) (four of 32 columns: 64 keys as pairs), the
 //     two accumulators in [384, 448) and [448, 512). A step's scores are released as soon as the compute warps have
@@ -34,7 +38,7 @@ struct BobSplitLayout {
   static constexpr int kItemBufs = 2;
   static constexpr int kStages = 3;
   static constexpr int kItemTiles = kCol ? 4 : 3;  // row passes: Q, dO, gQ; column pass: K, V, gK, gV
-  static constexpr int kRingTiles = kCol ? 3 : 4;  // row passes: K, V, gK, gV; column pass: Q, dO, gQ
+  static constexpr int kRingTiles = kCol ? 3 : 4;  // row passes: K, gK, V, gV; column pass: Q, gQ, dO
   static constexpr uint32_t kItemBytes = kItemTiles * kBig;
   static constexpr uint32_t kStageBytes = kRingTiles * kSmall;
   static constexpr uint32_t kRing = kItemBufs * kItemBytes;
@@ -48,24 +52,34 @@ struct BobSplitLayout {
   static constexpr int kThreads = 320;
 };
 
-// The score products of one step (M = 128, N = 64, K = 64), all K-major: a* are the 128-row item tiles, b* the 64-row
-// ring tiles (row passes: a = Q, dO, gQ and b = K, V, gK, gV; column pass: a = K, V, gK, gV and b = Q, dO, gQ). The
-// caller maps them so that S = a0 b0^T, dP = a1 b1^T, G = ag0 bg0^T + ag1 bg1^T, R = ar br^T.
-__device__ __forceinline__ void bob_scores(uint32_t t0, const unsigned char* aS, const unsigned char* bS,
-                                           const unsigned char* aP, const unsigned char* bP,
-                                           const unsigned char* aG0, const unsigned char* bG0,
-                                           const unsigned char* aG1, const unsigned char* bG1,
-                                           const unsigned char* aR, const unsigned char* bR, bool g0, bool g1, bool r,
-                                           uint32_t idesc) {
-  constexpr uint32_t kSmall = 64u * 128u;
+// The score products of one step into S, G, dP, R = t0 + 0, 64, 128, 192 (M = 128, K = 64, all K-major), from SW128
+// descriptors of the tiles' first K columns (K step kk adds 32 bytes, 2 in the descriptor's address field).
+// Row passes: a = Q, dO, gQ (128-row item tiles); bk / bv = the ring tiles K and V, each followed by gK / gV.
+__device__ __forceinline__ void bob_scores_rows(uint32_t t0, uint64_t aq, uint64_t ado, uint64_t agq, uint64_t bk,
+                                                uint64_t bv, bool has_gq, bool has_gk, bool has_gv, bool bf16) {
+  const uint32_t id64 = idesc_f16(bf16, 0, 0, 128, 64), id128 = idesc_f16(bf16, 0, 0, 128, 128);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const uint32_t acc = kk > 0 ? 1u : 0u;
-    mma_ss(t0, desc_kmajor(aS, kk), desc_kmajor_r(bS, kk, kSmall), idesc, acc);
-    mma_ss(t0 + 64, desc_kmajor(aP, kk), desc_kmajor_r(bP, kk, kSmall), idesc, acc);
-    if (g0) mma_ss(t0 + 128, desc_kmajor(aG0, kk), desc_kmajor_r(bG0, kk, kSmall), idesc, acc);
-    if (g1) mma_ss(t0 + 128, desc_kmajor(aG1, kk), desc_kmajor_r(bG1, kk, kSmall), idesc, (g0 || kk > 0) ? 1u : 0u);
-    if (r) mma_ss(t0 + 192, desc_kmajor(aR, kk), desc_kmajor_r(bR, kk, kSmall), idesc, acc);
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    mma_ss(t0, aq + o, bk + o, has_gk ? id128 : id64, acc);           // [S | Q gK^T] = Q [K; gK]^T
+    if (has_gq) mma_ss(t0 + 64, agq + o, bk + o, id64, (has_gk || kk > 0) ? 1u : 0u);  // G += gQ K^T
+    mma_ss(t0 + 128, ado + o, bv + o, has_gv ? id128 : id64, acc);   // [dP | R] = dO [V; gV]^T
+  }
+}
+// Column pass: a = K, V, gK, gV (item tiles); bq = the ring tile Q, followed by gQ; bdo = dO.
+__device__ __forceinline__ void bob_scores_cols(uint32_t t0, uint64_t ak, uint64_t av, uint64_t agk, uint64_t agv,
+                                                uint64_t bq, uint64_t bdo, bool has_gq, bool has_gk, bool has_gv,
+                                                bool bf16) {
+  const uint32_t id64 = idesc_f16(bf16, 0, 0, 128, 64), id128 = idesc_f16(bf16, 0, 0, 128, 128);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint32_t acc = kk > 0 ? 1u : 0u;
+    const uint64_t o = static_cast<uint64_t>(2 * kk);
+    mma_ss(t0, ak + o, bq + o, has_gq ? id128 : id64, acc);           // [S^T | K gQ^T] = K [Q; gQ]^T
+    if (has_gk) mma_ss(t0 + 64, agk + o, bq + o, id64, (has_gq || kk > 0) ? 1u : 0u);  // G^T += gK Q^T
+    mma_ss(t0 + 128, av + o, bdo + o, id64, acc);                     // dP^T = V dO^T
+    if (has_gv) mma_ss(t0 + 192, agv + o, bdo + o, id64, acc);        // R^T = gV dO^T
   }
 }
 
@@ -96,7 +110,7 @@ __global__ void __launch_bounds__(320, 1)
   const int64_t rows_total = static_cast<int64_t>(BH) * N;
   const bool has_gq = flags & 1u, has_gk = flags & 2u, has_gv = flags & 4u;
   auto item = [&](int b, int i) { return smem + b * L::kItemBytes + i * L::kBig; };                // 0 Q 1 dO 2 gQ
-  auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };  // 0 K 1 V 2 gK 3 gV
+  auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };  // 0 K 1 gK 2 V 3 gV
   float* part = reinterpret_cast<float*>(smem + L::kAux);
 
   if (tid == 0) {
@@ -151,8 +165,8 @@ __global__ void __launch_bounds__(320, 1)
           if (!ok) break;
           mbar_arrive_expect_tx(&rg_full[s], ring_bytes);
           tma_load_4d(ring(s, 0), &tk64, &rg_full[s], 0, j * 64, h, b);
-          tma_load_4d(ring(s, 1), &tv64, &rg_full[s], 0, j * 64, h, b);
-          if (has_gk) tma_load_4d(ring(s, 2), &tgk64, &rg_full[s], 0, j * 64, h, b);
+          if (has_gk) tma_load_4d(ring(s, 1), &tgk64, &rg_full[s], 0, j * 64, h, b);
+          tma_load_4d(ring(s, 2), &tv64, &rg_full[s], 0, j * 64, h, b);
           if (has_gv) tma_load_4d(ring(s, 3), &tgv64, &rg_full[s], 0, j * 64, h, b);
         }
       }
@@ -160,13 +174,17 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdNN = idesc_f16(is_bf16<T>(), 0, 0, 128, 64);
+      // K-major descriptor of a tile at byte offset `off` of the aligned shared block.
+      const uint64_t d0 = sw128_desc(smem_u32(smem), 16u, 1024u);
+      auto da = [&](int b, int i) { return d0 + ((b * L::kItemBytes + i * L::kBig) >> 4); };
+      auto db = [&](int s, int i) { return d0 + ((L::kRing + s * L::kStageBytes + i * L::kSmall) >> 4); };
       uint32_t g = 0;
       bool ok = true;
       int64_t li = 0;
       for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
         const int ib = static_cast<int>(li % NI);
         ok = mbar_wait_or_abort(&it_full[ib], static_cast<uint32_t>(li / NI) & 1, 521, abort);
+        const uint64_t aq = da(ib, 0), ado = da(ib, 1), agq = da(ib, 2);
         for (int j = 0; j < n_ks && ok; ++j, ++g) {
           const int s = static_cast<int>(g % NS), b = static_cast<int>(g & 1);
           // Buffer b is free once the compute warps have read its previous step (the first use passes at once).
@@ -174,8 +192,7 @@ __global__ void __launch_bounds__(320, 1)
           if (ok) ok = mbar_wait_or_abort(&rg_full[s], (g / NS) & 1, 523, abort);
           if (!ok) break;
           tc_fence_after();
-          bob_scores(tmem + 256 * b, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 2), ring(s, 0),
-                     item(ib, 0), ring(s, 2), item(ib, 1), ring(s, 3), has_gq, has_gk, has_gv, kIdNN);
+          bob_scores_rows(tmem + 256 * b, aq, ado, agq, db(s, 0), db(s, 2), has_gq, has_gk, has_gv, is_bf16<T>());
           mma_commit(&s_full[b]);
           mma_commit(&rg_empty[s]);
           if (j == n_ks - 1) mma_commit(&it_empty[ib]);
@@ -209,8 +226,8 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t t0 = tmem + lane_off + 256 * b + col0;
         uint32_t rs[32], rp[32], rg[32], rr[32];
         tmem_ld32(t0, rs);
-        tmem_ld32(t0 + 64, rp);
-        if (has_gq || has_gk) tmem_ld32(t0 + 128, rg);
+        if (has_gq || has_gk) tmem_ld32(t0 + 64, rg);
+        tmem_ld32(t0 + 128, rp);
         if (has_gv) tmem_ld32(t0 + 192, rr);
         tmem_wait_ld_regs(rs);
         tmem_wait_ld_regs(rp);
@@ -293,10 +310,10 @@ __global__ void __launch_bounds__(320, 1)
   const int64_t items = static_cast<int64_t>(BH) * n_it;
   const int64_t rows_total = static_cast<int64_t>(BH) * N;
   const bool has_gq = flags & 1u, has_gk = flags & 2u, has_gv = flags & 4u;
-  // Which optional tiles exist: row pass items (Q, dO, gQ) and ring (K, V, gK, gV); column pass items (K, V, gK, gV)
-  // and ring (Q, dO, gQ).
+  // Which optional tiles exist: row pass items (Q, dO, gQ) and ring (K, gK, V, gV); column pass items (K, V, gK, gV)
+  // and ring (Q, gQ, dO).
   const bool item_has[4] = {true, true, kCol ? has_gk : has_gq, kCol ? has_gv : false};
-  const bool ring_has[4] = {true, true, kCol ? has_gq : has_gk, kCol ? false : has_gv};
+  const bool ring_has[4] = {true, kCol ? has_gq : has_gk, true, kCol ? false : has_gv};
   auto item = [&](int b, int i) { return smem + b * L::kItemBytes + i * L::kBig; };
   auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };
   float* stg = reinterpret_cast<float*>(smem + L::kAux);  // column pass: [stage][64][lse, D, E, T]
@@ -390,9 +407,14 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdNN = idesc_f16(is_bf16<T>(), 0, 0, 128, 64);
       constexpr uint32_t kIdKM = idesc_f16(is_bf16<T>(), 0, 1, 128, 64);
       const uint32_t tPk = tmem + 256, tAcc0 = tmem + 384, tAcc1 = tmem + 448;
+      // Descriptors of a tile at byte offset `off` of the aligned shared block: K-major (score products) and MN-major
+      // (accumulating products, B = the ring tile read with its 64 columns as N; K step kk = 16 rows = 2048 bytes).
+      const uint64_t d0 = sw128_desc(smem_u32(smem), 16u, 1024u);
+      const uint64_t m0 = sw128_desc(smem_u32(smem), L::kSmall, 1024u);
+      auto da = [&](int b, int i) { return d0 + ((b * L::kItemBytes + i * L::kBig) >> 4); };
+      auto rof = [&](int s, int i) { return static_cast<uint64_t>((L::kRing + s * L::kStageBytes + i * L::kSmall) >> 4); };
       uint32_t g = 0;
       bool ok = true;
       // The accumulating products of step g are issued after the score products of step g + 1: the step waiting for
@@ -408,22 +430,18 @@ __global__ void __launch_bounds__(320, 1)
         if (pj == 0 && pli > 0 && !mbar_wait_or_abort(&acc_free, static_cast<uint32_t>(pli - 1) & 1, 554, abort))
           return false;
         tc_fence_after();
+        const uint64_t b0 = m0 + rof(ps, 0), b1 = m0 + rof(ps, 1), b2 = m0 + rof(ps, 2), b3 = m0 + rof(ps, 3);
+        const uint32_t first = pj > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t acc0 = (pj > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t acc0 = kk > 0 ? 1u : first;
           const uint32_t a = tPk + kk * 8;
-          if (!kCol) {
-            // hQ += gS K (+ dS gK); hdO += A V (+ P gV)
-            mma_ts(tAcc0, a, desc_mnmajor_r(ring(ps, 0), kk, L::kSmall), kIdKM, acc0);
-            if (has_gk) mma_ts(tAcc0, a + 32, desc_mnmajor_r(ring(ps, 2), kk, L::kSmall), kIdKM, 1u);
-            mma_ts(tAcc1, a + 64, desc_mnmajor_r(ring(ps, 1), kk, L::kSmall), kIdKM, acc0);
-            if (has_gv) mma_ts(tAcc1, a + 96, desc_mnmajor_r(ring(ps, 3), kk, L::kSmall), kIdKM, 1u);
-          } else {
-            // hK += gS^T Q (+ dS^T gQ); hV += A^T dO
-            mma_ts(tAcc0, a, desc_mnmajor_r(ring(ps, 0), kk, L::kSmall), kIdKM, acc0);
-            if (has_gq) mma_ts(tAcc0, a + 32, desc_mnmajor_r(ring(ps, 2), kk, L::kSmall), kIdKM, 1u);
-            mma_ts(tAcc1, a + 64, desc_mnmajor_r(ring(ps, 1), kk, L::kSmall), kIdKM, acc0);
-          }
+          const uint64_t o = static_cast<uint64_t>(128 * kk);
+          // Row pass: hQ += gS K (+ dS gK), hdO += A V (+ P gV). Column pass: hK += gS^T Q (+ dS^T gQ), hV += A^T dO.
+          mma_ts(tAcc0, a, b0 + o, kIdKM, acc0);
+          if (kCol ? has_gq : has_gk) mma_ts(tAcc0, a + 32, b1 + o, kIdKM, 1u);
+          mma_ts(tAcc1, a + 64, b2 + o, kIdKM, acc0);
+          if (!kCol && has_gv) mma_ts(tAcc1, a + 96, b3 + o, kIdKM, 1u);
         }
         mma_commit(&pk_free);
         mma_commit(&rg_empty[ps]);
@@ -441,12 +459,12 @@ __global__ void __launch_bounds__(320, 1)
           if (ok) ok = mbar_wait_or_abort(&s_free, (g & 1) ^ 1, 555, abort);
           if (!ok) break;
           tc_fence_after();
+          const uint64_t a0 = da(ib, 0), a1 = da(ib, 1), a2 = da(ib, 2), a3 = da(ib, 3);
+          const uint64_t r0 = d0 + rof(s, 0), r2 = d0 + rof(s, 2);
           if (!kCol)
-            bob_scores(tmem, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 2), ring(s, 0), item(ib, 0),
-                       ring(s, 2), item(ib, 1), ring(s, 3), has_gq, has_gk, has_gv, kIdNN);
+            bob_scores_rows(tmem, a0, a1, a2, r0, r2, has_gq, has_gk, has_gv, is_bf16<T>());
           else
-            bob_scores(tmem, item(ib, 0), ring(s, 0), item(ib, 1), ring(s, 1), item(ib, 0), ring(s, 2), item(ib, 2),
-                       ring(s, 0), item(ib, 3), ring(s, 1), has_gq, has_gk, has_gv, kIdNN);
+            bob_scores_cols(tmem, a0, a1, a2, a3, r0, r2, has_gq, has_gk, has_gv, is_bf16<T>());
           mma_commit(&s_full);
           if (j == n_st - 1) mma_commit(&it_empty[ib]);
           if (pend) ok = accumulate();
@@ -489,8 +507,8 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t rs[32], rp[32], rg[32], rr[32];
         const bool load_g = has_gq || has_gk, load_r = has_gv;
         tmem_ld32(t0, rs);
-        tmem_ld32(t0 + 64, rp);
-        if (load_g) tmem_ld32(t0 + 128, rg);
+        if (load_g) tmem_ld32(t0 + 64, rg);
+        tmem_ld32(t0 + 128, rp);
         if (load_r) tmem_ld32(t0 + 192, rr);
         tmem_wait_ld_regs(rs);
         tmem_wait_ld_regs(rp);
