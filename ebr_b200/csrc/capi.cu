@@ -404,8 +404,9 @@ int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, 
                         const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
                         void* hq, void* hk, void* hv, void* hdo, void* scratch, cudaStream_t st) {
   constexpr int D = 64;
-  using LR = BobSplitLayout<false>;
-  using LC = BobSplitLayout<true>;
+  using L0 = BobSplitLayout<0>;
+  using LR = BobSplitLayout<1>;
+  using LC = BobSplitLayout<2>;
   const bool has[3] = {gq && gq->data, gk && gk->data, gv && gv->data};
   const uint32_t flags = (has[0] ? 1u : 0u) | (has[1] ? 2u : 0u) | (has[2] ? 4u : 0u);
   CUtensorMap tq, tdo, tgq, tk, tv, tgk, tgv, tq64, tdo64, tgq64, tk64, tv64, tgk64, tgv64;
@@ -429,7 +430,7 @@ int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, 
   const void* f0 = reinterpret_cast<const void*>(tc_bob_stats_kernel<T>);
   const void* f1 = reinterpret_cast<const void*>(tc_bob_out_kernel<T, false>);
   const void* f2 = reinterpret_cast<const void*>(tc_bob_out_kernel<T, true>);
-  int s = prepare_tc_kernel(f0, device, LR::kSmem, LR::kTmemCols, LR::kThreads);
+  int s = prepare_tc_kernel(f0, device, L0::kSmem, L0::kTmemCols, L0::kThreads);
   if (s || (s = prepare_tc_kernel(f1, device, LR::kSmem, LR::kTmemCols, LR::kThreads)) ||
       (s = prepare_tc_kernel(f2, device, LC::kSmem, LC::kTmemCols, LC::kThreads)))
     return s;
@@ -440,7 +441,7 @@ int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, 
   const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
   const float sc = static_cast<float>(scale);
   const float* lsef = static_cast<const float*>(lse);
-  tc_bob_stats_kernel<T><<<grid, LR::kThreads, LR::kSmem, st>>>(tq, tdo, tgq, tk64, tv64, tgk64, tgv64,
+  tc_bob_stats_kernel<T><<<grid, L0::kThreads, L0::kSmem, st>>>(tq, tdo, tgq, tk64, tv64, tgk64, tgv64,
                                                                  static_cast<const T*>(o), lsef, stats, BH, Hi, Ni, sc,
                                                                  flags);
   if ((s = check_launch("tc_bob_stats_kernel"))) return s;

@@ -31,21 +31,23 @@
 
 namespace ebr {
 
-template <bool kCol>
+// kPass: 0 statistics, 1 row outputs, 2 column outputs.
+template <int kPass>
 struct BobSplitLayout {
+  static constexpr bool kCol = kPass == 2;
   static constexpr uint32_t kBig = kHalfBytes;   // [128 x 64] 16-bit tile
   static constexpr uint32_t kSmall = 64u * 128u;  // [64 x 64] 16-bit tile
   static constexpr int kItemBufs = 2;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = kCol ? 3 : 4;
   static constexpr int kItemTiles = kCol ? 4 : 3;  // row passes: Q, dO, gQ; column pass: K, V, gK, gV
   static constexpr int kRingTiles = kCol ? 3 : 4;  // row passes: K, gK, V, gV; column pass: Q, gQ, dO
   static constexpr uint32_t kItemBytes = kItemTiles * kBig;
   static constexpr uint32_t kStageBytes = kRingTiles * kSmall;
   static constexpr uint32_t kRing = kItemBufs * kItemBytes;
-  // Row passes: the second warpgroup's partial row sums, [2 slots][4 sums][128 rows] floats.
-  // Column pass: each stage's per-query (lse, D, E, T), [stage][64 queries][4] floats.
+  // Column pass: each stage's per-query (lse, D, E, T), [stage][64 queries][4] floats. (The statistics pass exchanges
+  // its partial row sums through the item's spent gQ tile.)
   static constexpr uint32_t kAux = kRing + kStages * kStageBytes;
-  static constexpr uint32_t kAuxBytes = kCol ? kStages * 64 * 4 * 4 : 2 * 4 * 128 * 4;
+  static constexpr uint32_t kAuxBytes = kCol ? kStages * 64 * 4 * 4 : 0;
   static constexpr uint32_t kBytes = kAux + kAuxBytes;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
@@ -95,12 +97,11 @@ __global__ void __launch_bounds__(320, 1)
                         const __grid_constant__ CUtensorMap tgv64, const T* __restrict__ o,
                         const float* __restrict__ lse, float* __restrict__ stats, int BH, int H, int N, float scale,
                         uint32_t flags) {
-  using L = BobSplitLayout<false>;
+  using L = BobSplitLayout<0>;
   constexpr int NS = L::kStages, NI = L::kItemBufs;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
-  __shared__ uint64_t it_full[NI], it_empty[NI], rg_full[NS], rg_empty[NS], s_full[2], s_free[2], part_full[2],
-      part_empty[2];
+  __shared__ uint64_t it_full[NI], it_empty[NI], rg_full[NS], rg_empty[NS], s_full[2], s_free[2], part_full[NI];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -111,12 +112,13 @@ __global__ void __launch_bounds__(320, 1)
   const bool has_gq = flags & 1u, has_gk = flags & 2u, has_gv = flags & 4u;
   auto item = [&](int b, int i) { return smem + b * L::kItemBytes + i * L::kBig; };                // 0 Q 1 dO 2 gQ
   auto ring = [&](int s, int i) { return smem + L::kRing + s * L::kStageBytes + i * L::kSmall; };  // 0 K 1 gK 2 V 3 gV
-  float* part = reinterpret_cast<float*>(smem + L::kAux);
 
   if (tid == 0) {
     for (int i = 0; i < NI; ++i) {
       mbar_init(&it_full[i], 1);
-      mbar_init(&it_empty[i], 1 + 256);  // the MMA warp's commit + every compute thread once it has read dO
+      // The MMA warp's commit + every compute thread once the item's partial sums have been exchanged.
+      mbar_init(&it_empty[i], 1 + 256);
+      mbar_init(&part_full[i], 128);
     }
     for (int i = 0; i < NS; ++i) {
       mbar_init(&rg_full[i], 1);
@@ -125,8 +127,6 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 256);
-      mbar_init(&part_full[i], 128);
-      mbar_init(&part_empty[i], 128);
     }
     abort_flag = 0;
     fence_barrier_init();
@@ -216,7 +216,6 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&it_full[ib], static_cast<uint32_t>(li / NI) & 1, 531, abort));
       if (!ok) break;
       const float Di = row_ok ? row_delta<T, 64>(item(ib, 1), lrow, o + grow * 64) : 0.f;
-      mbar_arrive(&it_empty[ib]);
       float e_ = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
       for (int j = 0; j < n_ks; ++j, ++g) {
         const int b = static_cast<int>(g & 1);
@@ -249,32 +248,31 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (!ok) break;
-      // The two halves of each row meet in shared memory (slot li % 2): warpgroup 1 writes, warpgroup 0 adds.
-      const int slot = static_cast<int>(li & 1);
-      const uint32_t use = static_cast<uint32_t>(li >> 1) & 1;
-      float* ps = part + slot * 512;
+      // The two halves of each row meet in the item's gQ tile, which no product reads any more (the last step's scores
+      // have completed): warpgroup 1 writes its sums, warpgroup 0 adds them; both then release the item buffer.
+      float* ps = reinterpret_cast<float*>(item(ib, 2));
       if (w == 1) {
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&part_empty[slot], use ^ 1, 533, abort));
-        if (!ok) break;
         ps[lrow] = e_;
         ps[128 + lrow] = c1;
         ps[256 + lrow] = c2;
         ps[384 + lrow] = c3;
-        mbar_arrive(&part_full[slot]);
+        mbar_arrive(&part_full[ib]);
       } else {
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&part_full[slot], use, 534, abort));
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&part_full[ib], static_cast<uint32_t>(li / NI) & 1, 534, abort));
         if (!ok) break;
         e_ += ps[lrow];
         c1 += ps[128 + lrow];
         c2 += ps[256 + lrow];
         c3 += ps[384 + lrow];
-        mbar_arrive(&part_empty[slot]);
         if (row_ok) {
           stats[grow] = Di;
           stats[rows_total + grow] = e_;
           stats[2 * rows_total + grow] = c1 - e_ * c2 + c3;
         }
       }
+      // The generic-proxy accesses above come before the next TMA write into this buffer.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&it_empty[ib]);
     }
   }
   tc_fence_before();
@@ -296,7 +294,7 @@ __global__ void __launch_bounds__(320, 1)
                       const __grid_constant__ CUtensorMap tb2, const __grid_constant__ CUtensorMap tb3,
                       const float* __restrict__ lse, const float* __restrict__ stats, T* __restrict__ out0,
                       T* __restrict__ out1, int BH, int H, int N, float scale, uint32_t flags) {
-  using L = BobSplitLayout<kCol>;
+  using L = BobSplitLayout<kCol ? 2 : 1>;
   constexpr int NS = L::kStages, NI = L::kItemBufs;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
