@@ -9,6 +9,7 @@
 
 #include "../../include/ebr_layers.h"
 #include "layers.cuh"
+#include "qkv_rope.cuh"
 
 namespace {
 
@@ -68,6 +69,23 @@ int check_rope_shape(int64_t B, int64_t N, int64_t H, int64_t D) {
   if (D < 4 || D % 4 != 0 || D > 4096) return set_error(EBR_ERR_SHAPE, "head dim must be a multiple of 4 in [4, 4096]%s%s");
   if (H > (1 << 20) || N > (int64_t{1} << 31) || B > (int64_t{1} << 31))
     return set_error(EBR_ERR_SHAPE, "size too large%s%s");
+  return EBR_OK;
+}
+
+// 2-D TMA map over a row-major [rows, cols] 16-bit matrix (row stride in elements), 64-column x box_rows boxes,
+// 128-byte swizzle; rows past the end read as zeros.
+int make_matrix_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t cols, int64_t row_stride,
+                    uint32_t box_rows) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled failed%s%s");
   return EBR_OK;
 }
 
@@ -285,6 +303,48 @@ int ebr_descent_step(int dtype, int64_t rows, int64_t row_elems, double alpha, d
     }
     return check_launch("sphere");
   });
+}
+
+int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, int64_t C, const void* x,
+                       int64_t x_stride, const void* w, const float* cos_table, const float* sin_table,
+                       const float* qscale, void* q, void* k, void* v, void* stream) {
+  if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
+    return set_error(EBR_ERR_DTYPE, "qkv_rope_split: bfloat16 or float16 only%s%s");
+  if (B < 0 || N < 0 || H < 1 || C < 1 || (D != 64 && D != 128) || (H * D) % 256 != 0 || C % 64 != 0 ||
+      N > INT32_MAX || H * D > (INT32_MAX / 3) || C > INT32_MAX)
+    return set_error(EBR_ERR_SHAPE, "qkv_rope_split: needs D = 64 or 128, H D a multiple of 256, C a multiple of 64%s%s");
+  if (B * N == 0) return EBR_OK;
+  if (!x || !w || !cos_table || !sin_table || !q || !k || !v)
+    return set_error(EBR_ERR_NULL, "qkv_rope_split: NULL pointer%s%s");
+  if (x_stride < C || x_stride % 8 != 0 || !all_aligned16({x, w, q, k, v, cos_table, sin_table}))
+    return set_error(EBR_ERR_STRIDE, "qkv_rope_split: x rows need a stride >= C, a multiple of 8 elements, and 16-byte "
+                                     "aligned pointers%s%s");
+  int device = 0;
+  int rc = check_device(&device);
+  if (rc != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  using L = ebr::QkvRopeLayout;
+  const int64_t M = B * N;
+  CUtensorMap tx, tw;
+  if ((rc = make_matrix_map(&tx, x, dtype, M, C, x_stride, L::kBM)) != EBR_OK) return rc;
+  if ((rc = make_matrix_map(&tw, w, dtype, 3 * H * D, C, C, L::kBN)) != EBR_OK) return rc;
+  const int64_t tiles = ((M + L::kBM - 1) / L::kBM) * (3 * H * D / L::kBN);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
+  auto launch = [&](auto kernel, auto* out_tag) -> int {
+    using T = std::remove_pointer_t<decltype(out_tag)>;
+    if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))
+      return rc;
+    kernel<<<grid, L::kThreads, L::kSmem, st>>>(tx, tw, M, static_cast<int>(C), static_cast<int>(N), static_cast<int>(H),
+                                                cos_table, sin_table, qscale, static_cast<T*>(q), static_cast<T*>(k),
+                                                static_cast<T*>(v));
+    return check_launch("tc_qkv_rope_kernel");
+  };
+  if (dtype == EBR_BFLOAT16)
+    return D == 64 ? launch(ebr::tc_qkv_rope_kernel<__nv_bfloat16, 64>, static_cast<__nv_bfloat16*>(nullptr))
+                   : launch(ebr::tc_qkv_rope_kernel<__nv_bfloat16, 128>, static_cast<__nv_bfloat16*>(nullptr));
+  return D == 64 ? launch(ebr::tc_qkv_rope_kernel<__half, 64>, static_cast<__half*>(nullptr))
+                 : launch(ebr::tc_qkv_rope_kernel<__half, 128>, static_cast<__half*>(nullptr));
 }
 
 }  // extern "C"

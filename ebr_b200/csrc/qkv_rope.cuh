@@ -1,0 +1,242 @@
+// qkv_rope.cuh: the qkv projection of the energy network's attention as a tensor-core GEMM whose epilogue is the 2D-RoPE
+// split: q, k, v = split(x W^T) with the rotation, the per-head temperature and the head-major layout applied to each
+// accumulator tile on its way out, so the [B, N, 3 H D] projection never reaches memory.
+//
+// One persistent CTA per SM; a tile is 128 rows of x (tokens) by 256 output columns (4 heads at D = 64, 2 at D = 128,
+// all of one of q / k / v since H D is a multiple of 256). Tiles are numbered with the 256-column blocks fastest, so
+// the CTAs working at one time read the same rows of x (from L2) against all of W. Roles (320 threads):
+//   warp 8     TMA producer: per 64-wide K block, the x tile [128 x 64] and the W tile [256 x 64] (both K-major,
+//              128-byte swizzle) into a 4-stage ring;
+//   warp 9     MMA issuer: 4 x tcgen05.mma M128 N256 K16 per K block into one of two 256-column accumulators in TMEM,
+//              so the epilogue of a tile overlaps the products of the next;
+//   warps 0-7  epilogue: warp w owns TMEM lanes [32 (w % 4), +32) (one token row per thread) and, in every head of
+//              the tile, the half of the columns that warpgroup w / 4 rotates together (see qkv_slot_start). It rounds
+//              the fp32 accumulators to the I/O type (the value the unfused GEMM writes), rotates q and k as
+//              ebr_rope_split does -- t' = round(t cos + quarter_swap(t) sin), multiplies and adds rounded separately;
+//              q' = round(q' qscale[h]) when a temperature is given -- and stores to q / k / v [B, H, N, D]
+//              (32-byte runs of a head row).
+// The GEMM sums in fp32 in K-steps of 16 where cuBLAS may order the sum differently, so a projection value can differ
+// from the unfused path's in the last bit of the I/O type; the rotation on equal inputs is bit-identical.
+// The reference's F.linear + rope_split (models/attention.py:233-242, models/fused_attn/rope_split.py:31-50, :77-82).
+#pragma once
+
+#include "layers.cuh"
+#include "tc_attn.cuh"
+
+namespace ebr {
+
+struct QkvRopeLayout {
+  static constexpr int kBM = 128, kBN = 256, kBK = 64;
+  static constexpr uint32_t kATile = kBM * kBK * 2;  // 16 KB
+  static constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KB
+  static constexpr int kStages = 4;
+  static constexpr uint32_t kStage = kATile + kBTile;
+  static constexpr uint32_t kBytes = kStages * kStage;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kThreads = 320;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Epilogue slots: the 32 columns of a head that one rotation pairs with each other, elements [da, da + 16) and
+// [da + D / 4, da + D / 4 + 16) (quarter_swap (a, b, c, d) -> (b, a, d, c) pairs element e with e +- D / 4). At D = 64 a
+// head has two slots (da = 0, 32), at D = 128 four (da = 0, 16, 64, 80). Warpgroup g of the epilogue takes slots
+// [S g, S g + S) of every head of the tile (S = 1 at D = 64, 2 at D = 128), so a thread loads its token's table values
+// for a slot once per tile and applies them to every head.
+template <int D>
+__device__ __forceinline__ int qkv_slot_start(int slot) {
+  return (slot / (D / 64)) * (D / 2) + (slot % (D / 64)) * 16;
+}
+
+// One slot of two heads of a token row: accumulators (fp32) at TMEM columns ta0 / ta1 + da and + da + D / 4.
+template <typename T, int D>
+__device__ __forceinline__ void qkv_rope_slot2(uint32_t ta0, uint32_t ta1, int da, bool rotate, bool scale_q,
+                                               float qs0, float qs1, const float (&tab)[64], bool row_ok, T* dst0,
+                                               T* dst1) {
+  using layers::add_rn;
+  using layers::mul_rn;
+  using layers::rnd;
+  constexpr int kQ = D / 4;
+  uint32_t r[4][16];
+  tmem_ld16(ta0 + da, r[0]);
+  tmem_ld16(ta0 + da + kQ, r[1]);
+  tmem_ld16(ta1 + da, r[2]);
+  tmem_ld16(ta1 + da + kQ, r[3]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float a[16], b[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      a[i] = rnd<T>(__uint_as_float(r[2 * hh][i]));
+      b[i] = rnd<T>(__uint_as_float(r[2 * hh + 1][i]));
+    }
+    if (rotate) {
+      const float qs = hh == 0 ? qs0 : qs1;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        // tab: cos of the first 16 elements, sin of them, cos of their partners, sin of the partners
+        const float oa = rnd<T>(add_rn(mul_rn(a[i], tab[i]), mul_rn(b[i], tab[16 + i])));
+        const float ob = rnd<T>(add_rn(mul_rn(b[i], tab[32 + i]), mul_rn(a[i], tab[48 + i])));
+        a[i] = scale_q ? mul_rn(oa, qs) : oa;
+        b[i] = scale_q ? mul_rn(ob, qs) : ob;
+      }
+    }
+    T* dst = hh == 0 ? dst0 : dst1;
+    if (row_ok) {
+      layers::store_c<T, 8>(dst + da, reinterpret_cast<const float(&)[8]>(a[0]));
+      layers::store_c<T, 8>(dst + da + 8, reinterpret_cast<const float(&)[8]>(a[8]));
+      layers::store_c<T, 8>(dst + da + kQ, reinterpret_cast<const float(&)[8]>(b[0]));
+      layers::store_c<T, 8>(dst + da + kQ + 8, reinterpret_cast<const float(&)[8]>(b[8]));
+    }
+  }
+}
+
+// x: [M, C] (TMA map, box 64 x 128), w: [3 H D, C] (TMA map, box 64 x 256); M = B N tokens, C % 64 == 0,
+// (H D) % 256 == 0. cos / sin: fp32 [N, D]; qscale: NULL or fp32 [H].
+template <typename T, int D>
+__global__ void __launch_bounds__(320, 1)
+    tc_qkv_rope_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw, int64_t M,
+                       int C, int N, int H, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                       const float* __restrict__ qscale, T* __restrict__ q, T* __restrict__ k, T* __restrict__ v) {
+  using L = QkvRopeLayout;
+  constexpr int NS = L::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  __shared__ uint64_t full[NS], empty[NS], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int HD = H * D, n_nt = 3 * HD / L::kBN, n_kb = C / L::kBK;
+  const int64_t n_mt = (M + L::kBM - 1) / L::kBM, tiles = n_mt * n_nt;
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 256);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tx);
+      tma_prefetch_desc(&tw);
+      uint32_t use = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int mt = static_cast<int>(t / n_nt), nt = static_cast<int>(t - static_cast<int64_t>(mt) * n_nt);
+        for (int kb = 0; kb < n_kb; ++kb, ++use) {
+          const int s = static_cast<int>(use % NS);
+          ok = mbar_wait_or_abort(&empty[s], ((use / NS) & 1) ^ 1, 611, abort);
+          if (!ok) break;
+          unsigned char* st = smem + s * L::kStage;
+          mbar_arrive_expect_tx(&full[s], L::kStage);
+          tma_load_2d(st, &tx, &full[s], kb * L::kBK, mt * L::kBM);
+          tma_load_2d(st + L::kATile, &tw, &full[s], kb * L::kBK, nt * L::kBN);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id = idesc_f16(is_bf16<T>(), 0, 0, 128, 256);
+      const uint64_t d0 = sw128_desc(smem_u32(smem), 16u, 1024u);
+      uint32_t use = 0, lt = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++lt) {
+        const uint32_t ab = lt & 1;
+        ok = mbar_wait_or_abort(&acc_empty[ab], ((lt >> 1) & 1) ^ 1, 621, abort);
+        for (int kb = 0; kb < n_kb && ok; ++kb, ++use) {
+          const int s = static_cast<int>(use % NS);
+          ok = mbar_wait_or_abort(&full[s], (use / NS) & 1, 622, abort);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t da = d0 + ((s * L::kStage) >> 4), db = da + (L::kATile >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ss(tmem + ab * 256, da + 2 * kk, db + 2 * kk, id, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[ab]);
+      }
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------------- epilogue
+    constexpr int kSlots = D / 64;          // slots per head this warpgroup takes
+    constexpr int kHeads = L::kBN / D;      // heads per tile
+    const int wq = warp & 3, grp = warp >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    uint32_t lt = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      const int mt = static_cast<int>(t / n_nt), nt = static_cast<int>(t - static_cast<int64_t>(mt) * n_nt);
+      const uint32_t ab = lt & 1;
+      const int64_t row = static_cast<int64_t>(mt) * L::kBM + wq * 32 + lane;
+      const bool row_ok = row < M;
+      const int64_t b = row_ok ? row / N : 0;
+      const int n = row_ok ? static_cast<int>(row - b * N) : 0;
+      const int sec = (nt * L::kBN) / HD, h0 = (nt * L::kBN - sec * HD) / D;  // the tile's part and first head
+      const bool rotate = sec != 2, scale_q = sec == 0 && qscale != nullptr;
+      T* base = (sec == 0 ? q : sec == 1 ? k : v) + ((b * H + h0) * N + n) * static_cast<int64_t>(D);
+      const int64_t head_stride = static_cast<int64_t>(N) * D;
+      // The first slot's table values are requested before the accumulators are waited for.
+      float tab[64];
+      auto load_tab = [&](int slot) {
+        if (!rotate) return;
+        const int da = qkv_slot_start<D>(grp * kSlots + slot);
+        const float* cs = cos_t + static_cast<int64_t>(n) * D;
+        const float* sn = sin_t + static_cast<int64_t>(n) * D;
+        layers::load_table_v<16>(cs + da, reinterpret_cast<float(&)[16]>(tab[0]));
+        layers::load_table_v<16>(sn + da, reinterpret_cast<float(&)[16]>(tab[16]));
+        layers::load_table_v<16>(cs + da + D / 4, reinterpret_cast<float(&)[16]>(tab[32]));
+        layers::load_table_v<16>(sn + da + D / 4, reinterpret_cast<float(&)[16]>(tab[48]));
+      };
+      load_tab(0);
+      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[ab], (lt >> 1) & 1, 631, abort))) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem + lane_off + ab * 256;
+#pragma unroll
+      for (int slot = 0; slot < kSlots; ++slot) {
+        if (slot > 0) load_tab(slot);
+        const int da = qkv_slot_start<D>(grp * kSlots + slot);
+#pragma unroll
+        for (int hl = 0; hl < kHeads; hl += 2) {
+          const float qs0 = scale_q ? __ldg(qscale + h0 + hl) : 1.f;
+          const float qs1 = scale_q ? __ldg(qscale + h0 + hl + 1) : 1.f;
+          qkv_rope_slot2<T, D>(tacc + hl * D, tacc + (hl + 1) * D, da, rotate, scale_q, qs0, qs1, tab, row_ok,
+                               base + hl * head_stride, base + (hl + 1) * head_stride);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+}  // namespace ebr

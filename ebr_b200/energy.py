@@ -192,12 +192,13 @@ class EnergyAttention(nn.Module):
         h, d = self.heads, self.head_dim
         temperature_applied = False
         if self.fused:
-            # One kernel: split + 2D RoPE + head-major layout (+ the temperature outside the graded window).
+            # One kernel: the projection GEMM with split + 2D RoPE + head-major layout (+ the temperature outside the
+            # graded window) as its epilogue.
             qscale = None
             if not second_order_required():
                 qscale = self.log_logit_scale.detach().exp().to(x.dtype)
                 temperature_applied = True
-            q, k, v = fl.rope_split(self.qkv(x), rope.cos_table, rope.sin_table, h, qscale)
+            q, k, v = fl.qkv_rope_split(x, self.qkv.weight.to(x.dtype), rope.cos_table, rope.sin_table, h, qscale)
         else:
             q, k, v = self.qkv(x).split([h * d] * 3, dim=-1)
             q, k, v = q.view(b, n, h, d), k.view(b, n, h, d), v.view(b, n, h, d)

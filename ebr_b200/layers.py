@@ -206,6 +206,98 @@ def rope_split(qkv: Tensor, cos: Tensor, sin: Tensor, heads: int,
     return _split(qkv, cos, sin, qscale.detach(), heads)
 
 
+# ---------------------------------------------------------------------------------------------------- qkv projection
+
+
+@torch.library.custom_op("ebr_fused::qkv_rope_split", mutates_args=())
+def qkv_rope_split_op(x: Tensor, weight: Tensor, cos: Tensor, sin: Tensor, qscale: Tensor,
+                      heads: int) -> Tuple[Tensor, Tensor, Tensor]:  # fmt: skip
+    _require_cuda(x, "qkv_rope_split")
+    b, n, c = x.shape
+    d = weight.shape[0] // (3 * heads)
+    x = x.contiguous()
+    weight = weight.to(x.dtype).contiguous()
+    q, k, v = (torch.empty((b, heads, n, d), device=x.device, dtype=x.dtype) for _ in range(3))
+    cos, sin = _table(cos, x.device), _table(sin, x.device)
+    qs, qs_ptr = _qscale_arg(qscale)
+    _native.check(
+        _native.lib().ebr_qkv_rope_split(_DTYPES[x.dtype], b, n, heads, d, c, x.data_ptr(), c, weight.data_ptr(),
+                                         cos.data_ptr(), sin.data_ptr(), qs_ptr, q.data_ptr(), k.data_ptr(),
+                                         v.data_ptr(), _stream()),  # fmt: skip
+        "qkv_rope_split",
+    )
+    return q, k, v
+
+
+@qkv_rope_split_op.register_fake
+def _(x, weight, cos, sin, qscale, heads):
+    b, n, _ = x.shape
+    d = weight.shape[0] // (3 * heads)
+    return tuple(x.new_empty((b, heads, n, d)) for _ in range(3))
+
+
+class _QkvSplit(torch.autograd.Function):
+    """Forward: the projection with the split as its epilogue. Backward: the merge (the split's exact adjoint), then
+    the projection's two products, all differentiable ops, so every higher order follows."""
+
+    @staticmethod
+    def forward(x, weight, cos, sin, qscale, heads):
+        return torch.ops.ebr_fused.qkv_rope_split(x, weight, cos, sin, qscale, heads)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        x, weight, cos, sin, qscale, heads = inputs
+        ctx.save_for_backward(x, weight, cos, sin, qscale)
+        ctx.shape = tuple(output[0].shape)
+
+    @staticmethod
+    def backward(ctx, gq, gk, gv):
+        x, weight, cos, sin, qscale = ctx.saved_tensors
+        ref = next(g for g in (gq, gk, gv) if g is not None)
+        z = None
+        if gq is None or gk is None or gv is None:
+            z = torch.zeros(ctx.shape, dtype=ref.dtype, device=ref.device)
+        gq, gk, gv = (z if g is None else g for g in (gq, gk, gv))
+        gqkv = _Merge.apply(gq, gk, gv, cos, sin, qscale)
+        gx = gqkv @ weight.to(gqkv.dtype) if ctx.needs_input_grad[0] else None
+        gw = gqkv.flatten(0, 1).t() @ x.flatten(0, 1) if ctx.needs_input_grad[1] else None
+        return gx, gw, None, None, None, None
+
+
+def _qkv_split(x: Tensor, weight: Tensor, cos: Tensor, sin: Tensor, qscale: Tensor, heads: int):
+    return _QkvSplit.apply(x, weight, cos, sin, qscale, heads)
+
+
+_qkv_split = torch._dynamo.allow_in_graph(_qkv_split)
+
+
+def qkv_fusable(x: Tensor, weight: Tensor, heads: int) -> bool:
+    """Whether ``ebr_qkv_rope_split`` serves this projection: 16-bit CUDA ``x`` [B, N, C] and ``weight`` [3 H D, C] of
+    one dtype, D = 64 or 128, H D a multiple of 256, C a multiple of 64."""
+    if x.dim() != 3 or not x.is_cuda or x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype:
+        return False
+    c = x.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != c or weight.shape[0] % (3 * heads):
+        return False
+    d = weight.shape[0] // (3 * heads)
+    return d in (64, 128) and (heads * d) % 256 == 0 and c % 64 == 0
+
+
+def qkv_rope_split(x: Tensor, weight: Tensor, cos: Tensor, sin: Tensor, heads: int,
+                   qscale: Optional[Tensor] = None) -> Tuple[Tensor, Tensor, Tensor]:  # fmt: skip
+    """``rope_split(F.linear(x, weight), cos, sin, heads, qscale)`` as one tensor-core GEMM whose epilogue rotates and
+    lays out q, k, v (``ebr_qkv_rope_split``); shapes the kernel does not take run the GEMM and the split kernel.
+    ``x`` [B, N, C], ``weight`` [3 H D, C] (no bias); differentiable to every order in x and weight."""
+    if qscale is None:
+        qscale = x.new_zeros((0,), dtype=torch.float32)
+    if not qkv_fusable(x, weight, heads):
+        return rope_split(F.linear(x, weight.to(x.dtype)), cos, sin, heads, qscale if qscale.numel() else None)
+    d = weight.shape[0] // (3 * heads)
+    if tuple(cos.shape) != (x.shape[1], d) or tuple(sin.shape) != (x.shape[1], d):
+        raise ValueError(f"qkv_rope_split: tables must be [N, D], got {tuple(cos.shape)} (N={x.shape[1]}, D={d})")
+    return _qkv_split(x, weight, cos, sin, qscale.detach(), heads)
+
+
 # ---------------------------------------------------------------------------------------------------- rms_norm
 
 
@@ -357,6 +449,9 @@ def step_and_project(v: Tensor, g: Tensor, alpha: float, eps: float = 1e-5) -> T
 __all__ = [
     "add_rms_norm",
     "noisy_point",
+    "qkv_fusable",
+    "qkv_rope_split",
+    "qkv_rope_split_op",
     "quarter_swap",
     "rope_merge_op",
     "rope_split",

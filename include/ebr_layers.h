@@ -34,6 +34,17 @@ int ebr_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const 
                    int64_t stride_n, const float* cos_table, const float* sin_table, const float* qscale, void* q,
                    void* k, void* v, void* stream);
 
+/* The qkv projection with the split as its epilogue (one tensor-core GEMM, the [B, N, 3 H D] projection never stored):
+ * qkv = x W^T with fp32 accumulation and one rounding to the I/O type, then q, k, v exactly as ebr_rope_split makes
+ * them from that qkv. x: [B N, C] rows (row stride x_stride elements, unit column stride), W: [3 H D, C] contiguous
+ * (the nn.Linear weight in the I/O type). bfloat16 / float16 only; D = 64 or 128, H D a multiple of 256, C a multiple
+ * of 64, x_stride a multiple of 8 and every pointer 16-byte aligned, else EBR_ERR_SHAPE / EBR_ERR_STRIDE (the caller
+ * then runs its GEMM and ebr_rope_split). Replaces: F.linear + rope_split in EnergyAttention
+ * (models/attention.py:233-242, models/fused_attn/rope_split.py:77-82). */
+int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, int64_t C, const void* x,
+                       int64_t x_stride, const void* w, const float* cos_table, const float* sin_table,
+                       const float* qscale, void* q, void* k, void* v, void* stream);
+
 /* The adjoint: dqkv [B, N, 3 H D] (contiguous) from dq, dk, dv (strided [B, H, N, D] operands): dq is first scaled
  * by qscale (if not NULL) and rounded, then g' = g * cos + quarter_swap(g * sin) for dq and dk, rounded once; dv
  * copied. Replaces: ebr_fused::rope_merge (models/fused_attn/rope_split.py:91-96, ref_merge :53-67). */

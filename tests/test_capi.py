@@ -61,6 +61,15 @@ def test_layer_entry_points_reject_bad_arguments_before_device(lib):
     assert lib.ebr_descent_step(_native.BFLOAT16, 4, 460800, 1.0, 1e-5, t, t, t, t, need - 1, None) == _native.ERR_SCRATCH
     # empty problems are no-ops
     assert lib.ebr_rope_split(_native.BFLOAT16, 0, 4, 2, 8, None, 0, 48, None, None, None, None, None, None, None) == 0
+    # The fused projection: 16-bit only, D = 64 / 128 with H D % 256 == 0 and C % 64 == 0, aligned row strides.
+    q = lib.ebr_qkv_rope_split
+    assert q(_native.FLOAT32, 1, 4, 4, 64, 64, t, 64, t, t, t, None, t, t, t, None) == _native.ERR_DTYPE
+    assert q(_native.BFLOAT16, 1, 4, 2, 64, 64, t, 64, t, t, t, None, t, t, t, None) == _native.ERR_SHAPE
+    assert q(_native.BFLOAT16, 1, 4, 4, 32, 64, t, 64, t, t, t, None, t, t, t, None) == _native.ERR_SHAPE
+    assert q(_native.BFLOAT16, 1, 4, 4, 64, 96, t, 96, t, t, t, None, t, t, t, None) == _native.ERR_SHAPE
+    assert q(_native.BFLOAT16, 1, 4, 4, 64, 64, None, 64, t, t, t, None, t, t, t, None) == _native.ERR_NULL
+    assert q(_native.BFLOAT16, 1, 4, 4, 64, 64, t, 60, t, t, t, None, t, t, t, None) == _native.ERR_STRIDE
+    assert q(_native.BFLOAT16, 0, 4, 4, 64, 64, None, 64, None, None, None, None, None, None, None, None) == 0
     assert lib.ebr_add_rms_norm(_native.BFLOAT16, 0, 8, 1e-5, None, None, None, None, None, None, 0.0, None) == 0
 
 

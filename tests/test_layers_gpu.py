@@ -141,6 +141,87 @@ def test_rope_merge_is_the_adjoint_and_autograd_is_exact():
     assert torch.autograd.gradgradcheck(fn, (x,), eps=1e-6, atol=1e-8)
 
 
+QKV_SHAPES = [(2, 9, 9, 8, 64, 512), (1, 30, 30, 8, 64, 512), (3, 10, 10, 2, 128, 256), (1, 3, 4, 4, 64, 128)]
+
+
+def _qkv_inputs(shape, dtype, seed):
+    b, hh, ww, h, d, c = shape
+    rope, cos, sin = _tables(hh, ww, d)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(b, hh * ww, c, generator=g).to(dtype).to(DEV)
+    w = (torch.randn(3 * h * d, c, generator=g) * c**-0.5).to(dtype).to(DEV)
+    qs = (torch.rand(h, generator=g) + 0.5).to(dtype).float().to(DEV)
+    return x, w, cos, sin, qs, h
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", QKV_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("with_scale", [False, True])
+def test_qkv_rope_split_is_the_projection_then_the_split(dtype, shape, with_scale):
+    """The fused GEMM + split equals the reference's dense split of the correctly rounded projection (x W^T summed
+    exactly, rounded once) and the unfused cuBLAS GEMM + split kernel, up to the last bit of a projection value whose
+    fp32 sum rounds the other way (rare): a rotated output t c + swap(t) s then moves by at most a few units of
+    eps (|t| + |swap(t)|), which near a cancellation is many ulps of the output itself. Row counts that are not a
+    multiple of the 128-row tile, D = 128 and a 256-column q / k / v section are included."""
+    from ebr_b200.layers import qkv_fusable, qkv_rope_split_op, rope_split_op
+
+    x, w, cos, sin, qs, h = _qkv_inputs(shape, dtype, seed=sum(shape))
+    b, n, _ = x.shape
+    d = w.shape[0] // (3 * h)
+    assert qkv_fusable(x, w, h)
+    scale = qs if with_scale else torch.zeros(0, device=DEV)
+    got = qkv_rope_split_op(x, w, cos, sin, scale, h)
+    exact = (x.double() @ w.double().t()).to(dtype)
+    ref = ref_split(exact, cos, sin, h, qs if with_scale else None)
+    # cuBLAS summing in fp32 throughout (torch otherwise lets 16-bit GEMMs reduce partial sums in 16 bits).
+    m = torch.backends.cuda.matmul
+    flags = (m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction)
+    m.allow_bf16_reduced_precision_reduction = m.allow_fp16_reduced_precision_reduction = False
+    try:
+        unfused = rope_split_op(F.linear(x, w), cos, sin, scale, h)
+    finally:
+        m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction = flags
+    # Per output element: the magnitude of the rotation's two inputs (v: the element itself) and the bound on their
+    # fp32 summation error (K 2^-24 sum |x_i w_i|, which dominates for values near zero), head-major.
+    def per_output(t):
+        t = t.view(b, n, 3, h, d)
+        t = torch.cat([t[:, :, :2] + quarter_swap(t[:, :, :2]), t[:, :, 2:]], dim=2).permute(2, 0, 3, 1, 4)
+        if with_scale:
+            t[0] = t[0] * qs.double().view(1, h, 1, 1)
+        return t
+
+    mag = per_output(exact.double().abs())
+    acc = per_output((x.double().abs() @ w.double().abs().t()) * (x.shape[-1] * 2.0**-24))
+    eps = torch.finfo(dtype).eps
+    for part, (a, r, u) in enumerate(zip(got, ref, unfused)):
+        for other in (r, u):
+            diff = (a.double() - other.double()).abs()
+            bound = 3 * eps * mag[part] + 2 * acc[part]
+            assert bool((diff <= bound).all()), float((diff / bound).max())
+            assert float((a != other).double().mean()) < 0.01
+
+
+def test_qkv_rope_split_gradients_match_the_unfused_path_to_second_order():
+    """First and second derivatives (create_graph) in x and the weight equal those of F.linear + rope_split."""
+    from ebr_b200.layers import qkv_rope_split, rope_split
+
+    x0, w0, cos, sin, qs, h = _qkv_inputs((2, 9, 9, 8, 64, 512), torch.bfloat16, seed=3)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    r = torch.randn(x0.shape, generator=g).to(x0.dtype).to(DEV)
+
+    def run(fused):
+        x, w = x0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+        q, k, v = qkv_rope_split(x, w, cos, sin, h, qs) if fused else rope_split(F.linear(x, w), cos, sin, h, qs)
+        s = (q.float() * k.float()).sum() + (v.float() ** 2).sum()
+        gx, gw = torch.autograd.grad(s, (x, w), create_graph=True)
+        hw = torch.autograd.grad((gx.float() * r.float()).sum(), w)[0]
+        return gx, gw, hw
+
+    for a, b in zip(run(True), run(False)):
+        err = float((a.double() - b.double()).abs().max() / b.double().abs().max())
+        assert err < 1e-2, err
+
+
 def _check_rounding(a, r):
     """16-bit outputs: at most one ulp apart on under 2% of the elements (a row sum in another order can move a
     rounding); float32: a few ulps (no final rounding hides the sum-order difference)."""
