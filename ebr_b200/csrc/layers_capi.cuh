@@ -328,9 +328,9 @@ int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, in
   CUtensorMap tx, tw;
   if ((rc = make_matrix_map(&tx, x, dtype, M, C, x_stride, L::kBM)) != EBR_OK) return rc;
   if ((rc = make_matrix_map(&tw, w, dtype, 3 * H * D, C, C, L::kBN)) != EBR_OK) return rc;
-  const int64_t tiles = ((M + L::kBM - 1) / L::kBM) * (3 * H * D / L::kBN);
+  const int64_t m_tiles = (M + L::kBM - 1) / L::kBM;  // a CTA takes whole 128-row m-tiles
   const int64_t cap = sm_count(device);
-  const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
+  const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
   auto launch = [&](auto kernel, auto* out_tag) -> int {
     using T = std::remove_pointer_t<decltype(out_tag)>;
     if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))

@@ -3,8 +3,8 @@
 // accumulator tile on its way out, so the [B, N, 3 H D] projection never reaches memory.
 //
 // One persistent CTA per SM; a tile is 128 rows of x (tokens) by 256 output columns (4 heads at D = 64, 2 at D = 128,
-// all of one of q / k / v since H D is a multiple of 256). Tiles are numbered with the 256-column blocks fastest, so
-// the CTAs working at one time read the same rows of x (from L2) against all of W. Roles (320 threads):
+// all of one of q / k / v since H D is a multiple of 256). A CTA takes whole m-tiles (128 rows, all 3 H D / 256 column
+// tiles in order q, k, v): m-tiles blockIdx.x, blockIdx.x + gridDim.x, ... Roles (320 threads):
 //   warp 8     TMA producer: per 64-wide K block, the x tile [128 x 64] and the W tile [256 x 64] (both K-major,
 //              128-byte swizzle) into a 4-stage ring;
 //   warp 9     MMA issuer: 4 x tcgen05.mma M128 N256 K16 per K block into one of two 256-column accumulators in TMEM,
@@ -55,14 +55,27 @@ __device__ __forceinline__ int qkv_slot_start(int slot) {
   return (slot / (D / 64)) * (D / 2) + (slot % (D / 64)) * 16;
 }
 
-// One slot of two heads of a token row: accumulators (fp32) at TMEM columns ta0 / ta1 + da and + da + D / 4.
+// The 16-bit pair of a rounded fp32 pair, and the pair widened back as an f32x2 operand.
+template <typename T>
+__device__ __forceinline__ uint64_t widen2(uint32_t w) {
+  return f2_pack(unpack_lo<T>(w), unpack_hi<T>(w));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t narrow2(uint64_t v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  return pack2<T>(lo, hi);
+}
+
+// One slot of two heads of a token row: accumulators (fp32) at TMEM columns ta0 / ta1 + da and + da + D / 4. `tab`:
+// the slot's table values as f32x2 pairs -- cos of the first 16 elements [0, 8), their sin [8, 16), cos of the
+// partners [16, 24), their sin [24, 32). Each rounding of the scalar formula happens at the same place here: products
+// and the sum in f32x2 (round to nearest per lane), the result rounded to the I/O type once, the temperature product
+// rounded to fp32 and then to the I/O type by the store.
 template <typename T, int D>
 __device__ __forceinline__ void qkv_rope_slot2(uint32_t ta0, uint32_t ta1, int da, bool rotate, bool scale_q,
-                                               float qs0, float qs1, const float (&tab)[64], bool row_ok, T* dst0,
+                                               float qs0, float qs1, const uint64_t (&tab)[32], bool row_ok, T* dst0,
                                                T* dst1) {
-  using layers::add_rn;
-  using layers::mul_rn;
-  using layers::rnd;
   constexpr int kQ = D / 4;
   uint32_t r[4][16];
   tmem_ld16(ta0 + da, r[0]);
@@ -72,29 +85,34 @@ __device__ __forceinline__ void qkv_rope_slot2(uint32_t ta0, uint32_t ta1, int d
   tmem_wait_ld();
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
-    float a[16], b[16];
+    uint32_t wa[8], wb[8];  // the head's outputs as 16-bit pairs: elements [da, da + 16) and their partners
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      a[i] = rnd<T>(__uint_as_float(r[2 * hh][i]));
-      b[i] = rnd<T>(__uint_as_float(r[2 * hh + 1][i]));
+    for (int i = 0; i < 8; ++i) {
+      wa[i] = pack2<T>(__uint_as_float(r[2 * hh][2 * i]), __uint_as_float(r[2 * hh][2 * i + 1]));
+      wb[i] = pack2<T>(__uint_as_float(r[2 * hh + 1][2 * i]), __uint_as_float(r[2 * hh + 1][2 * i + 1]));
     }
     if (rotate) {
-      const float qs = hh == 0 ? qs0 : qs1;
+      const float qsf = hh == 0 ? qs0 : qs1;
+      const uint64_t qs = f2_pack(qsf, qsf);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        // tab: cos of the first 16 elements, sin of them, cos of their partners, sin of the partners
-        const float oa = rnd<T>(add_rn(mul_rn(a[i], tab[i]), mul_rn(b[i], tab[16 + i])));
-        const float ob = rnd<T>(add_rn(mul_rn(b[i], tab[32 + i]), mul_rn(a[i], tab[48 + i])));
-        a[i] = scale_q ? mul_rn(oa, qs) : oa;
-        b[i] = scale_q ? mul_rn(ob, qs) : ob;
+      for (int i = 0; i < 8; ++i) {
+        const uint64_t a = widen2<T>(wa[i]), b = widen2<T>(wb[i]);
+        uint32_t oa = narrow2<T>(f2_add(f2_mul(a, tab[i]), f2_mul(b, tab[8 + i])));
+        uint32_t ob = narrow2<T>(f2_add(f2_mul(b, tab[16 + i]), f2_mul(a, tab[24 + i])));
+        if (scale_q) {
+          oa = narrow2<T>(f2_mul(widen2<T>(oa), qs));
+          ob = narrow2<T>(f2_mul(widen2<T>(ob), qs));
+        }
+        wa[i] = oa;
+        wb[i] = ob;
       }
     }
     T* dst = hh == 0 ? dst0 : dst1;
     if (row_ok) {
-      layers::store_c<T, 8>(dst + da, reinterpret_cast<const float(&)[8]>(a[0]));
-      layers::store_c<T, 8>(dst + da + 8, reinterpret_cast<const float(&)[8]>(a[8]));
-      layers::store_c<T, 8>(dst + da + kQ, reinterpret_cast<const float(&)[8]>(b[0]));
-      layers::store_c<T, 8>(dst + da + kQ + 8, reinterpret_cast<const float(&)[8]>(b[8]));
+      *reinterpret_cast<uint4*>(dst + da) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+      *reinterpret_cast<uint4*>(dst + da + 8) = make_uint4(wa[4], wa[5], wa[6], wa[7]);
+      *reinterpret_cast<uint4*>(dst + da + kQ) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+      *reinterpret_cast<uint4*>(dst + da + kQ + 8) = make_uint4(wb[4], wb[5], wb[6], wb[7]);
     }
   }
 }
@@ -116,7 +134,7 @@ __global__ void __launch_bounds__(320, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int HD = H * D, n_nt = 3 * HD / L::kBN, n_kb = C / L::kBK;
-  const int64_t n_mt = (M + L::kBM - 1) / L::kBM, tiles = n_mt * n_nt;
+  const int64_t n_mt = (M + L::kBM - 1) / L::kBM;
 
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -147,8 +165,10 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tw);
       uint32_t use = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int mt = static_cast<int>(t / n_nt), nt = static_cast<int>(t - static_cast<int64_t>(mt) * n_nt);
+      for (int64_t j = 0; ok; ++j) {
+        const int64_t mt = blockIdx.x + (j / n_nt) * gridDim.x;
+        if (mt >= n_mt) break;
+        const int nt = static_cast<int>(j % n_nt);
         for (int kb = 0; kb < n_kb; ++kb, ++use) {
           const int s = static_cast<int>(use % NS);
           ok = mbar_wait_or_abort(&empty[s], ((use / NS) & 1) ^ 1, 611, abort);
@@ -167,7 +187,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint64_t d0 = sw128_desc(smem_u32(smem), 16u, 1024u);
       uint32_t use = 0, lt = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++lt) {
+      for (int64_t j = 0; ok && blockIdx.x + (j / n_nt) * gridDim.x < n_mt; ++j, ++lt) {
         const uint32_t ab = lt & 1;
         ok = mbar_wait_or_abort(&acc_empty[ab], ((lt >> 1) & 1) ^ 1, 621, abort);
         for (int kb = 0; kb < n_kb && ok; ++kb, ++use) {
@@ -190,11 +210,34 @@ __global__ void __launch_bounds__(320, 1)
     constexpr int kHeads = L::kBN / D;      // heads per tile
     const int wq = warp & 3, grp = warp >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    // tab: this thread's table values for one slot of its token row, as f32x2 pairs (see qkv_rope_slot2). At D = 64
+    // (one slot) they serve every q / k tile of the m-tile and the next m-tile's are requested during its v tiles,
+    // which do not rotate; at D = 128 each slot's are loaded before its use.
+    uint64_t tab[32];
+    auto load_tab = [&](int64_t mt_, int slot) {
+      const int64_t row_ = mt_ * L::kBM + wq * 32 + lane;
+      const int64_t n_ = row_ < M ? row_ % N : 0;
+      const int da = qkv_slot_start<D>(grp * kSlots + slot);
+      const float* src[4] = {cos_t + n_ * D + da, sin_t + n_ * D + da, cos_t + n_ * D + da + D / 4,
+                             sin_t + n_ * D + da + D / 4};
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(src[part] + i));
+          tab[part * 8 + i / 2] = f2_pack(f.x, f.y);
+          tab[part * 8 + i / 2 + 1] = f2_pack(f.z, f.w);
+        }
+      }
+    };
+    if (kSlots == 1 && blockIdx.x < n_mt) load_tab(blockIdx.x, 0);
     uint32_t lt = 0;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
-      const int mt = static_cast<int>(t / n_nt), nt = static_cast<int>(t - static_cast<int64_t>(mt) * n_nt);
+    for (int64_t j = 0;; ++j, ++lt) {
+      const int64_t mt = blockIdx.x + (j / n_nt) * gridDim.x;
+      if (mt >= n_mt) break;
+      const int nt = static_cast<int>(j % n_nt);
       const uint32_t ab = lt & 1;
-      const int64_t row = static_cast<int64_t>(mt) * L::kBM + wq * 32 + lane;
+      const int64_t row = mt * L::kBM + wq * 32 + lane;
       const bool row_ok = row < M;
       const int64_t b = row_ok ? row / N : 0;
       const int n = row_ok ? static_cast<int>(row - b * N) : 0;
@@ -202,25 +245,13 @@ __global__ void __launch_bounds__(320, 1)
       const bool rotate = sec != 2, scale_q = sec == 0 && qscale != nullptr;
       T* base = (sec == 0 ? q : sec == 1 ? k : v) + ((b * H + h0) * N + n) * static_cast<int64_t>(D);
       const int64_t head_stride = static_cast<int64_t>(N) * D;
-      // The first slot's table values are requested before the accumulators are waited for.
-      float tab[64];
-      auto load_tab = [&](int slot) {
-        if (!rotate) return;
-        const int da = qkv_slot_start<D>(grp * kSlots + slot);
-        const float* cs = cos_t + static_cast<int64_t>(n) * D;
-        const float* sn = sin_t + static_cast<int64_t>(n) * D;
-        layers::load_table_v<16>(cs + da, reinterpret_cast<float(&)[16]>(tab[0]));
-        layers::load_table_v<16>(sn + da, reinterpret_cast<float(&)[16]>(tab[16]));
-        layers::load_table_v<16>(cs + da + D / 4, reinterpret_cast<float(&)[16]>(tab[32]));
-        layers::load_table_v<16>(sn + da + D / 4, reinterpret_cast<float(&)[16]>(tab[48]));
-      };
-      load_tab(0);
+      if (kSlots == 1 && sec == 2 && h0 == 0 && mt + gridDim.x < n_mt) load_tab(mt + gridDim.x, 0);
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[ab], (lt >> 1) & 1, 631, abort))) break;
       tc_fence_after();
       const uint32_t tacc = tmem + lane_off + ab * 256;
 #pragma unroll
       for (int slot = 0; slot < kSlots; ++slot) {
-        if (slot > 0) load_tab(slot);
+        if (kSlots > 1 && rotate) load_tab(mt, slot);
         const int da = qkv_slot_start<D>(grp * kSlots + slot);
 #pragma unroll
         for (int hl = 0; hl < kHeads; hl += 2) {

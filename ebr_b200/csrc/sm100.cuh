@@ -260,7 +260,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 
 // ------------------------------------------------------------------------------------------------ packed fp32 pairs
 
-// Blackwell's two-wide fp32 arithmetic (fma / add / sub .f32x2: one instruction for two lanes of work), on a pair
+// Blackwell's two-wide fp32 arithmetic (fma / mul / add / sub .f32x2: one instruction for two lanes of work, each lane
+// rounded as the scalar instruction rounds), on a pair
 // held as one 64-bit register; and the three-input max / min.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;
@@ -273,6 +274,11 @@ __device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
