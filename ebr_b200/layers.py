@@ -23,6 +23,7 @@ from typing import Optional, Tuple
 
 import torch
 import torch.nn.functional as F
+from torch.autograd.graph import get_gradient_edge
 
 from ebr_b200 import _native
 
@@ -236,6 +237,17 @@ def _(x, weight, cos, sin, qscale, heads):
     return tuple(x.new_empty((b, heads, n, d)) for _ in range(3))
 
 
+def _engine_needs(node) -> bool:
+    """Whether the running backward will execute ``node`` (None: the input needs no gradient). The engine cannot
+    answer for a leaf's accumulator under autograd.grad; such an input is assumed needed."""
+    if node is None:
+        return False
+    try:
+        return bool(torch._C._will_engine_execute_node(node))
+    except RuntimeError:
+        return True
+
+
 class _QkvSplit(torch.autograd.Function):
     """Forward: the projection with the split as its epilogue. Backward: the merge (the split's exact adjoint), then
     the projection's two products, all differentiable ops, so every higher order follows."""
@@ -249,6 +261,9 @@ class _QkvSplit(torch.autograd.Function):
         x, weight, cos, sin, qscale, heads = inputs
         ctx.save_for_backward(x, weight, cos, sin, qscale)
         ctx.shape = tuple(output[0].shape)
+        # The autograd nodes of x and weight: a backward that does not reach one of them (dE/dz in the descent never
+        # needs the weight's gradient) skips its product, as the engine skips it for a plain F.linear.
+        ctx.nodes = tuple(get_gradient_edge(t).node if t.requires_grad else None for t in (x, weight))
 
     @staticmethod
     def backward(ctx, gq, gk, gv):
@@ -258,9 +273,10 @@ class _QkvSplit(torch.autograd.Function):
         if gq is None or gk is None or gv is None:
             z = torch.zeros(ctx.shape, dtype=ref.dtype, device=ref.device)
         gq, gk, gv = (z if g is None else g for g in (gq, gk, gv))
+        need_x, need_w = (_engine_needs(n) for n in ctx.nodes)
         gqkv = _Merge.apply(gq, gk, gv, cos, sin, qscale)
-        gx = gqkv @ weight.to(gqkv.dtype) if ctx.needs_input_grad[0] else None
-        gw = gqkv.flatten(0, 1).t() @ x.flatten(0, 1) if ctx.needs_input_grad[1] else None
+        gx = gqkv @ weight.to(gqkv.dtype) if need_x else None
+        gw = gqkv.flatten(0, 1).t() @ x.flatten(0, 1) if need_w else None
         return gx, gw, None, None, None, None
 
 

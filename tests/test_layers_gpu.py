@@ -202,7 +202,8 @@ def test_qkv_rope_split_is_the_projection_then_the_split(dtype, shape, with_scal
 
 
 def test_qkv_rope_split_gradients_match_the_unfused_path_to_second_order():
-    """First and second derivatives (create_graph) in x and the weight equal those of F.linear + rope_split."""
+    """First and second derivatives (create_graph) in x and the weight equal those of F.linear + rope_split, and a
+    backward asked for x alone or the weight alone returns that gradient."""
     from ebr_b200.layers import qkv_rope_split, rope_split
 
     x0, w0, cos, sin, qs, h = _qkv_inputs((2, 9, 9, 8, 64, 512), torch.bfloat16, seed=3)
@@ -220,6 +221,15 @@ def test_qkv_rope_split_gradients_match_the_unfused_path_to_second_order():
     for a, b in zip(run(True), run(False)):
         err = float((a.double() - b.double()).abs().max() / b.double().abs().max())
         assert err < 1e-2, err
+
+    # A backward that asks for one input only gets it (the other product is skipped, not its own input's).
+    for want in (0, 1):
+        got = []
+        for fused in (True, False):
+            x, w = x0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+            q, k, v = qkv_rope_split(x, w, cos, sin, h, qs) if fused else rope_split(F.linear(x, w), cos, sin, h, qs)
+            got.append(torch.autograd.grad((q.float() * k.float()).sum() + (v.float() ** 2).sum(), (x, w)[want])[0])
+        assert torch.equal(got[0], got[1])
 
 
 def _check_rounding(a, r):
