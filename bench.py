@@ -13,7 +13,8 @@ per call / CUDA-event duration) against the measured bf16 peak; ``cpu_baseline``
 attention, torch CPU for the rest) timed on a bounded sample on this host.
 
 ``--impl reference`` times only that CPU path (rank 0) on the same config and prints its own line.
-``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape).
+``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape), and with
+``--passes qkv_rope,qkv_unfused`` the fused qkv projection against cuBLAS + the split kernel at the same shapes.
 ``--mode train`` times BASELINE config 2's training step (double backward, flat-bucket NCCL all-reduce, AdamW).
 """
 
@@ -502,10 +503,57 @@ def run_sweep(args) -> None:
                 tf, gbs = flop / ms / 1e9, byt / ms / 1e6
                 out[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "tc_frac": round(tf / pk["tf_burst"], 4),
                              "gbs": round(gbs, 0), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}  # fmt: skip
-            _native.device_status()
-            print(json.dumps(out), flush=True)
             del q, k, v, do, gq, gk, gv, o, lse, dq
             torch.cuda.empty_cache()
+            proj = [p for p in ("qkv_rope", "qkv_unfused") if p in args.passes.split(",")]
+            if proj:
+                out.update(sweep_qkv(args, proj, B, L, H, D, pk))
+            _native.device_status()
+            print(json.dumps(out), flush=True)
+            torch.cuda.empty_cache()
+
+
+def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
+    """The qkv projection of one attention layer at the sweep shape (x [B, L, H D], W [3 H D, H D]): the tcgen05 GEMM
+    with the RoPE split as its epilogue (``qkv_rope``) and cuBLAS + the split kernel (``qkv_unfused``)."""
+    import torch.nn.functional as F
+
+    from ebr_b200.energy import Rope2D
+    from ebr_b200.layers import qkv_rope_split_op, rope_split_op
+
+    side = int(round(L**0.5))
+    hh, ww = (side, side) if side * side == L else (32, L // 32)
+    rope = Rope2D(D, hh, ww).cuda()
+    C = H * D
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(B, L, C, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(3 * C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
+    e = torch.zeros(0, device="cuda")
+    fns = {
+        "qkv_rope": lambda: qkv_rope_split_op(x, w, rope.cos_table, rope.sin_table, e, H),
+        "qkv_unfused": lambda: rope_split_op(F.linear(x, w), rope.cos_table, rope.sin_table, e, H),
+    }
+    res = {}
+    for name in passes:
+        fn = fns[name]
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        ms = statistics.median(ts)
+        flop = 2.0 * B * L * C * 3 * C
+        byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)
+        res[name] = {"ms": round(ms, 4), "tflops": round(flop / ms / 1e9, 1),
+                     "tc_frac": round(flop / ms / 1e9 / pk["tf_burst"], 4), "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
+    del x, w
+    return res
 
 
 def main() -> None:
@@ -517,7 +565,8 @@ def main() -> None:
     ap.add_argument("--mode", choices=["descent", "sweep", "train"], default="descent")
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
-    ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd", help="sweep: which passes to time")
+    ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd",
+                    help="sweep: which passes to time (also qkv_rope, qkv_unfused: the fused qkv projection)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
