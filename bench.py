@@ -505,7 +505,7 @@ def run_sweep(args) -> None:
                              "gbs": round(gbs, 0), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}  # fmt: skip
             del q, k, v, do, gq, gk, gv, o, lse, dq
             torch.cuda.empty_cache()
-            proj = [p for p in ("qkv_rope", "qkv_unfused") if p in args.passes.split(",")]
+            proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused") if p in args.passes.split(",")]
             if proj:
                 out.update(sweep_qkv(args, proj, B, L, H, D, pk))
             _native.device_status()
@@ -514,12 +514,13 @@ def run_sweep(args) -> None:
 
 
 def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
-    """The qkv projection of one attention layer at the sweep shape (x [B, L, H D], W [3 H D, H D]): the tcgen05 GEMM
-    with the RoPE split as its epilogue (``qkv_rope``) and cuBLAS + the split kernel (``qkv_unfused``)."""
+    """The projections of one attention layer at the sweep shape: qkv (x [B, L, H D], W [3 H D, H D]) as the tcgen05
+    GEMM with the RoPE split as its epilogue (``qkv_rope``) and as cuBLAS + the split kernel (``qkv_unfused``); the output
+    projection from the head-major attention output (``o_proj``) and as transpose copy + cuBLAS (``o_unfused``)."""
     import torch.nn.functional as F
 
     from ebr_b200.energy import Rope2D
-    from ebr_b200.layers import qkv_rope_split_op, rope_split_op
+    from ebr_b200.layers import o_proj_op, qkv_rope_split_op, rope_split_op
 
     side = int(round(L**0.5))
     hh, ww = (side, side) if side * side == L else (32, L // 32)
@@ -529,9 +530,13 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     x = torch.randn(B, L, C, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(3 * C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     e = torch.zeros(0, device="cuda")
+    o = torch.randn(B, H, L, D, device="cuda", generator=g).to(torch.bfloat16)
+    wo = (torch.randn(C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     fns = {
         "qkv_rope": lambda: qkv_rope_split_op(x, w, rope.cos_table, rope.sin_table, e, H),
         "qkv_unfused": lambda: rope_split_op(F.linear(x, w), rope.cos_table, rope.sin_table, e, H),
+        "o_proj": lambda: o_proj_op(o, wo),
+        "o_unfused": lambda: F.linear(o.transpose(1, 2).reshape(B, L, C), wo),
     }
     res = {}
     for name in passes:
@@ -548,11 +553,15 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
         ms = statistics.median(ts)
-        flop = 2.0 * B * L * C * 3 * C
-        byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)
+        if name.startswith("qkv"):
+            flop = 2.0 * B * L * C * 3 * C
+            byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)
+        else:
+            flop = 2.0 * B * L * C * C
+            byt = 2.0 * (2 * B * L * C + C * C)  # O, W, y
         res[name] = {"ms": round(ms, 4), "tflops": round(flop / ms / 1e9, 1),
                      "tc_frac": round(flop / ms / 1e9 / pk["tf_burst"], 4), "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
-    del x, w
+    del x, w, o, wo
     return res
 
 
@@ -566,7 +575,7 @@ def main() -> None:
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
     ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd",
-                    help="sweep: which passes to time (also qkv_rope, qkv_unfused: the fused qkv projection)")
+                    help="sweep: which passes to time (also qkv_rope, qkv_unfused, o_proj, o_unfused: the projections)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

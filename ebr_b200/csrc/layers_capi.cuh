@@ -9,6 +9,7 @@
 
 #include "../../include/ebr_layers.h"
 #include "layers.cuh"
+#include "o_proj.cuh"
 #include "qkv_rope.cuh"
 
 namespace {
@@ -345,6 +346,44 @@ int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, in
                    : launch(ebr::tc_qkv_rope_kernel<__nv_bfloat16, 128>, static_cast<__nv_bfloat16*>(nullptr));
   return D == 64 ? launch(ebr::tc_qkv_rope_kernel<__half, 64>, static_cast<__half*>(nullptr))
                  : launch(ebr::tc_qkv_rope_kernel<__half, 128>, static_cast<__half*>(nullptr));
+}
+
+int ebr_o_proj(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t C_out, const ebr_operand* o,
+               const void* w, void* y, void* stream) {
+  if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
+    return set_error(EBR_ERR_DTYPE, "o_proj: bfloat16 or float16 only%s%s");
+  if (B < 0 || N < 0 || H < 1 || (D != 64 && D != 128) || C_out < 256 || C_out % 256 != 0 || B > INT32_MAX ||
+      N > INT32_MAX || H * D > INT32_MAX || C_out > INT32_MAX)
+    return set_error(EBR_ERR_SHAPE, "o_proj: needs D = 64 or 128 and C_out a positive multiple of 256%s%s");
+  if (B * N == 0) return EBR_OK;
+  int rc = check_operand(o, "o");
+  if (rc != EBR_OK) return rc;
+  if (!w || !y) return set_error(EBR_ERR_NULL, "o_proj: NULL pointer%s%s");
+  if (!tc_operand_ok(o, B, H, N) || !all_aligned16({w, y}))
+    return set_error(EBR_ERR_STRIDE, "o_proj: o needs 16-byte aligned data and strides, w / y 16-byte alignment%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  using L = ebr::OProjLayout;
+  CUtensorMap to, tw;
+  if (make_tile_map(&to, o, dtype, B, H, N, D)) return set_error(EBR_ERR_CUDA, "o_proj: tensor map for o%s%s");
+  if ((rc = make_matrix_map(&tw, w, dtype, C_out, H * D, H * D, L::kBN)) != EBR_OK) return rc;
+  const int64_t m_tiles = B * ((N + L::kBM - 1) / L::kBM);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
+  auto launch = [&](auto kernel, auto* out_tag) -> int {
+    using T = std::remove_pointer_t<decltype(out_tag)>;
+    if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))
+      return rc;
+    kernel<<<grid, L::kThreads, L::kSmem, st>>>(to, tw, static_cast<int>(B), static_cast<int>(H), static_cast<int>(N),
+                                                static_cast<int>(C_out), static_cast<T*>(y));
+    return check_launch("tc_o_proj_kernel");
+  };
+  if (dtype == EBR_BFLOAT16)
+    return D == 64 ? launch(ebr::tc_o_proj_kernel<__nv_bfloat16, 64>, static_cast<__nv_bfloat16*>(nullptr))
+                   : launch(ebr::tc_o_proj_kernel<__nv_bfloat16, 128>, static_cast<__nv_bfloat16*>(nullptr));
+  return D == 64 ? launch(ebr::tc_o_proj_kernel<__half, 64>, static_cast<__half*>(nullptr))
+                 : launch(ebr::tc_o_proj_kernel<__half, 128>, static_cast<__half*>(nullptr));
 }
 
 }  // extern "C"

@@ -207,6 +207,9 @@ class EnergyAttention(nn.Module):
         if not temperature_applied:
             q = q * self.log_logit_scale.exp().to(q.dtype).view(1, -1, 1, 1)
         y = self.attention(q, k, v)
+        if self.fused:
+            # The projection reads the head-major attention output directly (no transpose copy).
+            return fl.o_proj(y, self.o.weight.to(y.dtype))
         return self.o(y.transpose(1, 2).reshape(b, n, h * d))
 
 

@@ -314,6 +314,85 @@ def qkv_rope_split(x: Tensor, weight: Tensor, cos: Tensor, sin: Tensor, heads: i
     return _qkv_split(x, weight, cos, sin, qscale.detach(), heads)
 
 
+# ---------------------------------------------------------------------------------------------------- o projection
+
+
+@torch.library.custom_op("ebr_fused::o_proj", mutates_args=())
+def o_proj_op(o: Tensor, weight: Tensor) -> Tensor:
+    _require_cuda(o, "o_proj")
+    b, h, n, d = o.shape
+    if o.stride(-1) != 1:
+        o = o.contiguous()
+    weight = weight.to(o.dtype).contiguous()
+    y = torch.empty((b, n, weight.shape[0]), device=o.device, dtype=o.dtype)
+    op = _native.Operand(o.data_ptr(), o.stride(0), o.stride(1), o.stride(2))
+    _native.check(
+        _native.lib().ebr_o_proj(_DTYPES[o.dtype], b, h, n, d, weight.shape[0], ctypes.byref(op), weight.data_ptr(),
+                                 y.data_ptr(), _stream()),  # fmt: skip
+        "o_proj",
+    )
+    return y
+
+
+@o_proj_op.register_fake
+def _(o, weight):
+    b, _, n, _ = o.shape
+    return o.new_empty((b, n, weight.shape[0]))
+
+
+class _OProj(torch.autograd.Function):
+    """Forward: the projection read from the head-major attention output. Backward: the two products, as
+    differentiable ops, each only when the running backward reaches its input; the gradient of O is returned as a
+    head-major view of [B, N, H D] (the attention's backward reads strided dO), so no transpose is made."""
+
+    @staticmethod
+    def forward(o, weight):
+        return torch.ops.ebr_fused.o_proj(o, weight)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        o, weight = inputs
+        ctx.save_for_backward(o, weight)
+        ctx.nodes = tuple(get_gradient_edge(t).node if t.requires_grad else None for t in (o, weight))
+
+    @staticmethod
+    def backward(ctx, gy):
+        o, weight = ctx.saved_tensors
+        b, h, n, d = o.shape
+        need_o, need_w = (_engine_needs(nd) for nd in ctx.nodes)
+        go = (gy @ weight.to(gy.dtype)).view(b, n, h, d).transpose(1, 2) if need_o else None
+        gw = gy.flatten(0, 1).t() @ o.transpose(1, 2).reshape(b * n, h * d) if need_w else None
+        return go, gw
+
+
+def _o_proj(o: Tensor, weight: Tensor) -> Tensor:
+    return _OProj.apply(o, weight)
+
+
+_o_proj = torch._dynamo.allow_in_graph(_o_proj)
+
+
+def o_proj_fusable(o: Tensor, weight: Tensor) -> bool:
+    """Whether ``ebr_o_proj`` serves this projection: 16-bit CUDA ``o`` [B, H, N, D] with unit head-dim stride and
+    16-byte-multiple strides, ``weight`` [C_out, H D] of the same dtype, D = 64 or 128, C_out a multiple of 256."""
+    if o.dim() != 4 or not o.is_cuda or o.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != o.dtype:
+        return False
+    b, h, n, d = o.shape
+    if d not in (64, 128) or weight.dim() != 2 or weight.shape[1] != h * d or weight.shape[0] % 256:
+        return False
+    return o.stride(-1) == 1 and all(s % 8 == 0 for s in o.stride()[:3]) and o.data_ptr() % 16 == 0
+
+
+def o_proj(o: Tensor, weight: Tensor) -> Tensor:
+    """``F.linear(o.transpose(1, 2).reshape(B, N, H * D), weight)`` without the transpose copy (``ebr_o_proj``); shapes
+    the kernel does not take run the copy and the GEMM. ``o`` [B, H, N, D], ``weight`` [C_out, H D] (no bias);
+    differentiable to every order in o and weight."""
+    if not o_proj_fusable(o, weight):
+        b, h, n, d = o.shape
+        return F.linear(o.transpose(1, 2).reshape(b, n, h * d), weight.to(o.dtype))
+    return _o_proj(o, weight)
+
+
 # ---------------------------------------------------------------------------------------------------- rms_norm
 
 
@@ -465,6 +544,9 @@ def step_and_project(v: Tensor, g: Tensor, alpha: float, eps: float = 1e-5) -> T
 __all__ = [
     "add_rms_norm",
     "noisy_point",
+    "o_proj",
+    "o_proj_fusable",
+    "o_proj_op",
     "qkv_fusable",
     "qkv_rope_split",
     "qkv_rope_split_op",

@@ -45,6 +45,15 @@ int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, in
                        int64_t x_stride, const void* w, const float* cos_table, const float* sin_table,
                        const float* qscale, void* q, void* k, void* v, void* stream);
 
+/* The attention's output projection from the head-major attention output: y[b, n, :] = sum_h O[b, h, n, :] W_h^T with
+ * W_h = W[:, h D : (h + 1) D], fp32 accumulation and one rounding to the I/O type (the [B, N, H D] transpose of O is
+ * never stored). o: [B, H, N, D] operand (16-byte aligned data and strides, unit head-dim stride); w: [C_out, H D]
+ * contiguous; y: [B, N, C_out] contiguous. bfloat16 / float16 only, D = 64 or 128, C_out a multiple of 256, else
+ * EBR_ERR_SHAPE / EBR_ERR_STRIDE (the caller then transposes O and runs its GEMM). Replaces:
+ * self.o(y.transpose(1, 2).reshape(b, n, h d)) in EnergyAttention (models/attention.py:241-242). */
+int ebr_o_proj(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t C_out, const ebr_operand* o,
+               const void* w, void* y, void* stream);
+
 /* The adjoint: dqkv [B, N, 3 H D] (contiguous) from dq, dk, dv (strided [B, H, N, D] operands): dq is first scaled
  * by qscale (if not NULL) and rounded, then g' = g * cos + quarter_swap(g * sin) for dq and dk, rounded once; dv
  * copied. Replaces: ebr_fused::rope_merge (models/fused_attn/rope_split.py:91-96, ref_merge :53-67). */

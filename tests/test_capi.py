@@ -70,6 +70,16 @@ def test_layer_entry_points_reject_bad_arguments_before_device(lib):
     assert q(_native.BFLOAT16, 1, 4, 4, 64, 64, None, 64, t, t, t, None, t, t, t, None) == _native.ERR_NULL
     assert q(_native.BFLOAT16, 1, 4, 4, 64, 64, t, 60, t, t, t, None, t, t, t, None) == _native.ERR_STRIDE
     assert q(_native.BFLOAT16, 0, 4, 4, 64, 64, None, 64, None, None, None, None, None, None, None, None) == 0
+    # The o projection: 16-bit only, D = 64 / 128, C_out a multiple of 256, aligned operand and pointers.
+    p = lib.ebr_o_proj
+    good = _op()
+    assert p(_native.FLOAT32, 1, 4, 8, 64, 256, r(good), t, t, None) == _native.ERR_DTYPE
+    assert p(_native.BFLOAT16, 1, 4, 8, 32, 256, r(good), t, t, None) == _native.ERR_SHAPE
+    assert p(_native.BFLOAT16, 1, 4, 8, 64, 128, r(good), t, t, None) == _native.ERR_SHAPE
+    assert p(_native.BFLOAT16, 1, 4, 8, 64, 256, None, t, t, None) == _native.ERR_NULL
+    assert p(_native.BFLOAT16, 1, 4, 8, 64, 256, r(good), None, t, None) == _native.ERR_NULL
+    assert p(_native.BFLOAT16, 1, 4, 8, 64, 256, r(good), t + 2, t, None) == _native.ERR_STRIDE
+    assert p(_native.BFLOAT16, 0, 4, 8, 64, 256, None, None, None, None) == 0
     assert lib.ebr_add_rms_norm(_native.BFLOAT16, 0, 8, 1e-5, None, None, None, None, None, None, 0.0, None) == 0
 
 

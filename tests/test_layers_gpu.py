@@ -232,6 +232,82 @@ def test_qkv_rope_split_gradients_match_the_unfused_path_to_second_order():
         assert torch.equal(got[0], got[1])
 
 
+O_SHAPES = [(2, 8, 81, 64, 512), (1, 8, 900, 64, 512), (3, 2, 100, 128, 256), (2, 4, 300, 64, 256)]
+
+
+def _o_inputs(shape, dtype, seed, token_major=False):
+    b, h, n, d, c = shape
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    if token_major:  # the layout a [B, N, H, D] buffer viewed head-major gives (strides N H D, D, H D, 1)
+        o = (torch.randn(b, n, h, d, generator=g) * 0.5).to(dtype).to(DEV).transpose(1, 2)
+    else:
+        o = (torch.randn(b, h, n, d, generator=g) * 0.5).to(dtype).to(DEV)
+    w = (torch.randn(c, h * d, generator=g) * (h * d) ** -0.5).to(dtype).to(DEV)
+    return o, w
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", O_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("token_major", [False, True])
+def test_o_proj_is_the_gemm_of_the_transposed_output(dtype, shape, token_major):
+    """y = O^T-reshaped times W^T read from the head-major output: within one rounding of the exact product (plus the
+    fp32 summation bound for values near zero) and equal to cuBLAS with fp32 reduction but for a last-bit difference
+    of a sum taken in another order; token counts that are not a multiple of 128 and both O layouts included."""
+    from ebr_b200.layers import o_proj_fusable, o_proj_op
+
+    b, h, n, d, c = shape
+    o, w = _o_inputs(shape, dtype, seed=sum(shape), token_major=token_major)
+    assert o_proj_fusable(o, w)
+    got = o_proj_op(o, w)
+    x = o.transpose(1, 2).reshape(b, n, h * d)
+    exact = x.double() @ w.double().t()
+    ref = exact.to(dtype)
+    acc = (x.double().abs() @ w.double().abs().t()) * (h * d * 2.0**-24)
+    eps = torch.finfo(dtype).eps
+    diff = (got.double() - ref.double()).abs()
+    assert bool((diff <= 2 * eps * ref.double().abs() + 2 * acc).all()), float((diff / (ref.double().abs() + acc)).max())
+    m = torch.backends.cuda.matmul
+    flags = (m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction)
+    m.allow_bf16_reduced_precision_reduction = m.allow_fp16_reduced_precision_reduction = False
+    try:
+        unfused = F.linear(x, w)
+    finally:
+        m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction = flags
+    assert float((got != unfused).double().mean()) < 0.01
+
+
+def test_o_proj_gradients_match_the_unfused_path_to_second_order():
+    """First and second derivatives (create_graph) in O and the weight equal those of transpose + F.linear, and a
+    backward asked for one input alone returns that gradient."""
+    from ebr_b200.layers import o_proj
+
+    o0, w0 = _o_inputs((2, 8, 81, 64, 512), torch.bfloat16, seed=9)
+    b, h, n, d = o0.shape
+    g = torch.Generator(device="cpu").manual_seed(10)
+    r = torch.randn(o0.shape, generator=g).to(o0.dtype).to(DEV)
+
+    def proj(o, w, fused):
+        return o_proj(o, w) if fused else F.linear(o.transpose(1, 2).reshape(b, n, h * d), w)
+
+    def run(fused):
+        o, w = o0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+        s = (proj(o, w, fused).float() ** 2).sum()
+        go, gw = torch.autograd.grad(s, (o, w), create_graph=True)
+        hw = torch.autograd.grad((go.float() * r.float()).sum(), w)[0]
+        return go, gw, hw
+
+    for a, bb in zip(run(True), run(False)):
+        err = float((a.double() - bb.double()).abs().max() / bb.double().abs().max())
+        assert err < 1e-2, err
+    for want in (0, 1):
+        got = []
+        for fused in (True, False):
+            o, w = o0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+            got.append(torch.autograd.grad((proj(o, w, fused).float() ** 2).sum(), (o, w)[want])[0])
+        err = float((got[0].double() - got[1].double()).abs().max() / got[1].double().abs().max())
+        assert err < 1e-2, err
+
+
 def _check_rounding(a, r):
     """16-bit outputs: at most one ulp apart on under 2% of the elements (a row sum in another order can move a
     rounding); float32: a few ulps (no final rounding hides the sum-order difference)."""
