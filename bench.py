@@ -505,7 +505,8 @@ def run_sweep(args) -> None:
                              "gbs": round(gbs, 0), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}  # fmt: skip
             del q, k, v, do, gq, gk, gv, o, lse, dq
             torch.cuda.empty_cache()
-            proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused") if p in args.passes.split(",")]
+            proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused", "gate_up", "gate_up_unfused")
+                    if p in args.passes.split(",")]
             if proj:
                 out.update(sweep_qkv(args, proj, B, L, H, D, pk))
             _native.device_status()
@@ -520,7 +521,7 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     import torch.nn.functional as F
 
     from ebr_b200.energy import Rope2D
-    from ebr_b200.layers import o_proj_op, qkv_rope_split_op, rope_split_op
+    from ebr_b200.layers import gate_up_swiglu_op, o_proj_op, qkv_rope_split_op, rope_split_op, swiglu_act
 
     side = int(round(L**0.5))
     hh, ww = (side, side) if side * side == L else (32, L // 32)
@@ -532,11 +533,15 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     e = torch.zeros(0, device="cuda")
     o = torch.randn(B, H, L, D, device="cuda", generator=g).to(torch.bfloat16)
     wo = (torch.randn(C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
+    inter = -(round(4 * C * 2 / 3) // -256) * 256  # the energy network's SwiGLU width (EnergyConfig expansion 4)
+    wgu = (torch.randn(2 * inter, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     fns = {
         "qkv_rope": lambda: qkv_rope_split_op(x, w, rope.cos_table, rope.sin_table, e, H),
         "qkv_unfused": lambda: rope_split_op(F.linear(x, w), rope.cos_table, rope.sin_table, e, H),
         "o_proj": lambda: o_proj_op(o, wo),
         "o_unfused": lambda: F.linear(o.transpose(1, 2).reshape(B, L, C), wo),
+        "gate_up": lambda: gate_up_swiglu_op(x, wgu),
+        "gate_up_unfused": lambda: swiglu_act(F.linear(x, wgu)),
     }
     res = {}
     for name in passes:
@@ -556,12 +561,15 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         if name.startswith("qkv"):
             flop = 2.0 * B * L * C * 3 * C
             byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)
+        elif name.startswith("gate_up"):
+            flop = 2.0 * B * L * C * 2 * inter
+            byt = 2.0 * (B * L * C + 2 * inter * C + 3 * B * L * inter)  # x, W, h, act
         else:
             flop = 2.0 * B * L * C * C
             byt = 2.0 * (2 * B * L * C + C * C)  # O, W, y
         res[name] = {"ms": round(ms, 4), "tflops": round(flop / ms / 1e9, 1),
                      "tc_frac": round(flop / ms / 1e9 / pk["tf_burst"], 4), "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
-    del x, w, o, wo
+    del x, w, o, wo, wgu
     return res
 
 

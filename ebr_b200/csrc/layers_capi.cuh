@@ -9,6 +9,7 @@
 
 #include "../../include/ebr_layers.h"
 #include "layers.cuh"
+#include "gate_up.cuh"
 #include "o_proj.cuh"
 #include "qkv_rope.cuh"
 
@@ -384,6 +385,41 @@ int ebr_o_proj(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t C_
                    : launch(ebr::tc_o_proj_kernel<__nv_bfloat16, 128>, static_cast<__nv_bfloat16*>(nullptr));
   return D == 64 ? launch(ebr::tc_o_proj_kernel<__half, 64>, static_cast<__half*>(nullptr))
                  : launch(ebr::tc_o_proj_kernel<__half, 128>, static_cast<__half*>(nullptr));
+}
+
+int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void* x, int64_t x_stride, const void* w,
+                       void* h, void* act, void* stream) {
+  if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
+    return set_error(EBR_ERR_DTYPE, "gate_up_swiglu: bfloat16 or float16 only%s%s");
+  if (rows < 0 || C < 1 || I < 1 || C % 64 != 0 || I % 128 != 0 || C > INT32_MAX || I > INT32_MAX / 2)
+    return set_error(EBR_ERR_SHAPE, "gate_up_swiglu: needs C a multiple of 64 and I a multiple of 128%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!x || !w || !h || !act) return set_error(EBR_ERR_NULL, "gate_up_swiglu: NULL pointer%s%s");
+  if (x_stride < C || x_stride % 8 != 0 || !all_aligned16({x, w, h, act}))
+    return set_error(EBR_ERR_STRIDE, "gate_up_swiglu: x rows need a stride >= C, a multiple of 8 elements, and "
+                                     "16-byte aligned pointers%s%s");
+  int device = 0;
+  int rc = check_device(&device);
+  if (rc != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  using L = ebr::GateUpLayout;
+  CUtensorMap tx, tw;
+  if ((rc = make_matrix_map(&tx, x, dtype, rows, C, x_stride, L::kBM)) != EBR_OK) return rc;
+  if ((rc = make_matrix_map(&tw, w, dtype, 2 * I, C, C, 128)) != EBR_OK) return rc;
+  const int64_t m_tiles = (rows + L::kBM - 1) / L::kBM;
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
+  auto launch = [&](auto kernel, auto* out_tag) -> int {
+    using T = std::remove_pointer_t<decltype(out_tag)>;
+    if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))
+      return rc;
+    kernel<<<grid, L::kThreads, L::kSmem, st>>>(tx, tw, rows, static_cast<int>(C), static_cast<int>(I),
+                                                static_cast<T*>(h), static_cast<T*>(act));
+    return check_launch("tc_gate_up_swiglu_kernel");
+  };
+  if (dtype == EBR_BFLOAT16)
+    return launch(ebr::tc_gate_up_swiglu_kernel<__nv_bfloat16>, static_cast<__nv_bfloat16*>(nullptr));
+  return launch(ebr::tc_gate_up_swiglu_kernel<__half>, static_cast<__half*>(nullptr));
 }
 
 }  // extern "C"

@@ -127,7 +127,7 @@ class SwiGLU(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.fused:
-            return self.down(fl.swiglu_act(self.gate_up(x)))
+            return self.down(fl.gate_up_swiglu(x, self.gate_up.weight.to(x.dtype)))
         gate, up = self.gate_up(x).chunk(2, dim=-1)
         return self.down(F.silu(gate) * up)
 

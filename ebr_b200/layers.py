@@ -475,23 +475,100 @@ class _SwiGLUAct(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gout: Tensor):
         (h,) = ctx.saved_tensors
+        return _swiglu_grad(h, gout)
+
+
+def _swiglu_grad(h: Tensor, gout: Tensor) -> Tensor:
+    """d act / d h applied to gout: the fused kernel, or (building a higher-order graph) differentiable torch ops."""
+    if torch.is_grad_enabled():
+        # Differentiable torch ops (aten's silu_backward has no derivative of its own).
+        gate, up = h.chunk(2, dim=-1)
+        gf = gate.to(torch.float32)
+        sg = torch.sigmoid(gf)
+        ga = (gout * up).to(torch.float32)
+        gg = (ga * sg * (1.0 + gf * (1.0 - sg))).to(h.dtype)
+        return torch.cat([gg, gout * F.silu(gate)], dim=-1)
+    gout = gout.to(h.dtype).contiguous()
+    rows, c2 = _rows(h)
+    gh = torch.empty_like(h)
+    _native.check(
+        _native.lib().ebr_swiglu_bwd(_DTYPES[h.dtype], rows, c2 // 2, h.data_ptr(), gout.data_ptr(), gh.data_ptr(),
+                                     _stream()),  # fmt: skip
+        "swiglu_bwd",
+    )
+    return gh
+
+
+@torch.library.custom_op("ebr_fused::gate_up_swiglu", mutates_args=())
+def gate_up_swiglu_op(x: Tensor, weight: Tensor) -> Tuple[Tensor, Tensor]:
+    _require_cuda(x, "gate_up_swiglu")
+    x = x.contiguous()
+    weight = weight.to(x.dtype).contiguous()
+    rows, c = _rows(x)
+    i2 = weight.shape[0]
+    h = torch.empty((*x.shape[:-1], i2), device=x.device, dtype=x.dtype)
+    act = torch.empty((*x.shape[:-1], i2 // 2), device=x.device, dtype=x.dtype)
+    _native.check(
+        _native.lib().ebr_gate_up_swiglu(_DTYPES[x.dtype], rows, c, i2 // 2, x.data_ptr(), c, weight.data_ptr(),
+                                         h.data_ptr(), act.data_ptr(), _stream()),  # fmt: skip
+        "gate_up_swiglu",
+    )
+    return h, act
+
+
+@gate_up_swiglu_op.register_fake
+def _(x, weight):
+    i2 = weight.shape[0]
+    return x.new_empty((*x.shape[:-1], i2)), x.new_empty((*x.shape[:-1], i2 // 2))
+
+
+class _GateUpAct(torch.autograd.Function):
+    """Forward: the gate / up GEMM with the SwiGLU activation as its epilogue (h is kept for the backward). Backward:
+    the activation's gradient from the stored h, then the projection's two products, each only when the running
+    backward reaches its input; building a higher-order graph it recomputes h = x W^T with differentiable ops, so the
+    double backward differentiates through the projection too."""
+
+    @staticmethod
+    def forward(ctx, x, weight):
+        h, act = torch.ops.ebr_fused.gate_up_swiglu(x, weight)
+        ctx.save_for_backward(x, weight, h)
+        ctx.nodes = tuple(get_gradient_edge(t).node if t.requires_grad else None for t in (x, weight))
+        return act
+
+    @staticmethod
+    def backward(ctx, gact):
+        x, weight, h = ctx.saved_tensors
+        need_x, need_w = (_engine_needs(nd) for nd in ctx.nodes)
         if torch.is_grad_enabled():
-            # Differentiable torch ops (aten's silu_backward has no derivative of its own).
-            gate, up = h.chunk(2, dim=-1)
-            gf = gate.to(torch.float32)
-            sg = torch.sigmoid(gf)
-            ga = (gout * up).to(torch.float32)
-            gg = (ga * sg * (1.0 + gf * (1.0 - sg))).to(h.dtype)
-            return torch.cat([gg, gout * F.silu(gate)], dim=-1)
-        gout = gout.to(h.dtype).contiguous()
-        rows, c2 = _rows(h)
-        gh = torch.empty_like(h)
-        _native.check(
-            _native.lib().ebr_swiglu_bwd(_DTYPES[h.dtype], rows, c2 // 2, h.data_ptr(), gout.data_ptr(),
-                                         gh.data_ptr(), _stream()),  # fmt: skip
-            "swiglu_bwd",
-        )
-        return gh
+            h = F.linear(x, weight.to(x.dtype))
+        gh = _swiglu_grad(h, gact)
+        gx = gh @ weight.to(gh.dtype) if need_x else None
+        gw = gh.flatten(0, -2).t() @ x.flatten(0, -2) if need_w else None
+        return gx, gw
+
+
+def _gate_up(x: Tensor, weight: Tensor) -> Tensor:
+    return _GateUpAct.apply(x, weight)
+
+
+_gate_up = torch._dynamo.allow_in_graph(_gate_up)
+
+
+def gate_up_fusable(x: Tensor, weight: Tensor) -> bool:
+    """Whether ``ebr_gate_up_swiglu`` serves this projection: 16-bit CUDA ``x`` [..., C] and ``weight`` [2 I, C] of
+    one dtype, C a multiple of 64, I a multiple of 128."""
+    if not x.is_cuda or x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype:
+        return False
+    c = x.shape[-1]
+    return weight.dim() == 2 and weight.shape[1] == c and c % 64 == 0 and weight.shape[0] % 256 == 0
+
+
+def gate_up_swiglu(x: Tensor, weight: Tensor) -> Tensor:
+    """``swiglu_act(F.linear(x, weight))`` as one GEMM with the activation in its epilogue (``ebr_gate_up_swiglu``);
+    shapes it does not take run the GEMM and the activation kernel. Differentiable to every order in x and weight."""
+    if not gate_up_fusable(x, weight):
+        return swiglu_act(F.linear(x, weight.to(x.dtype)))
+    return _gate_up(x, weight)
 
 
 def swiglu_act(h: Tensor) -> Tensor:
@@ -543,6 +620,9 @@ def step_and_project(v: Tensor, g: Tensor, alpha: float, eps: float = 1e-5) -> T
 
 __all__ = [
     "add_rms_norm",
+    "gate_up_fusable",
+    "gate_up_swiglu",
+    "gate_up_swiglu_op",
     "noisy_point",
     "o_proj",
     "o_proj_fusable",

@@ -79,6 +79,15 @@ int ebr_rms_norm_bwd(int dtype, int64_t rows, int64_t C, const void* s, const fl
  * Replaces: F.silu(gate) * up after gate_up_proj(x).chunk(2) (models/layers.py:82-84). */
 int ebr_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* h, void* out, void* stream);
 
+/* The MLP's gate / up projection with the activation as its epilogue (one tensor-core GEMM): h = x W^T [rows, 2 I]
+ * (fp32 accumulation, one rounding to the I/O type; gate columns [0, I), up columns [I, 2 I)) and act [rows, I] exactly
+ * as ebr_swiglu_fwd makes it from that h. x: [rows, C] (row stride x_stride elements), W: [2 I, C] contiguous.
+ * bfloat16 / float16 only; C a multiple of 64, I a multiple of 128, x_stride a multiple of 8, 16-byte aligned
+ * pointers, else EBR_ERR_SHAPE / EBR_ERR_STRIDE. Replaces: gate_up_proj(x) and F.silu(gate) * up
+ * (models/layers.py:80-84). */
+int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void* x, int64_t x_stride, const void* w,
+                       void* h, void* act, void* stream);
+
 /* Its backward: gh [rows, 2 I] = (silu'(gate) * round(gout * up), round(gout * round(silu(gate)))). */
 int ebr_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, void* gh, void* stream);
 

@@ -80,6 +80,14 @@ def test_layer_entry_points_reject_bad_arguments_before_device(lib):
     assert p(_native.BFLOAT16, 1, 4, 8, 64, 256, r(good), None, t, None) == _native.ERR_NULL
     assert p(_native.BFLOAT16, 1, 4, 8, 64, 256, r(good), t + 2, t, None) == _native.ERR_STRIDE
     assert p(_native.BFLOAT16, 0, 4, 8, 64, 256, None, None, None, None) == 0
+    # The gate / up projection: 16-bit only, C % 64 == 0, I % 128 == 0, aligned row stride.
+    gu = lib.ebr_gate_up_swiglu
+    assert gu(_native.FLOAT32, 4, 64, 128, t, 64, t, t, t, None) == _native.ERR_DTYPE
+    assert gu(_native.BFLOAT16, 4, 96, 128, t, 96, t, t, t, None) == _native.ERR_SHAPE
+    assert gu(_native.BFLOAT16, 4, 64, 192, t, 64, t, t, t, None) == _native.ERR_SHAPE
+    assert gu(_native.BFLOAT16, 4, 64, 128, t, 64, None, t, t, None) == _native.ERR_NULL
+    assert gu(_native.BFLOAT16, 4, 64, 128, t, 60, t, t, t, None) == _native.ERR_STRIDE
+    assert gu(_native.BFLOAT16, 0, 64, 128, None, 64, None, None, None, None) == 0
     assert lib.ebr_add_rms_norm(_native.BFLOAT16, 0, 8, 1e-5, None, None, None, None, None, None, 0.0, None) == 0
 
 

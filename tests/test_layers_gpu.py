@@ -308,6 +308,79 @@ def test_o_proj_gradients_match_the_unfused_path_to_second_order():
         assert err < 1e-2, err
 
 
+GU_SHAPES = [(2, 81, 512, 1536), (1, 900, 512, 1536), (3, 100, 256, 128), (2, 37, 128, 256)]
+
+
+def _gu_inputs(shape, dtype, seed):
+    b, n, c, i = shape
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(b, n, c, generator=g).to(dtype).to(DEV)
+    w = (torch.randn(2 * i, c, generator=g) * c**-0.5).to(dtype).to(DEV)
+    return x, w
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", GU_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_gate_up_swiglu_is_the_gemm_then_the_activation(dtype, shape):
+    """h equals cuBLAS with fp32 reduction (but for last-bit differences of a sum taken in another order, bounded by
+    one rounding plus the fp32 summation error) and act equals the activation kernel applied to that h, bit for bit."""
+    from ebr_b200.layers import gate_up_fusable, gate_up_swiglu_op
+
+    b, n, c, i = shape
+    x, w = _gu_inputs(shape, dtype, seed=sum(shape))
+    assert gate_up_fusable(x, w)
+    h, act = gate_up_swiglu_op(x, w)
+    exact = x.double() @ w.double().t()
+    ref = exact.to(dtype)
+    accb = (x.double().abs() @ w.double().abs().t()) * (c * 2.0**-24)
+    eps = torch.finfo(dtype).eps
+    diff = (h.double() - ref.double()).abs()
+    assert bool((diff <= 2 * eps * ref.double().abs() + 2 * accb).all())
+    m = torch.backends.cuda.matmul
+    flags = (m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction)
+    m.allow_bf16_reduced_precision_reduction = m.allow_fp16_reduced_precision_reduction = False
+    try:
+        unfused = F.linear(x, w)
+    finally:
+        m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction = flags
+    assert float((h != unfused).double().mean()) < 0.01
+    from ebr_b200.layers import swiglu_act
+
+    with torch.no_grad():
+        assert torch.equal(act, swiglu_act(h))
+
+
+def test_gate_up_swiglu_gradients_match_the_unfused_path_to_second_order():
+    """First and second derivatives (create_graph) in x and the weight equal those of F.linear + swiglu_act, and a
+    backward asked for one input alone returns that gradient."""
+    from ebr_b200.layers import gate_up_swiglu, swiglu_act
+
+    x0, w0 = _gu_inputs((2, 81, 512, 1536), torch.bfloat16, seed=12)
+    g = torch.Generator(device="cpu").manual_seed(13)
+    r = torch.randn(x0.shape, generator=g).to(x0.dtype).to(DEV)
+
+    def act(x, w, fused):
+        return gate_up_swiglu(x, w) if fused else swiglu_act(F.linear(x, w))
+
+    def run(fused):
+        x, w = x0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+        s = (act(x, w, fused).float() ** 2).sum()
+        gx, gw = torch.autograd.grad(s, (x, w), create_graph=True)
+        hw = torch.autograd.grad((gx.float() * r.float()).sum(), w)[0]
+        return gx, gw, hw
+
+    for a, bb in zip(run(True), run(False)):
+        err = float((a.double() - bb.double()).abs().max() / bb.double().abs().max())
+        assert err < 1e-2, err
+    for want in (0, 1):
+        got = []
+        for fused in (True, False):
+            x, w = x0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+            got.append(torch.autograd.grad((act(x, w, fused).float() ** 2).sum(), (x, w)[want])[0])
+        err = float((got[0].double() - got[1].double()).abs().max() / got[1].double().abs().max())
+        assert err < 1e-2, err
+
+
 def _check_rounding(a, r):
     """16-bit outputs: at most one ulp apart on under 2% of the elements (a row sum in another order can move a
     rounding); float32: a few ulps (no final rounding hides the sum-order difference)."""
