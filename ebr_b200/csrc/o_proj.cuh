@@ -6,19 +6,20 @@
 // partial block of a sample reads zeros past N and stores only its valid rows), an n-tile 256 output columns. A CTA
 // takes whole m-tiles (all of their n-tiles): m-tiles blockIdx.x, blockIdx.x + gridDim.x, ... Roles (320 threads):
 //   warp 8     TMA producer: per 64-wide K block (head h, columns [64 c, 64 c + 64) of it) the O tile [128 x 64] (a
-//              4-D box of one (b, h)) and the W tile [256 x 64], both K-major with 128-byte swizzle, into a 4-stage
+//              4-D box of one (b, h)) and the W tile [256 x 64], both K-major with 128-byte swizzle, into a 3-stage
 //              ring;
 //   warp 9     MMA issuer: 4 x tcgen05.mma M128 N256 K16 per K block into one of two 256-column TMEM accumulators;
 //   warps 0-7  epilogue: warp w owns TMEM lanes [32 (w % 4), +32) (one token per thread) and columns
-//              [128 (w / 4), +128) of the tile; it rounds the fp32 sums to the I/O type and stores them to y.
+//              [128 (w / 4), +128) of the tile; it rounds the fp32 sums to the I/O type and stores them to y through
+//              its shared-memory staging buffer (eight 64-byte row segments per store instruction).
 // The reference's self.o(y.transpose(1, 2).reshape(b, n, h d)) in EnergyAttention (models/attention.py:241-242).
 #pragma once
 
-#include "qkv_rope.cuh"
+#include "gate_up.cuh"
 
 namespace ebr {
 
-using OProjLayout = QkvRopeLayout;  // same tiles, ring and TMEM split
+using OProjLayout = GateUpLayout;  // same tiles, ring, TMEM split and per-warp store staging
 
 // o: 4-D TMA map over O (D, N, H, B), box 64 x 128; w: [C_out, H D] (TMA map, box 64 x 256); y: [B, N, C_out].
 template <typename T, int D>
@@ -112,15 +113,15 @@ __global__ void __launch_bounds__(320, 1)
     // ---------------------------------------------------------------- epilogue
     const int wq = warp & 3, grp = warp >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    unsigned char* stage = smem + L::kStaging + warp * 32 * L::kStagePitch;
     uint32_t lt = 0;
     for (int64_t j = 0;; ++j, ++lt) {
       const int64_t mt = blockIdx.x + (j / n_nt) * gridDim.x;
       if (mt >= n_mt) break;
       const int nt = static_cast<int>(j % n_nt);
       const int b = static_cast<int>(mt / n_nb), nb = static_cast<int>(mt - static_cast<int64_t>(b) * n_nb);
-      const int n = nb * L::kBM + wq * 32 + lane;
-      const bool row_ok = n < N;
-      T* dst = y + (static_cast<int64_t>(b) * N + (row_ok ? n : 0)) * C_out + nt * L::kBN + grp * 128;
+      const int n0 = nb * L::kBM + wq * 32;  // this warp's first token
+      T* dst = y + static_cast<int64_t>(b) * N * C_out + nt * L::kBN + grp * 128;
       const uint32_t ab = lt & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[ab], (lt >> 1) & 1, 831, abort))) break;
       tc_fence_after();
@@ -132,17 +133,26 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < 4; ++c) {
         tmem_wait_ld_regs(r[c & 1]);
         if (c < 3) tmem_ld32(tacc + 32 * (c + 1), r[(c + 1) & 1]);
-        if (row_ok) {
+        // The row's 32 columns go to the warp's staging buffer; lane l then stores 16 bytes (l % 4) of token
+        // n0 + l / 4 + 8 k, so each store instruction writes eight whole 64-byte row segments.
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const uint32_t* v = &r[c & 1][8 * q4];
-            *reinterpret_cast<uint4*>(dst + 32 * c + 8 * q4) =
-                make_uint4(pack2<T>(__uint_as_float(v[0]), __uint_as_float(v[1])),
-                           pack2<T>(__uint_as_float(v[2]), __uint_as_float(v[3])),
-                           pack2<T>(__uint_as_float(v[4]), __uint_as_float(v[5])),
-                           pack2<T>(__uint_as_float(v[6]), __uint_as_float(v[7])));
-          }
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint32_t* v = &r[c & 1][8 * q4];
+          *reinterpret_cast<uint4*>(stage + lane * L::kStagePitch + 16 * q4) =
+              make_uint4(pack2<T>(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                         pack2<T>(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                         pack2<T>(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                         pack2<T>(__uint_as_float(v[6]), __uint_as_float(v[7])));
         }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int rr = lane / 4 + 8 * k;
+          const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * L::kStagePitch + 16 * (lane % 4));
+          if (n0 + rr < N)
+            *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(n0 + rr) * C_out + 32 * c + 8 * (lane % 4)) = val;
+        }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);

@@ -31,10 +31,19 @@ struct QkvRopeLayout {
   static constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KB
   static constexpr int kStages = 4;
   static constexpr uint32_t kStage = kATile + kBTile;
-  static constexpr uint32_t kBytes = kStages * kStage;
+  static constexpr uint32_t kStagePitch = 80;  // bytes per staged row of an epilogue warp (64 of data)
+  static constexpr uint32_t kStaging = kStages * kStage;
+  static constexpr uint32_t kBytes = kStaging + 8 * 32 * kStagePitch;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kThreads = 320;
+};
+
+// The four token rows one epilogue lane stores for its warp (rows l / 4 + 8 k of the warp's 32, k = 0 .. 3): the
+// offset of each row in a [B, H, N, D] tensor at head 0 (-1 for rows past M). A staged chunk of the warp's 32 rows is
+// stored 16 bytes per lane, four lanes per row: eight rows per store instruction.
+struct StoreRows {
+  int64_t off[4];
 };
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -74,8 +83,8 @@ __device__ __forceinline__ uint32_t narrow2(uint64_t v) {
 // rounded to fp32 and then to the I/O type by the store.
 template <typename T, int D>
 __device__ __forceinline__ void qkv_rope_slot2(uint32_t ta0, uint32_t ta1, int da, bool rotate, bool scale_q,
-                                               float qs0, float qs1, const uint64_t (&tab)[32], bool row_ok, T* dst0,
-                                               T* dst1) {
+                                               float qs0, float qs1, const uint64_t (&tab)[32], unsigned char* stage,
+                                               const StoreRows& rows, T* head0, T* head1, int lane) {
   constexpr int kQ = D / 4;
   uint32_t r[4][16];
   tmem_ld16(ta0 + da, r[0]);
@@ -107,13 +116,22 @@ __device__ __forceinline__ void qkv_rope_slot2(uint32_t ta0, uint32_t ta1, int d
         wb[i] = ob;
       }
     }
-    T* dst = hh == 0 ? dst0 : dst1;
-    if (row_ok) {
-      *reinterpret_cast<uint4*>(dst + da) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
-      *reinterpret_cast<uint4*>(dst + da + 8) = make_uint4(wa[4], wa[5], wa[6], wa[7]);
-      *reinterpret_cast<uint4*>(dst + da + kQ) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
-      *reinterpret_cast<uint4*>(dst + da + kQ + 8) = make_uint4(wb[4], wb[5], wb[6], wb[7]);
+    // Stage the row's 64 bytes (elements [da, da + 16) then [da + D / 4, ...)), then store four rows' pieces.
+    uint4* sr = reinterpret_cast<uint4*>(stage + lane * QkvRopeLayout::kStagePitch);
+    sr[0] = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+    sr[1] = make_uint4(wa[4], wa[5], wa[6], wa[7]);
+    sr[2] = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+    sr[3] = make_uint4(wb[4], wb[5], wb[6], wb[7]);
+    __syncwarp();
+    T* head = hh == 0 ? head0 : head1;
+    const int p = lane & 3, col = da + (p < 2 ? 8 * p : kQ + 8 * (p - 2));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int rr = (lane >> 2) + 8 * k;
+      const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * QkvRopeLayout::kStagePitch + 16 * p);
+      if (rows.off[k] >= 0) *reinterpret_cast<uint4*>(head + rows.off[k] + col) = v;
     }
+    __syncwarp();
   }
 }
 
@@ -210,6 +228,7 @@ __global__ void __launch_bounds__(320, 1)
     constexpr int kHeads = L::kBN / D;      // heads per tile
     const int wq = warp & 3, grp = warp >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    unsigned char* stage = smem + L::kStaging + warp * 32 * L::kStagePitch;
     // tab: this thread's table values for one slot of its token row, as f32x2 pairs (see qkv_rope_slot2). At D = 64
     // (one slot) they serve every q / k tile of the m-tile and the next m-tile's are requested during its v tiles,
     // which do not rotate; at D = 128 each slot's are loaded before its use.
@@ -237,14 +256,17 @@ __global__ void __launch_bounds__(320, 1)
       if (mt >= n_mt) break;
       const int nt = static_cast<int>(j % n_nt);
       const uint32_t ab = lt & 1;
-      const int64_t row = mt * L::kBM + wq * 32 + lane;
-      const bool row_ok = row < M;
-      const int64_t b = row_ok ? row / N : 0;
-      const int n = row_ok ? static_cast<int>(row - b * N) : 0;
       const int sec = (nt * L::kBN) / HD, h0 = (nt * L::kBN - sec * HD) / D;  // the tile's part and first head
       const bool rotate = sec != 2, scale_q = sec == 0 && qscale != nullptr;
-      T* base = (sec == 0 ? q : sec == 1 ? k : v) + ((b * H + h0) * N + n) * static_cast<int64_t>(D);
       const int64_t head_stride = static_cast<int64_t>(N) * D;
+      T* base = (sec == 0 ? q : sec == 1 ? k : v) + h0 * head_stride;
+      StoreRows rows;
+#pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {
+        const int64_t tok = mt * L::kBM + wq * 32 + (lane >> 2) + 8 * kq;
+        const int64_t bq = tok / N;
+        rows.off[kq] = tok < M ? (bq * H * N + (tok - bq * N)) * D : -1;
+      }
       if (kSlots == 1 && sec == 2 && h0 == 0 && mt + gridDim.x < n_mt) load_tab(mt + gridDim.x, 0);
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[ab], (lt >> 1) & 1, 631, abort))) break;
       tc_fence_after();
@@ -257,8 +279,8 @@ __global__ void __launch_bounds__(320, 1)
         for (int hl = 0; hl < kHeads; hl += 2) {
           const float qs0 = scale_q ? __ldg(qscale + h0 + hl) : 1.f;
           const float qs1 = scale_q ? __ldg(qscale + h0 + hl + 1) : 1.f;
-          qkv_rope_slot2<T, D>(tacc + hl * D, tacc + (hl + 1) * D, da, rotate, scale_q, qs0, qs1, tab, row_ok,
-                               base + hl * head_stride, base + (hl + 1) * head_stride);
+          qkv_rope_slot2<T, D>(tacc + hl * D, tacc + (hl + 1) * D, da, rotate, scale_q, qs0, qs1, tab, stage, rows,
+                               base + hl * head_stride, base + (hl + 1) * head_stride, lane);
         }
       }
       tc_fence_before();
