@@ -5,8 +5,9 @@
 // One persistent CTA per SM; a tile is 128 rows of x by 128 gate columns [j0, j0 + 128) and the matching 128 up
 // columns [I + j0, I + j0 + 128): the W tile of a K block is two 128-row TMA boxes stacked into one [256 x 64] operand,
 // so one M128 N256 K16 instruction forms both halves. A CTA takes whole m-tiles (all I / 128 column tiles). Roles as in
-// the qkv projection (qkv_rope.cuh): producer warp, MMA warp, eight epilogue warps -- warp w owns TMEM lanes
-// [32 (w % 4), +32) (one row per thread) and the 64 gate / up column pairs [64 (w / 4), +64) of the tile. The epilogue
+// the qkv projection (qkv_rope.cuh): producer warp (16), MMA warp (17), sixteen epilogue warps -- warp w owns TMEM
+// lanes [32 (w % 4), +32) (one row per thread) and the gate / up column pairs [16 g, +16) and [16 (g + 4), +16) of the
+// tile, g = w / 4. The epilogue
 // rounds gate and up to the I/O type (the values the unfused GEMM writes), stores them to h, and forms the activation
 // as ebr_swiglu_fwd does (silu(g) = g / (1 + exp(-g)) in fp32, rounded; times up, rounded).
 // The reference's F.silu(gate) * up after gate_up_proj(x).chunk(2) (models/layers.py:82-84).
@@ -16,26 +17,29 @@
 
 namespace ebr {
 
-// 128 x 256 tiles, 64-wide K blocks, two TMEM accumulators as the qkv projection; a 3-stage ring and, after it, one
-// [32 rows x 80 B] staging buffer per epilogue warp (the output chunks are re-read from it so that four consecutive
-// lanes store one row's 64 bytes: eight rows per instruction instead of 32 scattered 16-byte pieces).
+// 128 x 256 tiles, 64-wide K blocks, two TMEM accumulators as the qkv projection; a 4-stage ring and, after it, one
+// [32 rows x 48 B] staging buffer per epilogue warp (a chunk of 16 columns is re-read from it so that two consecutive
+// lanes store one row's 32 bytes: sixteen whole sectors per store instruction instead of 32 scattered 16-byte pieces).
+// Sixteen epilogue warps (four per TMEM lane quarter) keep enough exponentials and divisions in flight to stay ahead of
+// the tensor pipe; 576 threads leave 96 registers a thread.
 struct GateUpLayout {
   static constexpr int kBM = 128, kBN = 256, kBK = 64;
   static constexpr uint32_t kATile = kBM * kBK * 2;
   static constexpr uint32_t kBTile = kBN * kBK * 2;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = 4;
   static constexpr uint32_t kStage = kATile + kBTile;
-  static constexpr uint32_t kStagePitch = 80;  // bytes per staged row (64 of data, 16 of padding against conflicts)
+  static constexpr int kEpiWarps = 16;
+  static constexpr uint32_t kStagePitch = 48;  // bytes per staged row (32 of data, 16 of padding against conflicts)
   static constexpr uint32_t kStaging = kStages * kStage;
-  static constexpr uint32_t kBytes = kStaging + 8 * 32 * kStagePitch;
+  static constexpr uint32_t kBytes = kStaging + kEpiWarps * 32 * kStagePitch;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = (kEpiWarps + 2) * 32;
 };
 
 // x: [M, C] (TMA map, box 64 x 128); w: [2 I, C] (TMA map, box 64 x 128); h: [M, 2 I]; act: [M, I].
 template <typename T>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(GateUpLayout::kThreads, 1)
     tc_gate_up_swiglu_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                              int64_t M, int C, int I, T* __restrict__ h, T* __restrict__ act) {
   using L = GateUpLayout;
@@ -58,7 +62,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 256);
+      mbar_init(&acc_empty[i], L::kEpiWarps * 32);
     }
     abort_flag = 0;
     fence_barrier_init();
@@ -73,7 +77,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
-  if (warp == 8) {
+  if (warp == L::kEpiWarps) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tx);
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == L::kEpiWarps + 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t id = idesc_f16(is_bf16<T>(), 0, 0, 128, 256);
@@ -120,27 +124,26 @@ __global__ void __launch_bounds__(320, 1)
         if (ok) mma_commit(&acc_full[ab]);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < L::kEpiWarps) {
     // ---------------------------------------------------------------- epilogue
     using layers::mul_rn;
     using layers::rnd;
     const int wq = warp & 3, grp = warp >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     unsigned char* stage = smem + L::kStaging + warp * 32 * L::kStagePitch;
-    // Store a [32 rows x 32 columns] chunk (this warp's rows; row_base + r, columns col .. col + 31 of a row-major
-    // matrix with `ld` elements per row): each lane writes its row's 64 bytes to the staging buffer, then lane l stores
-    // 16 bytes (l % 4) of row l / 4 + 8 k, k = 0 .. 3.
-    auto store_chunk = [&](const uint32_t (&w)[16], T* base, int64_t ld, int64_t row_base, int col) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(stage + lane * L::kStagePitch + 16 * q) =
-            make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    // Store a [32 rows x 16 columns] chunk (this warp's rows row_base + r, columns col .. col + 15 of a row-major
+    // matrix with `ld` elements per row): each lane stages its row's 32 bytes, then lane l stores 16 bytes (l % 2) of
+    // row l / 2 + 16 k, k = 0, 1.
+    auto store_chunk = [&](const uint32_t (&w)[8], T* base, int64_t ld, int64_t row_base, int col) {
+      uint4* sr = reinterpret_cast<uint4*>(stage + lane * L::kStagePitch);
+      sr[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      sr[1] = make_uint4(w[4], w[5], w[6], w[7]);
       __syncwarp();
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int r = lane / 4 + 8 * k;
-        const uint4 v = *reinterpret_cast<const uint4*>(stage + r * L::kStagePitch + 16 * (lane % 4));
-        if (row_base + r < M) *reinterpret_cast<uint4*>(base + (row_base + r) * ld + col + 8 * (lane % 4)) = v;
+      for (int k = 0; k < 2; ++k) {
+        const int r = lane / 2 + 16 * k;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + r * L::kStagePitch + 16 * (lane % 2));
+        if (row_base + r < M) *reinterpret_cast<uint4*>(base + (row_base + r) * ld + col + 8 * (lane % 2)) = v;
       }
       __syncwarp();
     };
@@ -150,21 +153,20 @@ __global__ void __launch_bounds__(320, 1)
       if (mt >= n_mt) break;
       const int nt = static_cast<int>(j % n_nt);
       const int64_t row_base = mt * L::kBM + wq * 32;  // this warp's first row
-      const int c0 = nt * 128 + grp * 64;              // this warpgroup's first gate column
       const uint32_t ab = lt & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full[ab], (lt >> 1) & 1, 931, abort))) break;
       tc_fence_after();
-      const uint32_t tg = tmem + lane_off + ab * 256 + grp * 64, tu = tg + 128;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t rg[32], ru[32];
-        tmem_ld32(tg + c, rg);
-        tmem_ld32(tu + c, ru);
-        tmem_wait_ld_regs(rg);
-        tmem_wait_ld_regs(ru);
-        uint32_t wg[16], wu[16], wa[16];
+      for (int part = 0; part < 2; ++part) {
+        const int cc = 16 * (grp + 4 * part);  // gate / up column pair offset within the tile
+        const uint32_t tg = tmem + lane_off + ab * 256 + cc, tu = tg + 128;
+        uint32_t rg[16], ru[16];
+        tmem_ld16(tg, rg);
+        tmem_ld16(tu, ru);
+        tmem_wait_ld();
+        uint32_t wg[8], wu[8], wa[8];
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
+        for (int p = 0; p < 8; ++p) {
           wg[p] = pack2<T>(__uint_as_float(rg[2 * p]), __uint_as_float(rg[2 * p + 1]));
           wu[p] = pack2<T>(__uint_as_float(ru[2 * p]), __uint_as_float(ru[2 * p + 1]));
           float a2[2];
@@ -176,9 +178,10 @@ __global__ void __launch_bounds__(320, 1)
           }
           wa[p] = pack2<T>(a2[0], a2[1]);
         }
-        store_chunk(wg, h, 2 * static_cast<int64_t>(I), row_base, c0 + c);
-        store_chunk(wu, h, 2 * static_cast<int64_t>(I), row_base, I + c0 + c);
-        store_chunk(wa, act, I, row_base, c0 + c);
+        const int c0 = nt * 128 + cc;
+        store_chunk(wg, h, 2 * static_cast<int64_t>(I), row_base, c0);
+        store_chunk(wu, h, 2 * static_cast<int64_t>(I), row_base, I + c0);
+        store_chunk(wa, act, I, row_base, c0);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);

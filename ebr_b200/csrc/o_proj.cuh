@@ -15,11 +15,26 @@
 // The reference's self.o(y.transpose(1, 2).reshape(b, n, h d)) in EnergyAttention (models/attention.py:241-242).
 #pragma once
 
-#include "gate_up.cuh"
+#include "qkv_rope.cuh"
 
 namespace ebr {
 
-using OProjLayout = GateUpLayout;  // same tiles, ring, TMEM split and per-warp store staging
+// 128 x 256 tiles, 64-wide K blocks, a 3-stage ring, two TMEM accumulators and, after the ring, one [32 rows x 80 B]
+// staging buffer per epilogue warp (a 32-column chunk is re-read from it so that four consecutive lanes store one row's
+// 64 bytes: eight whole row segments per store instruction).
+struct OProjLayout {
+  static constexpr int kBM = 128, kBN = 256, kBK = 64;
+  static constexpr uint32_t kATile = kBM * kBK * 2;
+  static constexpr uint32_t kBTile = kBN * kBK * 2;
+  static constexpr int kStages = 3;
+  static constexpr uint32_t kStage = kATile + kBTile;
+  static constexpr uint32_t kStagePitch = 80;
+  static constexpr uint32_t kStaging = kStages * kStage;
+  static constexpr uint32_t kBytes = kStaging + 8 * 32 * kStagePitch;
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kThreads = 320;
+};
 
 // o: 4-D TMA map over O (D, N, H, B), box 64 x 128; w: [C_out, H D] (TMA map, box 64 x 256); y: [B, N, C_out].
 template <typename T, int D>
