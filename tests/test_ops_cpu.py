@@ -63,3 +63,33 @@ def test_default_scale():
     q = torch.zeros(1, 1, 1, 64)
     assert fused_attn.default_scale(q, None) == 0.125
     assert fused_attn.default_scale(q, 0.3) == 0.3
+
+
+def test_projection_ops_fake_kernels_and_no_cpu_path():
+    """The fused projections' fake kernels give the shapes the CUDA ops return (torch.compile traces through them), the
+    ops refuse CPU tensors, and the Python wrappers' kernel checks turn CPU inputs away (no CPU fallback is taken)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from ebr_b200 import layers
+
+    with FakeTensorMode():
+        x = torch.empty(2, 81, 512, dtype=torch.bfloat16)
+        w_qkv = torch.empty(1536, 512, dtype=torch.bfloat16)
+        tab = torch.empty(81, 64)
+        q, k, v = torch.ops.ebr_fused.qkv_rope_split(x, w_qkv, tab, tab, torch.empty(0), 8)
+        assert q.shape == k.shape == v.shape == (2, 8, 81, 64) and q.dtype == torch.bfloat16
+        o = torch.empty(2, 8, 81, 64, dtype=torch.bfloat16)
+        y = torch.ops.ebr_fused.o_proj(o, torch.empty(512, 512, dtype=torch.bfloat16))
+        assert y.shape == (2, 81, 512)
+        h, act = torch.ops.ebr_fused.gate_up_swiglu(x, torch.empty(3072, 512, dtype=torch.bfloat16))
+        assert h.shape == (2, 81, 3072) and act.shape == (2, 81, 1536)
+    x = torch.zeros(1, 4, 512, dtype=torch.bfloat16)
+    w = torch.zeros(1536, 512, dtype=torch.bfloat16)
+    assert not layers.qkv_fusable(x, w, 8)
+    assert not layers.gate_up_fusable(x, torch.zeros(3072, 512, dtype=torch.bfloat16))
+    o = torch.zeros(1, 8, 4, 64, dtype=torch.bfloat16)
+    assert not layers.o_proj_fusable(o, torch.zeros(512, 512, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="only on CUDA"):
+        torch.ops.ebr_fused.qkv_rope_split(x, w, torch.zeros(4, 64), torch.zeros(4, 64), torch.zeros(0), 8)
+    with pytest.raises(RuntimeError, match="only on CUDA"):
+        torch.ops.ebr_fused.gate_up_swiglu(x, torch.zeros(3072, 512, dtype=torch.bfloat16))
