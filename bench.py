@@ -515,9 +515,11 @@ def run_sweep(args) -> None:
 
 
 def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
-    """The projections of one attention layer at the sweep shape: qkv (x [B, L, H D], W [3 H D, H D]) as the tcgen05
-    GEMM with the RoPE split as its epilogue (``qkv_rope``) and as cuBLAS + the split kernel (``qkv_unfused``); the output
-    projection from the head-major attention output (``o_proj``) and as transpose copy + cuBLAS (``o_unfused``)."""
+    """The projections of one block at the sweep shape: qkv (x [B, L, H D], W [3 H D, H D]) as the tcgen05 GEMM with
+    the RoPE split as its epilogue (``qkv_rope``) and as cuBLAS + the split kernel (``qkv_unfused``); the output
+    projection from the head-major attention output (``o_proj``) and as transpose copy + cuBLAS (``o_unfused``); the
+    MLP's gate / up projection with the SwiGLU activation as its epilogue (``gate_up``) and as cuBLAS + the activation
+    kernel (``gate_up_unfused``)."""
     import torch.nn.functional as F
 
     from ebr_b200.energy import Rope2D
@@ -567,8 +569,9 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         else:
             flop = 2.0 * B * L * C * C
             byt = 2.0 * (2 * B * L * C + C * C)  # O, W, y
-        res[name] = {"ms": round(ms, 4), "tflops": round(flop / ms / 1e9, 1),
-                     "tc_frac": round(flop / ms / 1e9 / pk["tf_burst"], 4), "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
+        tf = flop / ms / 1e9
+        res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "tc_frac": round(tf / pk["tf_burst"], 4),
+                     "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
     del x, w, o, wo, wgu
     return res
 
