@@ -469,7 +469,7 @@ struct BobPipeLayout {
   static constexpr int kThreads = 192;
 };
 
-// Row passes of the double backward for N > 128 or D = 128 (the reference's _bob_row_kernel,
+// Row passes of the double backward at D = 128 (D = 64 uses tc_bob.cuh) (the reference's _bob_row_kernel,
 // triton_kernels.py:347-445, restated with the closed form of reference.py:80-90). An item is 128 query rows of one
 // slice (Q, dO, gQ per item); the key-side tiles K, V, gK, gV stream in steps of 64 keys. Per step the MMA warp forms
 // S = Q K^T, dP = dO V^T, G = gQ K^T + Q gK^T and R = dO gV^T (M = 128, N = 64) in TMEM.
@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
-// Column pass of the double backward for N > 128 or D = 128 (the reference's _bob_col_kernel,
+// Column pass of the double backward at D = 128 (D = 64 uses tc_bob.cuh) (the reference's _bob_col_kernel,
 // triton_kernels.py:448-551): an item is 128 keys of one slice (K, V, gK, gV per item); the query-side tiles Q, dO,
 // gQ stream in steps of 64 queries, with each step's lse, D, E, T staged in shared memory by the producer warp.
 // Per step: S^T, dP^T, G^T = K gQ^T + gK Q^T, R^T = gV dO^T (M = 128 keys, N = 64 queries); the compute warps
