@@ -140,13 +140,13 @@ def maze_tokens(n: int, gen: torch.Generator) -> torch.Tensor:
     return tok
 
 
-def build_model(device, attention=None):
-    from ebr_b200.energy import EnergyConfig, EnergyReasoner
+def build_model(device):
+    """The benchmark network (4 layers, hidden 512, 8 heads x 64, SwiGLU 4x, softplus cell head, bf16) on the 30 x 30
+    board, random weights from a fixed seed."""
+    from ebr_b200.energy import LatentEnergyNet, NetShape
 
     torch.manual_seed(0)
-    layers = "eager" if torch.device(device).type == "cpu" else "fused"
-    cfg = EnergyConfig(board_height=BOARD, board_width=BOARD, vocab_size=5, softplus=True, layers=layers)
-    return EnergyReasoner(cfg, attention=attention).to(device)
+    return LatentEnergyNet(NetShape(board=(BOARD, BOARD), vocab=5, cell_softplus=True)).to(device)
 
 
 def run_segment(model, x: torch.Tensor, z: torch.Tensor):
@@ -157,55 +157,138 @@ def run_segment(model, x: torch.Tensor, z: torch.Tensor):
     return z, e, lowest_energy_pick(e, SAMPLES)
 
 
-# --------------------------------------------------------------------------------------------------------- CPU path
+# --------------------------------------------------------------------------------------------------------- reference
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_installed() -> bool:
+    """The unmodified reference installed by ``baseline/install_reference.sh`` (git-ignored; it travels with the tree)."""
+    return (REF_DIR / "models" / "energy.py").exists() and (REF_DIR / "models" / "fused_attn" / "ops.py").exists()
+
+
+def import_reference(impl: str):
+    """Import the installed reference's ``models.energy`` with ``EBR_FUSED_ATTN_IMPL=impl`` (``reference``: its dense
+    torch path; ``triton``: its Triton kernels, an error if they do not load). Must not share a process with
+    ``ebr_b200.fused_attn``: both register the ``ebr_fused::`` ops."""
+    os.environ["EBR_FUSED_ATTN_IMPL"] = impl
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import models.energy as ref_energy
+
+    return ref_energy
+
+
+def reference_energy_config(ref_energy, *, board: int, vocab: int, softplus: bool, gpu_fast: bool):
+    """The reference's ``EnergyConfig`` for the benchmark architecture (4 layers, hidden 512, 8 heads x 64, SwiGLU 4x,
+    bf16) with the descent settings of its config/arch/ebr.yaml and config/train/maze_hard.yaml. ``gpu_fast``: its
+    own fast GPU recipe (config/train/maze_hard_fast.yaml: fused Triton attention in both tiers, fused RoPE split,
+    compiled dE/dz and descent wrapper, no host syncs); otherwise its eager CPU path (math attention, broadcast RoPE,
+    no compilation)."""
+    attn = "fused" if gpu_fast else "math"
+    return ref_energy.EnergyConfig(
+        seq_len=board * board, vocab_size=vocab, num_layers=4, hidden_size=512, expansion=4.0, num_heads=8,
+        board_height=board, board_width=board, forward_dtype="bfloat16",
+        energy_cell_activation="softplus" if softplus else "linear", attn_backend=attn, attn_nograd_backend=attn,
+        cycles=MICROSTEPS, grad_cycles=7, randomize_min_cycles=MICROSTEPS, reset_cycles_low=7,
+        reset_cycles_high=MICROSTEPS, halt_max_steps=16, halt_exploration_prob=0.0, step_size=250.0,
+        step_size_low=200.0, step_size_high=250.0, init_std=1.0, noise_scale=0.05, noise_cosine=False,
+        noise_settle_hot=0.4, microstep_ce=0.5, microstep_ce_ramp=1.0, convergence_threshold=0.75,
+        convergence_temperature=0.05, convergence_window=2, explore_k=1, energy_compile=gpu_fast,
+        descent_wrapper_compile=gpu_fast, rope_impl="fused" if gpu_fast else "broadcast", avoid_host_syncs=gpu_fast,
+    )  # fmt: skip
+
+
+def reference_network(ref_energy, device, gpu_fast: bool):
+    """The reference's ``InnerNetwork`` (embeddings, energy, descent) for the cfg3 workload, in eval mode."""
+    torch.manual_seed(0)
+    cfg = reference_energy_config(ref_energy, board=BOARD, vocab=5, softplus=True, gpu_fast=gpu_fast)
+    with torch.device(device):
+        net = ref_energy.InnerNetwork(cfg)
+    return net.eval()
 
 
 def cpu_reference_sample(seconds: float = 10.0, rows: int = 2, min_steps: int = 1) -> dict:
-    """The reference's CPU path (dense oracle attention + torch CPU), timed on `rows` rows of the same workload until
-    `seconds` have passed. Returns sample-steps/s and what was run."""
-    from ebr_b200.energy import descend
-    from oracle.torch_attention import oracle_attention
-
+    """The reference's CPU path timed on ``rows`` rows of the cfg3 workload until ``seconds`` have passed: its own
+    eager modules from the installed reference (math attention, ``EBR_FUSED_ATTN_IMPL=reference``, no compilation,
+    one ``EnergyDescent`` microstep per step), else this repository's CPU port (oracle attention inside the oracle's
+    restatement of the network). Returns sample-steps/s and what was run."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    model = build_model("cpu", attention=oracle_attention)
     gen = torch.Generator().manual_seed(1)
     tok = maze_tokens(rows, gen)
-    with torch.no_grad():
-        x = model.input_embeddings(tok)
-    z = model.fresh_states(rows, "cpu")
+    if reference_installed():
+        ref_energy = import_reference("reference")
+        net = reference_network(ref_energy, "cpu", gpu_fast=False)
+        with torch.no_grad():
+            x = net.input_embeddings(tok)
+            z = net.fresh_states((rows, BOARD * BOARD, 512), x)
+        cos_sin = net.cos_sin()
+        step = lambda z_: net.level(z_, x, cos_sin)
+        kind, what = "reference", "the reference's eager path (models/energy.py EnergyDescent, math attention, bf16)"
+    else:
+        from oracle import energy as oe
+        from oracle.torch_attention import oracle_attention
+
+        net = build_model("cpu")
+        state = net.reference_state()
+        spec = {"board": (BOARD, BOARD), "hidden": 512, "heads": 8, "layers": 4, "softplus": True}
+        x = oe.embed(state, spec, tok, torch.bfloat16)
+        z = net.fresh_states(rows)
+        step = lambda z_: oe.microstep(state, spec, z_, x, noise=torch.randn_like(z_) * 0.05,
+                                       attention=oracle_attention)[0]  # fmt: skip
+        kind, what = "port", "the oracle's restatement of the network (numpy oracle attention, torch CPU bf16 layers)"
     steps, t0 = 0, time.perf_counter()
-    while steps < min_steps or time.perf_counter() - t0 < seconds:
-        z, _ = descend(model, z, x, 1)
-        steps += 1
+    with torch.no_grad():
+        while steps < min_steps or time.perf_counter() - t0 < seconds:
+            z = step(z)
+            steps += 1
     dt = time.perf_counter() - t0
     return {
         "value": rows * steps / dt,
         "unit": UNIT,
         "cores": threads,
-        "kind": "port",
-        "sample": f"{rows} rows x {steps} microsteps at L=900 ({dt:.1f} s): numpy oracle attention (fp32), torch CPU "
-        f"bf16 for the rest, {threads} threads",
+        "kind": kind,
+        "sample": f"{rows} rows x {steps} microsteps at L=900 ({dt:.1f} s) through {what}, {threads} threads",
     }
 
 
+def cpu_reference_subprocess(seconds: float) -> dict | None:
+    """``cpu_reference_sample`` in a child process (the reference registers the same ``ebr_fused::`` op names as this
+    package, so they cannot share one)."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0",
+           "--cpu-seconds", str(seconds)]  # fmt: skip
+    env = {**os.environ, "CUDA_VISIBLE_DEVICES": "", "RANK": "0", "WORLD_SIZE": "1"}
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=max(600.0, 20 * seconds))
+        line = [ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1]
+        return json.loads(line)["cpu_baseline"]
+    except (subprocess.SubprocessError, IndexError, KeyError, json.JSONDecodeError):
+        return None
+
+
 def run_reference(args) -> None:
+    """``--impl reference``: the reference's CPU path on the host cores (rank 0 only; other ranks exit at once).
+    Each step is a bounded sample: ``--cpu-seconds`` of microsteps on 2 rows (at least one microstep)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    warm = [cpu_reference_sample(seconds=0.0, rows=2, min_steps=1) for _ in range(max(args.warmup, 0))]
-    del warm
+    for _ in range(max(args.warmup, 0)):
+        cpu_reference_sample(seconds=0.0, rows=2, min_steps=1)
     vals, last = [], None
     for _ in range(args.steps):
-        last = cpu_reference_sample(seconds=0.0, rows=2, min_steps=1)
+        last = cpu_reference_sample(seconds=args.cpu_seconds if args.steps == 1 else 0.0, rows=2, min_steps=1)
         vals.append(last["value"])
     value = statistics.median(vals)
+    cfg = config_dict(INPUTS * SAMPLES, args.gpus)
+    cfg["parallelism"] = "host CPU on rank 0 only: the figure does not grow with n_gpus"
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": UNIT,
         "n_gpus": args.gpus,
+        "cpu_only": True,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": 1000.0 * 2 / value if value else None,
@@ -214,11 +297,53 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded maze-like boards; Maze-Hard is not available offline), random-init weights",
-        "config": config_dict(INPUTS * SAMPLES, args.gpus),
+        "config": cfg,
         "cpu_baseline": {**last, "value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_triton_descent(args) -> None:
+    """``--impl triton``: the reference's own GPU path on this box, for comparison (not a contract arm): its
+    ``InnerNetwork.rollout`` in eval mode with its fast recipe (fused Triton attention and RoPE split, inductor-
+    compiled dE/dz and descent wrapper), one 16-microstep segment per step on the same 640 rows, CUDA events."""
+    if not reference_installed():
+        print(json.dumps({"impl": "triton", "unavailable": "reference not installed (baseline/install_reference.sh)"}))
+        return
+    ref_energy = import_reference("triton")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    net = reference_network(ref_energy, device, gpu_fast=True)
+    rows = INPUTS * SAMPLES
+    gen = torch.Generator().manual_seed(1000)
+    tokens = maze_tokens(INPUTS, gen).repeat_interleave(SAMPLES, dim=0).to(device)
+    plan = ref_energy.SegmentPlan()
+    with torch.no_grad():
+        z = net.fresh_states((rows, BOARD * BOARD, 512), net.input_embeddings(tokens))
+    batch = {"inputs": tokens}
+    for _ in range(max(args.warmup, 1)):
+        with torch.no_grad():
+            z, *_ = net.rollout(z, batch, plan)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        with torch.no_grad():
+            z, *_ = net.rollout(z, batch, plan)
+    b.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b)
+    print(json.dumps({
+        "impl": "triton", "metric": METRIC, "value": round(rows * MICROSTEPS * args.steps / (ms / 1000.0), 3),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "config": {**config_dict(rows, 1), "reference_recipe": "maze_hard_fast (fused Triton attention + RoPE split, "
+                   "energy_compile, descent_wrapper_compile, avoid_host_syncs)"},
+        "clocks": clocks,
+    }), flush=True)  # fmt: skip
 
 
 # --------------------------------------------------------------------------------------------------------- GPU path
@@ -237,14 +362,13 @@ def run_ours(args) -> None:
     if world > 1:
         torch.distributed.barrier()
     model = build_model(device)
-    model.eval()
     rows = INPUTS * SAMPLES
     gen = torch.Generator().manual_seed(1000 + rank)
     tokens_host = maze_tokens(INPUTS, gen).repeat_interleave(SAMPLES, dim=0).pin_memory()
     tokens = tokens_host.to(device)
     with torch.no_grad():
-        x = model.input_embeddings(tokens)
-    z0 = model.fresh_states(rows, device)
+        x = model.embed(tokens)
+    z0 = model.fresh_states(rows)
 
     def barrier():
         if world > 1:
@@ -290,7 +414,7 @@ def run_ours(args) -> None:
     for _ in range(e2e_steps):
         tok_d = tokens_host.to(device, non_blocking=True)
         with torch.no_grad():
-            xx = model.input_embeddings(tok_d)
+            xx = model.embed(tok_d)
         zz, ee, pp = run_segment(model, xx, zz)
         energies_host.copy_(ee, non_blocking=True)
         picks_host.copy_(pp, non_blocking=True)
@@ -334,7 +458,7 @@ def run_ours(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_reference_sample(seconds=args.cpu_seconds)
+        cpu = cpu_reference_subprocess(args.cpu_seconds)
 
     if rank == 0:
         line = {
@@ -383,7 +507,7 @@ def run_train(args) -> None:
     decoded endpoint, backward, one flat-bucket NCCL all-reduce of all gradients, AdamW step."""
     from ebr_b200 import _native, fused_attn, runtime
     from ebr_b200.build import build
-    from ebr_b200.energy import EnergyConfig, EnergyReasoner, train_step_loss
+    from ebr_b200.energy import LatentEnergyNet, NetShape, train_segment_loss
 
     rank, world, local = runtime.init_distributed()
     device = torch.device("cuda", local)
@@ -393,19 +517,18 @@ def run_train(args) -> None:
     if world > 1:
         torch.distributed.barrier()
     torch.manual_seed(0)
-    cfg = EnergyConfig(board_height=TRAIN_BOARD, board_width=TRAIN_BOARD, vocab_size=10)
-    model = EnergyReasoner(cfg).to(device)
+    model = LatentEnergyNet(NetShape(board=(TRAIN_BOARD, TRAIN_BOARD), vocab=10)).to(device)
     runtime.broadcast_model(model)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
     gen = torch.Generator().manual_seed(2000 + rank)
     tok, labels = sudoku_like_tokens(TRAIN_ROWS, gen)
     tok, labels = tok.to(device), labels.to(device)
-    z0 = model.fresh_states(TRAIN_ROWS, device)
+    z0 = model.fresh_states(TRAIN_ROWS)
     params = [p for p in model.parameters() if p.requires_grad]
 
     def step():
-        x = model.input_embeddings(tok)
-        loss = train_step_loss(model, z0, x, labels, prefix=TRAIN_MICROSTEPS - TRAIN_GRADED, graded=TRAIN_GRADED)
+        x = model.embed(tok)
+        loss = train_segment_loss(model, z0, x, labels, prefix=TRAIN_MICROSTEPS - TRAIN_GRADED, graded=TRAIN_GRADED)
         opt.zero_grad(set_to_none=True)
         (loss / (TRAIN_ROWS * world)).backward()
         runtime.allreduce_gradients(params)
@@ -458,12 +581,47 @@ def run_train(args) -> None:
 # --------------------------------------------------------------------------------------------------------- sweep
 
 
-def run_sweep(args) -> None:
-    """BASELINE config 5: each pass alone, bf16, H = 8, B = 262144 // L (per GPU), CUDA events, median of K."""
-    from ebr_b200 import _native
-    from ebr_b200.build import build
+def median_call_ms(fn, args, budget_ms: float = 4000.0) -> float:
+    """Median CUDA-event time of ``fn`` (synchronized on both sides of each call) after ``--warmup`` calls, over
+    ``--steps`` calls, or fewer (at least 3) when that many would take longer than ``budget_ms``."""
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    while len(ts) < args.steps and (len(ts) < 3 or sum(ts) < budget_ms):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
 
-    build()
+
+def run_sweep(args) -> None:
+    """The isolated kernel sweep: each pass alone, bf16, H = 8, B = 262144 // L (per GPU), CUDA events, median of K.
+
+    ``--impl ours``: the sm_100a kernels through ``torch.ops.ebr_fused``. ``--impl triton``: the same ops as the
+    installed reference registers them (its Triton kernels, JIT-compiled for this GPU by Triton, default plans), on
+    the same inputs with the same timing; the projection passes are ours only."""
+    if args.impl == "triton":
+        if not reference_installed():
+            print(json.dumps({"impl": "triton", "unavailable": "reference not installed (baseline/install_reference.sh)"}))
+            return
+        import_reference("triton")
+        from models.fused_attn import ops as _ref_ops  # noqa: F401  (registers ebr_fused:: with the Triton kernels)
+
+        class _NoNative:
+            @staticmethod
+            def device_status() -> None:
+                return None
+
+        _native = _NoNative
+    else:
+        from ebr_b200 import _native
+        from ebr_b200.build import build
+
+        build()
     torch.cuda.set_device(0)
     pk = peaks()
     Ls = [int(v) for v in args.lengths.split(",")]
@@ -481,22 +639,11 @@ def run_sweep(args) -> None:
                 "attn_bwd": lambda: torch.ops.ebr_fused.attn_bwd(q, k, v, o, lse, do, s),
                 "attn_bwd_bwd": lambda: torch.ops.ebr_fused.attn_bwd_bwd(q, k, v, o, lse, do, dq, gq, gk, gv, s),
             }
-            out = {"mode": "sweep", "L": L, "D": D, "B": B, "H": H}
+            out = {"mode": "sweep", "impl": args.impl, "L": L, "D": D, "B": B, "H": H}
             for name, fn in fns.items():
                 if name not in args.passes.split(","):
                     continue
-                for _ in range(max(args.warmup, 1)):
-                    fn()
-                torch.cuda.synchronize()
-                ts = []
-                for _ in range(args.steps):
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record()
-                    fn()
-                    b.record()
-                    torch.cuda.synchronize()
-                    ts.append(a.elapsed_time(b))
-                ms = statistics.median(ts)
+                ms = median_call_ms(fn, args)
                 flop = PASS_FLOP[name] * L * L * D * B * H
                 nd, nn = PASS_BYTES[name]
                 byt = (nd * L * D + nn * L) * B * H
@@ -507,7 +654,7 @@ def run_sweep(args) -> None:
             torch.cuda.empty_cache()
             proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused", "gate_up", "gate_up_unfused")
                     if p in args.passes.split(",")]
-            if proj:
+            if proj and args.impl == "ours":
                 out.update(sweep_qkv(args, proj, B, L, H, D, pk))
             _native.device_status()
             print(json.dumps(out), flush=True)
@@ -522,24 +669,24 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     kernel (``gate_up_unfused``)."""
     import torch.nn.functional as F
 
-    from ebr_b200.energy import Rope2D
+    from ebr_b200.energy import NetShape, rope_tables
     from ebr_b200.layers import gate_up_swiglu_op, o_proj_op, qkv_rope_split_op, rope_split_op, swiglu_act
 
     side = int(round(L**0.5))
     hh, ww = (side, side) if side * side == L else (32, L // 32)
-    rope = Rope2D(D, hh, ww).cuda()
     C = H * D
+    cos_t, sin_t = rope_tables(NetShape(board=(hh, ww), hidden=C, heads=H), device="cuda")
     g = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(B, L, C, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(3 * C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     e = torch.zeros(0, device="cuda")
     o = torch.randn(B, H, L, D, device="cuda", generator=g).to(torch.bfloat16)
     wo = (torch.randn(C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
-    inter = -(round(4 * C * 2 / 3) // -256) * 256  # the energy network's SwiGLU width (EnergyConfig expansion 4)
+    inter = NetShape(hidden=C, heads=H).mlp_width  # the energy network's SwiGLU width (expansion 4)
     wgu = (torch.randn(2 * inter, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     fns = {
-        "qkv_rope": lambda: qkv_rope_split_op(x, w, rope.cos_table, rope.sin_table, e, H),
-        "qkv_unfused": lambda: rope_split_op(F.linear(x, w), rope.cos_table, rope.sin_table, e, H),
+        "qkv_rope": lambda: qkv_rope_split_op(x, w, cos_t, sin_t, e, H),
+        "qkv_unfused": lambda: rope_split_op(F.linear(x, w), cos_t, sin_t, e, H),
         "o_proj": lambda: o_proj_op(o, wo),
         "o_unfused": lambda: F.linear(o.transpose(1, 2).reshape(B, L, C), wo),
         "gate_up": lambda: gate_up_swiglu_op(x, wgu),
@@ -547,19 +694,7 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     }
     res = {}
     for name in passes:
-        fn = fns[name]
-        for _ in range(max(args.warmup, 1)):
-            fn()
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(args.steps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            torch.cuda.synchronize()
-            ts.append(a.elapsed_time(b))
-        ms = statistics.median(ts)
+        ms = median_call_ms(fns[name], args)
         if name.startswith("qkv"):
             flop = 2.0 * B * L * C * 3 * C
             byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)
@@ -581,7 +716,9 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours",
+                    help="reference: the reference's CPU path (the contract's reference arm); triton: the reference's "
+                    "own GPU path on this box (descent or sweep mode)")
     ap.add_argument("--mode", choices=["descent", "sweep", "train"], default="descent")
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
@@ -598,6 +735,8 @@ def main() -> None:
         run_sweep(args)
     elif args.mode == "train":
         run_train(args)
+    elif args.impl == "triton":
+        run_triton_descent(args)
     else:
         run_ours(args)
 

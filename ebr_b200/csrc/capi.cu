@@ -34,6 +34,7 @@ int cuda_error(cudaError_t e, const char* what) {
 // ------------------------------------------------------------------------------------------------ device checks
 
 constexpr int kMaxDevices = 64;
+constexpr int kBoundedWaitTestSite = 9001;  // the site ebr_attn_test_bounded_wait's wait records
 
 int check_device(int* device_out) {
   int dev = 0;
@@ -98,6 +99,10 @@ int check_shape(int dtype, int64_t B, int64_t H, int64_t N, int64_t D) {
   if (D < 1 || D > 256) return set_error(EBR_ERR_SHAPE, "head dim must be in [1, 256]%s%s");
   if (N > (int64_t{1} << 30) || H > (int64_t{1} << 30) || B > (int64_t{1} << 30))
     return set_error(EBR_ERR_SHAPE, "size too large%s%s");
+  // Bound the products before any size arithmetic: the kernels index slices with 32-bit B * H, and rows / scratch
+  // sizes are B * H * N (each factor <= 2^30, so B * H fits and (B * H) * N cannot overflow once B * H < 2^31).
+  if (B * H >= (int64_t{1} << 31) || B * H * N >= (int64_t{1} << 40))
+    return set_error(EBR_ERR_SHAPE, "B * H or B * H * N too large%s%s");
   return EBR_OK;
 }
 
@@ -490,20 +495,56 @@ int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N,
 // to a kernel: it names a host-side stand-in. noalloc_scratch() returns this device's address of it.
 static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[EBR_ATTN_NOALLOC_SCRATCH_BYTES];
 
-// The device address of g_bwd_noalloc_scratch on `device` (the current device), looked up once per device.
-int noalloc_scratch(int device, void** out) {
-  static std::mutex mu;
-  static void* ptrs[kMaxDevices] = {};
-  if (device < 0 || device >= kMaxDevices) return set_error(EBR_ERR_DEVICE, "device index out of range%s%s");
-  std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[device]) {
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+CtxGetCurrent ctx_get_current_fn() {
+  static CtxGetCurrent fn = []() -> CtxGetCurrent {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
-    if (e != cudaSuccess || !p) return cuda_error(e, "cudaGetSymbolAddress(g_bwd_noalloc_scratch)");
-    ptrs[device] = p;
-  }
-  *out = ptrs[device];
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<CtxGetCurrent>(p);
+  }();
+  return fn;
+}
+
+// The address of g_bwd_noalloc_scratch in the calling thread's current CUDA context, looked up with
+// cudaGetSymbolAddress once per context (a symbol has one address per context: the primary context of each device,
+// or a context the caller created with the driver API). Up to kMaxScratchContexts contexts are remembered at once.
+int noalloc_scratch(void** out) {
+  constexpr int kMaxScratchContexts = 64;
+  static std::mutex mu;
+  static CUcontext ctxs[kMaxScratchContexts] = {};
+  static void* ptrs[kMaxScratchContexts] = {};
+  static int next = 0;
+  CtxGetCurrent get_ctx = ctx_get_current_fn();
+  if (!get_ctx) return set_error(EBR_ERR_CUDA, "cuCtxGetCurrent is unavailable%s%s");
+  std::lock_guard<std::mutex> lock(mu);
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuCtxGetCurrent failed%s%s");
+  for (int i = 0; ctx && i < kMaxScratchContexts; ++i)
+    if (ctxs[i] == ctx) {
+      *out = ptrs[i];
+      return EBR_OK;
+    }
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);  // makes the device's primary context current
+  if (e != cudaSuccess || !p) return cuda_error(e, "cudaGetSymbolAddress(g_bwd_noalloc_scratch)");
+  if (!ctx && (get_ctx(&ctx) != CUDA_SUCCESS || !ctx)) return set_error(EBR_ERR_CUDA, "no current CUDA context%s%s");
+  ctxs[next] = ctx;
+  ptrs[next] = p;
+  next = (next + 1) % kMaxScratchContexts;
+  *out = p;
   return EBR_OK;
+}
+
+// One thread waits, with a limit of `limit_ns`, on an mbarrier that nothing completes (ebr_attn_test_bounded_wait).
+__global__ void bounded_wait_test_kernel(uint64_t limit_ns, int site) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  mbar_wait_limited(&bar, 0, site, limit_ns);
 }
 
 }  // namespace
@@ -700,7 +741,7 @@ int ebr_attn_bwd_noalloc(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, 
   int device = 0;
   if ((s = check_device(&device))) return s;
   void* scratch = nullptr;
-  if ((s = noalloc_scratch(device, &scratch))) return s;
+  if ((s = noalloc_scratch(&scratch))) return s;
   return ebr_attn_bwd(dtype, B, H, N, D, scale, q, k, v, o, lse, dout, dq, dk, dv, scratch,
                       EBR_ATTN_NOALLOC_SCRATCH_BYTES, stream);
 }
@@ -718,6 +759,15 @@ int ebr_attn_device_status(void) {
     return EBR_ERR_DEVICE_TIMEOUT;
   }
   return EBR_OK;
+}
+
+int ebr_attn_test_bounded_wait(int64_t limit_ns, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000) return set_error(EBR_ERR_SHAPE, "limit_ns must be in [1 us, 1 s]%s%s");
+  int device = 0, s;
+  if ((s = check_device(&device))) return s;
+  bounded_wait_test_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(limit_ns),
+                                                                          kBoundedWaitTestSite);
+  return check_launch("bounded_wait_test_kernel");
 }
 
 const char* ebr_attn_status_string(int status) {

@@ -77,19 +77,24 @@ __device__ __forceinline__ bool mbar_test(const uint64_t* bar, uint32_t parity) 
   return done != 0;
 }
 
-// Wait for the phase with the given parity to complete. Bounded: after kWaitLimitNs it records `site` in the device
+// Wait for the phase with the given parity to complete. Bounded: after `limit_ns` it records `site` in the device
 // error word and returns false, so the kernel can unwind instead of hanging the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
+__device__ __forceinline__ bool mbar_wait_limited(uint64_t* bar, uint32_t parity, int site, uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       atomicExch(&g_device_error, site);
       return false;
     }
   }
+}
+
+// mbar_wait_limited with the kernels' limit, kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
+  return mbar_wait_limited(bar, parity, site, kWaitLimitNs);
 }
 
 // As mbar_wait, but also gives up at once when another role of the CTA has raised `*abort` (so one failed wait does

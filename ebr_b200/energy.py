@@ -1,375 +1,325 @@
-"""The energy network E(z; x) and its latent descent: the caller of the attention path.
+"""Latent-descent energy network on the sm_100a kernels: the caller that drives the attention hot path.
 
-This restates the parts of the reference's model code that drive the hot path, with the same shapes, dtypes and
-call semantics, so the benchmark exercises the sm_100a attention exactly as the reference's training and evaluation
-loops do:
+The network computes the reference's scalar energy E(z; x) and its descent microstep (``models/energy.py``
+``ScalarEnergy`` :190-216, ``EnergyDescent.forward`` :285-319; blocks of ``models/attention.py`` :181-266), but is
+built as a pipeline of this package's fused CUDA ops rather than as a tree of layer modules:
 
-* ``rms_norm`` / ``CastedLinear`` / ``CastedEmbedding`` / ``SwiGLU`` / 2D RoPE: ``models/layers.py:37-132``;
-* ``EnergyAttention``: qkv projection, 2D RoPE, per-head temperature ``exp(log_logit_scale)``, attention on
-  ``[B, H, N, D]`` views, o projection (``models/attention.py:181-242``); post-norm block
-  (``models/attention.py:248-266``);
-* ``ScalarEnergy`` = sum over cells of a per-cell head on top of the blocks (``models/energy.py:190-216``);
-* ``EnergyDescent.forward``: one microstep ``z <- sphere(rms_norm(z) + sigma * eps - alpha * dE/dv)`` with
-  ``create_graph`` in graded (training) microsteps (``models/energy.py:219-222``, ``:285-350``);
-* ``descend`` runs a segment of microsteps; ``lowest_energy_pick`` keeps the lowest-energy sample of each input
-  (``evaluators/protocol.py:10-12``).
+    h = v + x
+    per block:  q, k, v = qkv_rope_split(h W_qkv^T)        (one tcgen05 GEMM; 2D RoPE + head-major layout epilogue)
+                y = fused_attention(q * temperature, k, v)  (the sm_100a forward / backward / double backward)
+                h = add_rms_norm(h, o_proj(y))              (projection read from the head-major output)
+                h = add_rms_norm(h, gate_up_swiglu(h) W_down^T)
+    E = sum over cells of  w2 . silu(W1 h + b1)   (softplus per cell when the head is non-negative)
 
-The attention is ``ebr_b200.fused_attn.fused_attention`` unless a caller injects another callable with the same
-signature (the CPU baseline of the benchmark injects the oracle there); there is no backend registry or fallback.
+Parameters live in one flat module (``LatentEnergyNet``) in float32 and are cast to the compute dtype at use, as the
+reference's casted layers do; ``load_reference_state`` / ``reference_state`` translate to and from the reference's
+state-dict names, so weights move between the two and the golden tests pin this network to the reference's outputs.
+Every op runs on CUDA; there is no CPU path (the CPU restatement used as a yardstick lives in the test oracle).
 
-``EnergyConfig.layers`` picks how the layers around the attention run: ``"fused"`` (CUDA: the kernels of
-``ebr_b200.layers`` -- the 2D-RoPE split / merge, residual + rms_norm, the SwiGLU activation, and the pointwise ops of
-inference microsteps) or ``"eager"`` (plain torch ops, the reference's ``rope_impl: eager`` code; the CPU model and
-the parity yardstick). As in the reference (``models/attention.py:215-242``), the per-head temperature is folded into
-the RoPE split only outside the graded window, where log_logit_scale needs no gradient.
+Graded microsteps (those differentiated again by training) apply the per-head temperature as a differentiable
+product; elsewhere it is folded into the projection's epilogue, as the reference does (``models/attention.py``
+:228-240).
 """
 
 from __future__ import annotations
 
-import contextlib
 import math
-import threading
 from dataclasses import dataclass
-from typing import Callable
+from typing import Callable, Optional
 
 import torch
 import torch.nn.functional as F
-from torch import nn
+from torch import Tensor, nn
 
 from ebr_b200 import layers as fl
 from ebr_b200.fused_attn import fused_attention
 
-RMS_NORM_EPS = 1e-5
-ROPE_THETA = 10000.0
-
-AttentionFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+AttentionFn = Callable[[Tensor, Tensor, Tensor], Tensor]
 
 
-def _fused(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-    return fused_attention(q, k, v, scale=q.shape[-1] ** -0.5)
+@dataclass(frozen=True)
+class NetShape:
+    """Architecture and descent settings. Defaults: the benchmark network (4 layers, hidden 512, 8 heads x 64, SwiGLU
+    4x, bf16) with the reference's eval descent (step 250, noise 0.05, config/arch/ebr.yaml)."""
 
-
-_window = threading.local()
-
-
-@contextlib.contextmanager
-def second_order_window(enabled: bool):
-    """Mark the energy evaluations inside as graded (their dE/dz is differentiated again), thread-locally
-    (``models/attention.py:22-37``)."""
-    prev = getattr(_window, "graded", False)
-    _window.graded = enabled
-    try:
-        yield
-    finally:
-        _window.graded = prev
-
-
-def second_order_required() -> bool:
-    return getattr(_window, "graded", False)
-
-
-# ------------------------------------------------------------------------------------------------------------ layers
-
-
-def trunc_normal_(t: torch.Tensor, std: float = 1.0, lower: float = -2.0, upper: float = 2.0) -> torch.Tensor:
-    """Normal truncated to [lower, upper] standard deviations, rescaled to standard deviation ``std``."""
-    with torch.no_grad():
-        if std == 0:
-            return t.zero_()
-        sqrt2 = math.sqrt(2.0)
-        a, b = math.erf(lower / sqrt2), math.erf(upper / sqrt2)
-        z = (b - a) / 2.0
-        c = (2.0 * math.pi) ** -0.5
-        pdf_u, pdf_l = c * math.exp(-0.5 * lower**2), c * math.exp(-0.5 * upper**2)
-        comp_std = std / math.sqrt(1.0 - (upper * pdf_u - lower * pdf_l) / z - ((pdf_u - pdf_l) / z) ** 2)
-        t.uniform_(a, b).erfinv_().mul_(sqrt2 * comp_std).clip_(lower * comp_std, upper * comp_std)
-        return t
-
-
-def rms_norm(x: torch.Tensor, eps: float = RMS_NORM_EPS) -> torch.Tensor:
-    """Unit RMS over the last dim, computed in float32, returned in the input dtype."""
-    dtype = x.dtype
-    x = x.to(torch.float32)
-    return (x * torch.rsqrt(x.square().mean(-1, keepdim=True) + eps)).to(dtype)
-
-
-class CastedLinear(nn.Module):
-    """Linear layer with float32 weights cast to the input dtype at use."""
-
-    def __init__(self, fan_in: int, fan_out: int, bias: bool) -> None:
-        super().__init__()
-        self.weight = nn.Parameter(trunc_normal_(torch.empty(fan_out, fan_in), std=fan_in**-0.5))
-        self.bias = nn.Parameter(torch.zeros(fan_out)) if bias else None
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        b = self.bias.to(x.dtype) if self.bias is not None else None
-        return F.linear(x, self.weight.to(x.dtype), b)
-
-
-class CastedEmbedding(nn.Module):
-    def __init__(self, num: int, dim: int, init_std: float, cast_to: torch.dtype) -> None:
-        super().__init__()
-        self.cast_to = cast_to
-        self.weight = nn.Parameter(trunc_normal_(torch.empty(num, dim), std=init_std))
-
-    def forward(self, ids: torch.Tensor) -> torch.Tensor:
-        return F.embedding(ids, self.weight.to(self.cast_to))
-
-
-class SwiGLU(nn.Module):
-    def __init__(self, hidden: int, expansion: float, fused: bool = False) -> None:
-        super().__init__()
-        inter = round(expansion * hidden * 2 / 3)
-        inter = -(inter // -256) * 256
-        self.gate_up = CastedLinear(hidden, 2 * inter, bias=False)
-        self.down = CastedLinear(inter, hidden, bias=False)
-        self.fused = fused
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.fused:
-            return self.down(fl.gate_up_swiglu(x, self.gate_up.weight.to(x.dtype)))
-        gate, up = self.gate_up(x).chunk(2, dim=-1)
-        return self.down(F.silu(gate) * up)
-
-
-def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-    x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2 :]
-    return torch.cat((-x2, x1), dim=-1)
-
-
-class Rope2D(nn.Module):
-    """2D RoPE over a height x width board: the first half of each head's channels rotates with the row, the second
-    half with the column."""
-
-    def __init__(self, head_dim: int, height: int, width: int, base: float = ROPE_THETA) -> None:
-        super().__init__()
-        half = head_dim // 2
-        inv = 1.0 / (base ** (torch.arange(0, half, 2, dtype=torch.float32) / half))
-        rows = torch.outer(torch.arange(height, dtype=torch.float32), inv)
-        cols = torch.outer(torch.arange(width, dtype=torch.float32), inv)
-        rows, cols = torch.cat((rows, rows), -1), torch.cat((cols, cols), -1)
-        self.height, self.width = height, width
-        self.register_buffer("cos_h", rows.cos(), persistent=False)
-        self.register_buffer("sin_h", rows.sin(), persistent=False)
-        self.register_buffer("cos_w", cols.cos(), persistent=False)
-        self.register_buffer("sin_w", cols.sin(), persistent=False)
-        # The same angles as [height * width, D] tables for the fused split (sign of rotate_half folded into sin).
-        cos_t, sin_t = fl.rotary_tables(self.cos_h, self.sin_h, self.cos_w, self.sin_w)
-        self.register_buffer("cos_table", cos_t, persistent=False)
-        self.register_buffer("sin_table", sin_t, persistent=False)
-
-    def apply(self, q: torch.Tensor, k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """q, k: [B, N, heads, D] with N = height * width."""
-        ch, sh = self.cos_h[None, :, None, None, :], self.sin_h[None, :, None, None, :]
-        cw, sw = self.cos_w[None, None, :, None, :], self.sin_w[None, None, :, None, :]
-
-        def rot(x: torch.Tensor) -> torch.Tensor:
-            b, n, heads, d = x.shape
-            g = x.reshape(b, self.height, self.width, heads, d).to(ch.dtype)
-            r, c = g[..., : d // 2], g[..., d // 2 :]
-            r = r * ch + _rotate_half(r) * sh
-            c = c * cw + _rotate_half(c) * sw
-            return torch.cat([r, c], -1).to(x.dtype).reshape(b, n, heads, d)
-
-        return rot(q), rot(k)
-
-
-# ------------------------------------------------------------------------------------------------------------ blocks
-
-
-class EnergyAttention(nn.Module):
-    def __init__(self, hidden: int, heads: int, attention: AttentionFn | None = None, fused: bool = False) -> None:
-        super().__init__()
-        self.heads, self.head_dim = heads, hidden // heads
-        self.qkv = CastedLinear(hidden, 3 * hidden, bias=False)
-        self.o = CastedLinear(hidden, hidden, bias=False)
-        self.log_logit_scale = nn.Parameter(torch.zeros(heads))
-        self.attention = attention or _fused
-        self.fused = fused
-
-    def forward(self, rope: Rope2D, x: torch.Tensor) -> torch.Tensor:
-        b, n, _ = x.shape
-        h, d = self.heads, self.head_dim
-        temperature_applied = False
-        if self.fused:
-            # One kernel: the projection GEMM with split + 2D RoPE + head-major layout (+ the temperature outside the
-            # graded window) as its epilogue.
-            qscale = None
-            if not second_order_required():
-                qscale = self.log_logit_scale.detach().exp().to(x.dtype)
-                temperature_applied = True
-            q, k, v = fl.qkv_rope_split(x, self.qkv.weight.to(x.dtype), rope.cos_table, rope.sin_table, h, qscale)
-        else:
-            q, k, v = self.qkv(x).split([h * d] * 3, dim=-1)
-            q, k, v = q.view(b, n, h, d), k.view(b, n, h, d), v.view(b, n, h, d)
-            q, k = rope.apply(q, k)
-            q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-        if not temperature_applied:
-            q = q * self.log_logit_scale.exp().to(q.dtype).view(1, -1, 1, 1)
-        y = self.attention(q, k, v)
-        if self.fused:
-            # The projection reads the head-major attention output directly (no transpose copy).
-            return fl.o_proj(y, self.o.weight.to(y.dtype))
-        return self.o(y.transpose(1, 2).reshape(b, n, h * d))
-
-
-class Block(nn.Module):
-    def __init__(self, hidden: int, heads: int, expansion: float, attention: AttentionFn | None = None,
-                 fused: bool = False) -> None:  # fmt: skip
-        super().__init__()
-        self.attn = EnergyAttention(hidden, heads, attention, fused)
-        self.mlp = SwiGLU(hidden, expansion, fused)
-        self.fused = fused
-
-    def forward(self, rope: Rope2D, x: torch.Tensor) -> torch.Tensor:
-        if self.fused:
-            x = fl.add_rms_norm(x, self.attn(rope, x), RMS_NORM_EPS)
-            return fl.add_rms_norm(x, self.mlp(x), RMS_NORM_EPS)
-        x = rms_norm(x + self.attn(rope, x))
-        return rms_norm(x + self.mlp(x))
-
-
-class ScalarEnergy(nn.Module):
-    """E(z, x): blocks over z + x, then the sum over cells of a per-cell scalar head. Returns [B] float32."""
-
-    def __init__(self, hidden: int, heads: int, layers: int, expansion: float, softplus: bool,
-                 attention: AttentionFn | None = None, fused: bool = False) -> None:  # fmt: skip
-        super().__init__()
-        self.blocks = nn.ModuleList(Block(hidden, heads, expansion, attention, fused) for _ in range(layers))
-        self.head_hidden = CastedLinear(hidden, hidden, bias=True)
-        self.head_out = CastedLinear(hidden, 1, bias=False)
-        self.softplus = softplus
-
-    def forward(self, z: torch.Tensor, x: torch.Tensor, rope: Rope2D) -> torch.Tensor:
-        h = z + x
-        for blk in self.blocks:
-            h = blk(rope, h)
-        raw = self.head_out(F.silu(self.head_hidden(h)))
-        if self.softplus:
-            raw = F.softplus(raw.to(torch.float32))
-        return raw.to(torch.float32).squeeze(-1).sum(dim=1)
-
-
-def sphere(z: torch.Tensor, eps: float = RMS_NORM_EPS) -> torch.Tensor:
-    """Rescale each row (the whole board) to unit RMS, in float32."""
-    rms = z.to(torch.float32).square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(eps)
-    return (z.to(torch.float32) / rms).to(z.dtype)
-
-
-# ------------------------------------------------------------------------------------------------------------ model
-
-
-@dataclass
-class EnergyConfig:
-    """The benchmark architecture: 4 layers, hidden 512, 8 heads x 64, SwiGLU 4x."""
-
-    board_height: int = 9
-    board_width: int = 9
-    vocab_size: int = 10
-    hidden_size: int = 512
-    num_heads: int = 8
-    num_layers: int = 4
+    board: tuple[int, int] = (9, 9)
+    vocab: int = 10
+    hidden: int = 512
+    heads: int = 8
+    layers: int = 4
     expansion: float = 4.0
-    forward_dtype: torch.dtype = torch.bfloat16
-    softplus: bool = False
+    cell_softplus: bool = False
+    dtype: torch.dtype = torch.bfloat16
+    eps: float = 1e-5
+    rope_base: float = 10000.0
     step_size: float = 250.0
     noise_scale: float = 0.05
     init_std: float = 1.0
-    layers: str = "fused"  # "fused" (CUDA kernels around the attention) or "eager" (torch ops; CPU)
 
     @property
     def seq_len(self) -> int:
-        return self.board_height * self.board_width
+        return self.board[0] * self.board[1]
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+    @property
+    def mlp_width(self) -> int:
+        """2/3 of ``expansion * hidden`` rounded up to a multiple of 256 (the reference's SwiGLU width rule,
+        ``models/layers.py:74-80``)."""
+        width = round(self.expansion * self.hidden * 2 / 3)
+        return (width + 255) // 256 * 256
 
 
-class EnergyReasoner(nn.Module):
-    """Token embedding + energy + one descent microstep (``models/energy.py:264-319``, ``:447-490``)."""
+def rope_tables(shape: NetShape, device=None) -> tuple[Tensor, Tensor]:
+    """``[H * W, D]`` cos / sign-folded sin tables of the 2D rotation: the first half of each head's channels turns
+    with the cell's row, the second with its column, at frequencies ``1 / base^(2i / (D / 2))`` (the angles of the
+    reference's ``RotaryEmbedding2D``, ``models/layers.py:98-117``, evaluated in the same form so that the tables
+    agree to the last bit)."""
+    half = shape.head_dim // 2
+    freq = 1.0 / (shape.rope_base ** (torch.arange(0, half, 2, dtype=torch.float32, device=device) / half))
+    ang_h = torch.outer(torch.arange(shape.board[0], dtype=torch.float32, device=device), freq).repeat(1, 2)
+    ang_w = torch.outer(torch.arange(shape.board[1], dtype=torch.float32, device=device), freq).repeat(1, 2)
+    return fl.rotary_tables(ang_h.cos(), ang_h.sin(), ang_w.cos(), ang_w.sin())
 
-    def __init__(self, cfg: EnergyConfig, attention: AttentionFn | None = None) -> None:
+
+class _BlockWeights(nn.Module):
+    def __init__(self, shape: NetShape) -> None:
         super().__init__()
-        self.cfg = cfg
-        self.embed_scale = math.sqrt(cfg.hidden_size)
-        self.embed = CastedEmbedding(cfg.vocab_size, cfg.hidden_size, 1.0 / self.embed_scale, cfg.forward_dtype)
-        self.lm_head = CastedLinear(cfg.hidden_size, cfg.vocab_size, bias=False)
-        self.rope = Rope2D(cfg.hidden_size // cfg.num_heads, cfg.board_height, cfg.board_width)
-        if cfg.layers not in ("fused", "eager"):
-            raise ValueError(f"EnergyConfig.layers must be 'fused' or 'eager', got {cfg.layers!r}")
-        self.fused = cfg.layers == "fused"
-        self.energy = ScalarEnergy(cfg.hidden_size, cfg.num_heads, cfg.num_layers, cfg.expansion, cfg.softplus,
-                                   attention, self.fused)  # fmt: skip
+        c, w = shape.hidden, shape.mlp_width
+        self.w_qkv = nn.Parameter(torch.empty(3 * c, c))
+        self.w_out = nn.Parameter(torch.empty(c, c))
+        self.log_temp = nn.Parameter(torch.zeros(shape.heads))
+        self.w_gate_up = nn.Parameter(torch.empty(2 * w, c))
+        self.w_down = nn.Parameter(torch.empty(c, w))
 
-    def input_embeddings(self, tokens: torch.Tensor) -> torch.Tensor:
-        return self.embed_scale * self.embed(tokens.to(torch.int32))
 
-    def fresh_states(self, rows: int, device, generator: torch.Generator | None = None) -> torch.Tensor:
-        shape = (rows, self.cfg.seq_len, self.cfg.hidden_size)
-        z = torch.empty(shape, device=device, dtype=torch.float32)
-        if generator is None:
-            trunc_normal_(z, std=self.cfg.init_std)
-        else:
-            z.normal_(generator=generator).clamp_(-2.0, 2.0)
-        return z.to(self.cfg.forward_dtype)
+# this module's parameter name -> the reference's state-dict name ({i}: block index)
+_BLOCK_NAMES = {
+    "log_temp": "level.energy.layers.{i}.self_attn.log_logit_scale",
+    "w_qkv": "level.energy.layers.{i}.self_attn.qkv_proj.weight",
+    "w_out": "level.energy.layers.{i}.self_attn.o_proj.weight",
+    "w_gate_up": "level.energy.layers.{i}.mlp.gate_up_proj.weight",
+    "w_down": "level.energy.layers.{i}.mlp.down_proj.weight",
+}
+_TOP_NAMES = {
+    "embedding": "embed_tokens.embedding_weight",
+    "readout": "lm_head.weight",
+    "cell_w1": "level.energy.energy_head.hidden.weight",
+    "cell_b1": "level.energy.energy_head.hidden.bias",
+    "cell_w2": "level.energy.energy_head.output.weight",
+}
 
-    def energy_and_grad(self, v: torch.Tensor, x: torch.Tensor, create_graph: bool):
-        """E(v, x) per row and dE/dv (``_energy_gradient``, ``models/energy.py:345-350``)."""
-        with torch.enable_grad(), second_order_window(create_graph):
+
+class LatentEnergyNet(nn.Module):
+    """Token embedding, the energy E(z; x), dE/dz, the descent microstep and the readout, on CUDA.
+
+    ``attention`` replaces the sm_100a attention by another callable with the same ``(q, k, v) -> o`` contract on
+    ``[B, H, N, D]`` tensors; the tests use it to measure the kernels against softmax attention inside the same
+    network. There is no registry and no fallback: the default is ``fused_attention``."""
+
+    def __init__(self, shape: NetShape, attention: Optional[AttentionFn] = None,
+                 generator: Optional[torch.Generator] = None) -> None:  # fmt: skip
+        super().__init__()
+        self.shape = shape
+        c, v = shape.hidden, shape.vocab
+        self.embedding = nn.Parameter(torch.empty(v, c))
+        self.readout = nn.Parameter(torch.empty(v, c))
+        self.blocks = nn.ModuleList(_BlockWeights(shape) for _ in range(shape.layers))
+        self.cell_w1 = nn.Parameter(torch.empty(c, c))
+        self.cell_b1 = nn.Parameter(torch.zeros(c))
+        self.cell_w2 = nn.Parameter(torch.empty(1, c))
+        cos, sin = rope_tables(shape)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+        self._attention = attention
+        self.reset_parameters(generator)
+
+    # -- parameters -------------------------------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def reset_parameters(self, generator: Optional[torch.Generator] = None) -> None:
+        """Truncated normals (two standard deviations) with fan-in scaling; the embedding at 1/sqrt(hidden); zero
+        temperatures and bias."""
+
+        def fill(t: Tensor, std: float) -> None:
+            t.copy_(torch.randn(t.shape, generator=generator, device=t.device).clamp_(-2.0, 2.0) * std)
+
+        fill(self.embedding, self.shape.hidden**-0.5)
+        fill(self.readout, self.shape.hidden**-0.5)
+        for blk in self.blocks:
+            for w in (blk.w_qkv, blk.w_out, blk.w_gate_up, blk.w_down):
+                fill(w, w.shape[1] ** -0.5)
+            blk.log_temp.zero_()
+        fill(self.cell_w1, self.shape.hidden**-0.5)
+        self.cell_b1.zero_()
+        fill(self.cell_w2, self.shape.hidden**-0.5)
+
+    def _name_map(self) -> dict[str, str]:
+        out = dict(_TOP_NAMES)
+        for i in range(len(self.blocks)):
+            for mine, ref in _BLOCK_NAMES.items():
+                out[f"blocks.{i}.{mine}"] = ref.format(i=i)
+        return out
+
+    @torch.no_grad()
+    def load_reference_state(self, state: dict[str, Tensor]) -> None:
+        """Copy weights from a state dict in the reference's names (``InnerNetwork.state_dict()``); every parameter
+        of this network must be present."""
+        own = dict(self.named_parameters())
+        for mine, ref in self._name_map().items():
+            if ref not in state:
+                raise KeyError(f"reference state lacks {ref!r}")
+            own[mine].copy_(state[ref].to(own[mine].device, torch.float32))
+
+    @torch.no_grad()
+    def reference_state(self) -> dict[str, Tensor]:
+        """This network's weights under the reference's state-dict names."""
+        own = dict(self.named_parameters())
+        return {ref: own[mine].detach().clone() for mine, ref in self._name_map().items()}
+
+    # -- energy -----------------------------------------------------------------------------------------------------
+
+    def embed(self, tokens: Tensor) -> Tensor:
+        """x = sqrt(hidden) * embedding[tokens] in the compute dtype, ``[B, L, hidden]``."""
+        dt = self.shape.dtype
+        return F.embedding(tokens.to(torch.int32), self.embedding.to(dt)) * math.sqrt(self.shape.hidden)
+
+    def fresh_states(self, rows: int, generator: Optional[torch.Generator] = None) -> Tensor:
+        """Initial latents ``[rows, L, hidden]``: a normal truncated at two standard deviations, times init_std."""
+        s = self.shape
+        z = torch.randn((rows, s.seq_len, s.hidden), generator=generator, device=self.embedding.device)
+        return (z.clamp_(-2.0, 2.0) * s.init_std).to(s.dtype)
+
+    def _attend(self, q: Tensor, k: Tensor, v: Tensor) -> Tensor:
+        if self._attention is not None:
+            return self._attention(q, k, v)
+        return fused_attention(q, k, v, scale=q.shape[-1] ** -0.5)
+
+    def _block(self, blk: _BlockWeights, h: Tensor, graded: bool) -> Tensor:
+        s, dt = self.shape, h.dtype
+        folded = None if graded else blk.log_temp.detach().exp().to(dt)
+        q, k, v = fl.qkv_rope_split(h, blk.w_qkv.to(dt), self.rope_cos, self.rope_sin, s.heads, folded)
+        if graded:
+            q = q * blk.log_temp.exp().to(dt).view(1, -1, 1, 1)
+        h = fl.add_rms_norm(h, fl.o_proj(self._attend(q, k, v), blk.w_out.to(dt)), s.eps)
+        mlp = F.linear(fl.gate_up_swiglu(h, blk.w_gate_up.to(dt)), blk.w_down.to(dt))
+        return fl.add_rms_norm(h, mlp, s.eps)
+
+    def energy(self, v: Tensor, x: Tensor, graded: bool = False) -> Tensor:
+        """E(v; x) per row, ``[B]`` float32. ``graded``: the call's dE/dv will be differentiated again."""
+        dt = v.dtype
+        h = v + x
+        for blk in self.blocks:
+            h = self._block(blk, h, graded)
+        cell = F.linear(F.silu(F.linear(h, self.cell_w1.to(dt), self.cell_b1.to(dt))), self.cell_w2.to(dt))
+        if self.shape.cell_softplus:
+            cell = F.softplus(cell.float())
+        return cell.float().squeeze(-1).sum(dim=1)
+
+    def energy_and_grad(self, v: Tensor, x: Tensor, create_graph: bool = False) -> tuple[Tensor, Tensor]:
+        """(E per row, dE/dv); with ``create_graph`` the gradient is itself differentiable (double backward)."""
+        with torch.enable_grad():
             if not v.requires_grad:
                 v = v.detach().requires_grad_(True)
-            e = self.energy(v, x, self.rope)
+            e = self.energy(v, x, graded=create_graph)
             (g,) = torch.autograd.grad(e.sum(), v, create_graph=create_graph)
-        return e, g, v
+        return e, g
 
-    def microstep(self, z: torch.Tensor, x: torch.Tensor, *, graded: bool, noise: torch.Tensor | None = None,
-                  sigma: float | None = None, alpha: float | torch.Tensor | None = None):  # fmt: skip
-        """One descent microstep from ``z``; returns (z_next, E(v) per row)."""
-        cfg = self.cfg
-        sigma = cfg.noise_scale if sigma is None else sigma
-        step = cfg.step_size if alpha is None else alpha
-        if self.fused and not graded and not torch.is_tensor(step):
-            # Inference microstep: v = rms_norm(z) + noise and z' = sphere(v - alpha g) as fused kernels.
+    # -- descent ----------------------------------------------------------------------------------------------------
+
+    def microstep(self, z: Tensor, x: Tensor, *, graded: bool = False, noise: Optional[Tensor] = None,
+                  sigma: Optional[float] = None, alpha=None) -> tuple[Tensor, Tensor]:  # fmt: skip
+        """One descent step ``z' = sphere(rms_norm(z) + noise - alpha dE/dv)``; returns (z', E per row).
+
+        ``noise``: replayed noise, added as is; otherwise ``sigma`` (default noise_scale) times a fresh normal draw.
+        ``alpha``: a float or a per-row ``[B, 1, 1]`` tensor (default step_size). ``graded``: build the graph through
+        dE/dv (training); otherwise the step runs as fused kernels and returns detached tensors."""
+        s = self.shape
+        sigma = s.noise_scale if sigma is None else sigma
+        alpha = s.step_size if alpha is None else alpha
+        if not graded and not torch.is_tensor(alpha):
             if noise is not None:
-                v = fl.noisy_point(z, noise, 1.0, RMS_NORM_EPS)
-            elif sigma:
-                v = fl.noisy_point(z, torch.randn_like(z), float(sigma), RMS_NORM_EPS)
+                v = fl.noisy_point(z, noise, 1.0, s.eps)
             else:
-                v = fl.noisy_point(z, None, 0.0, RMS_NORM_EPS)
-            e, g, v = self.energy_and_grad(v, x, create_graph=False)
-            return fl.step_and_project(v.detach(), g, float(step), RMS_NORM_EPS), e.detach()
-        v = rms_norm(z)
+                v = fl.noisy_point(z, torch.randn_like(z) if sigma else None, float(sigma), s.eps)
+            e, g = self.energy_and_grad(v, x)
+            return fl.step_and_project(v, g, float(alpha), s.eps), e.detach()
+        v = cell_unit_rms(z, s.eps)
         if noise is not None:
             v = v + noise.to(v.dtype)
         elif sigma:
             v = v + torch.randn_like(v) * sigma
-        e, g, v = self.energy_and_grad(v, x, create_graph=graded)
-        z_next = sphere(v - step * g)
+        e, g = self.energy_and_grad(v, x, create_graph=graded)
+        step = alpha.to(v.dtype) if torch.is_tensor(alpha) else alpha
+        z_next = board_unit_rms(v - step * g, s.eps)
         return (z_next, e) if graded else (z_next.detach(), e.detach())
 
-    def decode(self, z: torch.Tensor) -> torch.Tensor:
-        return self.lm_head(z)
+    def decode(self, z: Tensor) -> Tensor:
+        """Per-cell token logits ``[B, L, vocab]``."""
+        return F.linear(z, self.readout.to(z.dtype))
 
 
-@torch.no_grad()
-def lowest_energy_pick(energy: torch.Tensor, samples: int) -> torch.Tensor:
-    """energy [inputs * samples] (an input's samples contiguous) -> index of each input's lowest-energy sample."""
-    return energy.view(-1, samples).argmin(dim=1)
+def cell_unit_rms(z: Tensor, eps: float = 1e-5) -> Tensor:
+    """Each cell's vector scaled to unit RMS over the hidden dim, in float32 (rms_norm, ``models/layers.py:37-42``);
+    differentiable."""
+    zf = z.float()
+    return (zf * torch.rsqrt(zf.square().mean(-1, keepdim=True) + eps)).to(z.dtype)
 
 
-def descend(model: EnergyReasoner, z: torch.Tensor, x: torch.Tensor, steps: int, *, sigma: float | None = None,
-            noises: list[torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:  # fmt: skip
-    """``steps`` no-graph microsteps (inference: forward + first-order dE/dz each). Returns (z, last energies)."""
+def board_unit_rms(z: Tensor, eps: float = 1e-5) -> Tensor:
+    """Each row (whole board) scaled to unit RMS, in float32 (sphere, ``models/energy.py:219-222``); differentiable."""
+    zf = z.float()
+    rms = zf.square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(eps)
+    return (zf / rms).to(z.dtype)
+
+
+def descend(net: LatentEnergyNet, z: Tensor, x: Tensor, steps: int, *, sigma: Optional[float] = None,
+            noises: Optional[list[Tensor]] = None) -> tuple[Tensor, Tensor]:  # fmt: skip
+    """``steps`` inference microsteps (forward + first-order dE/dz each). Returns (z, energies of the last)."""
     e = None
     for t in range(steps):
-        z, e = model.microstep(z, x, graded=False, sigma=sigma, noise=None if noises is None else noises[t])
+        z, e = net.microstep(z, x, sigma=sigma, noise=None if noises is None else noises[t])
     return z, e
 
 
-def train_step_loss(model: EnergyReasoner, z: torch.Tensor, x: torch.Tensor, labels: torch.Tensor,
-                    prefix: int, graded: int, alpha: torch.Tensor | None = None) -> torch.Tensor:  # fmt: skip
-    """A training segment: ``prefix`` no-graph microsteps, then ``graded`` microsteps with ``create_graph=True``
-    (double backward through the attention), and cross-entropy of the decoded endpoint against ``labels``."""
+@torch.no_grad()
+def lowest_energy_pick(energy: Tensor, samples: int) -> Tensor:
+    """``energy`` [inputs * samples] (each input's samples contiguous) -> index of each input's lowest-energy sample
+    (the evaluation protocol's pick, ``evaluators/protocol.py:10-12``)."""
+    return energy.view(-1, samples).argmin(dim=1)
+
+
+def stablemax_cross_entropy(logits: Tensor, labels: Tensor) -> Tensor:
+    """Per-cell cross entropy under stablemax (exp(x) replaced by x + 1 for x >= 0 and 1 / (1 - x) below), in
+    float64 (the reference's training loss, ``models/losses.py:29-44``). ``logits`` [..., V], ``labels`` [...]."""
+    x = logits.double()
+    s = torch.where(x < 0, 1.0 / (1.0 - x + 1e-30), x + 1.0)
+    logp = torch.log(s / s.sum(-1, keepdim=True))
+    return -logp.gather(-1, labels.long().unsqueeze(-1)).squeeze(-1)
+
+
+def train_segment_loss(net: LatentEnergyNet, z: Tensor, x: Tensor, labels: Tensor, prefix: int, graded: int,
+                       alpha=None) -> Tensor:  # fmt: skip
+    """A training segment: ``prefix`` microsteps without a graph, then ``graded`` with ``create_graph=True`` (so the
+    backward runs the attention's double backward), and the mean stablemax cross entropy of the decoded endpoint
+    against ``labels`` (``models/energy.py:582-636`` rollout, ``models/losses.py`` loss)."""
     for _ in range(prefix):
-        z, _ = model.microstep(z, x, graded=False, alpha=alpha)
+        z, _ = net.microstep(z, x, alpha=alpha)
     for _ in range(graded):
-        z, _ = model.microstep(z, x, graded=True, alpha=alpha)
-    logits = model.decode(rms_norm(z)).float()
-    return F.cross_entropy(logits.flatten(0, 1), labels.flatten().long())
+        z, _ = net.microstep(z, x, graded=True, alpha=alpha)
+    return stablemax_cross_entropy(net.decode(z), labels).mean()
+
+
+__all__ = [
+    "LatentEnergyNet",
+    "NetShape",
+    "board_unit_rms",
+    "cell_unit_rms",
+    "descend",
+    "lowest_energy_pick",
+    "rope_tables",
+    "stablemax_cross_entropy",
+    "train_segment_loss",
+]

@@ -50,7 +50,7 @@ typedef enum ebr_dtype {
 typedef enum ebr_status {
   EBR_OK = 0,
   EBR_ERR_NULL = 1,          /* a required pointer is NULL */
-  EBR_ERR_SHAPE = 2,         /* negative sizes, or D outside [1, 256] */
+  EBR_ERR_SHAPE = 2,         /* negative sizes, D outside [1, 256], B * H >= 2^31 or B * H * N >= 2^40 */
   EBR_ERR_DTYPE = 3,         /* unknown dtype */
   EBR_ERR_STRIDE = 4,        /* head-dim stride is not 1, or a stride is negative */
   EBR_ERR_SCRATCH = 5,       /* scratch missing or smaller than ebr_attn_*_scratch_bytes() */
@@ -102,8 +102,10 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
  * process exits. It calls no allocator of any kind.
  *   - Limit: the row scratch needs B*H*N*4 bytes (B*H*N*8 for float64), so B*H*N <= 2,097,152 rows (1,048,576 for
  *     float64). Larger calls return EBR_ERR_SCRATCH before any launch.
- *   - The first call on a device looks up that device's address of the buffer (cudaGetSymbolAddress); make that first
- *     call before any stream capture.
+ *   - The first call in a CUDA context (the primary context of a device, or a context the caller created with the
+ *     driver API) looks up the buffer's address in that context (cudaGetSymbolAddress) and remembers it for that
+ *     context; make that first call before any stream capture. A context destroyed and re-created under the same
+ *     handle (cudaDeviceReset) is not detected: after a device reset, reload the library.
  *   - All calls share the one buffer per device and it keeps the last call's contents (every value a call reads is
  *     written earlier in the same call). Calls whose executions overlap on the GPU (for example on two streams) race
  *     on it: serialize them.
@@ -122,6 +124,12 @@ int ebr_attn_uses_tensor_cores(int dtype, int64_t D, const ebr_operand* q, const
 /* Synchronizes the current device, returns EBR_OK or EBR_ERR_DEVICE_TIMEOUT if a bounded device wait ran out since
  * the last call, and clears the device error word. */
 int ebr_attn_device_status(void);
+
+/* Test support for the error path above, with no counterpart in the reference: launches one thread on `stream` that
+ * waits, with a limit of `limit_ns` (1 us to 1 s), on a device barrier that nothing completes. The wait runs out and
+ * sets the device error word, so the next ebr_attn_device_status() returns EBR_ERR_DEVICE_TIMEOUT (and clears it);
+ * the context stays usable. */
+int ebr_attn_test_bounded_wait(int64_t limit_ns, void* stream);
 
 /* Human-readable text of a status code, and of the last CUDA error seen by this thread. */
 const char* ebr_attn_status_string(int status);

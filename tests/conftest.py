@@ -14,6 +14,7 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 GOLDEN = ROOT / "tests" / "golden" / "attn_golden.npz"
+LAYERS_GOLDEN = ROOT / "tests" / "golden" / "layers_golden.npz"
 
 
 def pytest_configure(config):
@@ -23,6 +24,12 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def golden():
     return np.load(GOLDEN, allow_pickle=False)
+
+
+@pytest.fixture(scope="session")
+def layers_golden():
+    """The reference's RoPE split / merge and energy-network outputs (tests/golden/make_golden.py)."""
+    return np.load(LAYERS_GOLDEN, allow_pickle=False)
 
 
 def golden_case(golden, name: str) -> dict[str, np.ndarray]:

@@ -146,3 +146,33 @@ def test_kernel_family_choice(lib):
 def test_status_strings(lib):
     assert lib.ebr_attn_status_string(0) == b"ok"
     assert lib.ebr_attn_status_string(_native.ERR_DEVICE_TIMEOUT) == b"device wait timed out"
+
+
+def test_size_products_are_bounded_before_any_arithmetic(lib):
+    """B * H >= 2^31 or B * H * N >= 2^40 is refused on the host (each factor alone is within [0, 2^30])."""
+    q = _op()
+    r = ctypes.byref
+    big = 1 << 30
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, big, 4, 8, 64, 0.1, r(q), r(q), r(q), 0x2000, 0x3000, None) == _native.ERR_SHAPE
+    assert lib.ebr_attn_fwd(_native.BFLOAT16, 1 << 20, 1 << 10, 1 << 10, 64, 0.1, r(q), r(q), r(q), 0x2000, 0x3000,
+                            None) == _native.ERR_SHAPE  # fmt: skip
+    # the allocation-free backward refuses them too, before sizing its scratch (no wrap below the buffer size)
+    assert lib.ebr_attn_bwd_noalloc(_native.BFLOAT16, 1 << 20, 1 << 10, 1 << 10, 64, 0.1, r(q), r(q), r(q), 0x2,
+                                    0x3, r(q), 0x4, 0x5, 0x6, None) == _native.ERR_SHAPE  # fmt: skip
+    assert lib.ebr_attn_test_bounded_wait(10, None) == _native.ERR_SHAPE  # limit outside [1 us, 1 s]
+
+
+@pytest.mark.gpu
+def test_bounded_wait_reports_a_timeout_and_the_context_survives(lib):
+    """The device error path: a wait that nothing completes runs out after its limit (50 ms), the host reads
+    EBR_ERR_DEVICE_TIMEOUT once (the word is then cleared), and the context keeps working."""
+    import torch
+
+    torch.cuda.synchronize()
+    assert lib.ebr_attn_device_status() == _native.OK
+    assert lib.ebr_attn_test_bounded_wait(50_000_000, None) == _native.OK
+    assert lib.ebr_attn_device_status() == _native.ERR_DEVICE_TIMEOUT
+    assert b"9001" in lib.ebr_attn_last_error()
+    assert lib.ebr_attn_device_status() == _native.OK
+    x = torch.arange(1024, device="cuda", dtype=torch.float32)
+    assert float(x.sum()) == 1023 * 1024 / 2

@@ -95,3 +95,28 @@ def test_oracle_empty_and_single():
 def test_max_rel_metric():
     assert oracle.max_rel(np.array([1.0, 2.0]), np.array([1.0, 2.0])) == 0.0
     assert abs(oracle.max_rel(np.array([1.1, 2.0]), np.array([1.0, 2.0])) - 0.05) < 1e-12
+
+
+def test_rope_restatement_matches_reference_fixtures(layers_golden):
+    """oracle/rope.py (the GPU RoPE tests' yardstick) reproduces the reference's ref_split / ref_merge bit for bit."""
+    import torch
+
+    from oracle.rope import merge, split
+
+    g_ = layers_golden
+
+    def load(key):
+        a = g_[key]
+        if a.dtype == np.uint16:
+            return torch.from_numpy(a.astype(np.int32)).to(torch.int16).view(torch.bfloat16)
+        return torch.from_numpy(a)
+
+    names = sorted({k.split("/")[1] for k in g_.files if k.startswith("rope/")})
+    assert len(names) == 4
+    for name in names:
+        heads = int(g_[f"rope/{name}/meta"][1])
+        t = {k: load(f"rope/{name}/{k}") for k in ("qkv", "cos", "sin", "q", "k", "v", "dq", "dk", "dv", "g")}
+        qs = load(f"rope/{name}/qscale") if f"rope/{name}/qscale" in g_.files else None
+        for a, r in zip(split(t["qkv"], t["cos"], t["sin"], heads, qs), (t["q"], t["k"], t["v"])):
+            assert torch.equal(a, r), name
+        assert torch.equal(merge(t["dq"], t["dk"], t["dv"], t["cos"], t["sin"], qs), t["g"]), name

@@ -1,9 +1,18 @@
 """GPU parity of the sm_100a attention kernels against the CPU oracle (numpy restatement of reference.py).
 
-Tolerances: with 16-bit I/O the forward output is within 2e-3 max-rel of an fp32 reference on
-top of its own final rounding to the 16-bit type (half an ulp, 2^-8 relative for bf16, 2^-11 for fp16); first- and
-second-order gradients are within 1e-2 max-rel. float32 calls (IEEE CUDA-core kernels) are within 1e-4, float64
-within 1e-10. max-rel is the reference's metric, max|a - r| / max|r| (models/attention.py:156-161).
+Tolerances (forward within 2e-3 max-rel of an fp32 reference, first- and second-order gradients
+within 1e-2). max-rel is the reference's metric, max|a - r| / max|r| (models/attention.py:156-161), against the oracle
+run in fp32 on the same rounded inputs.
+
+* fp16 I/O: the forward is asserted at 2e-3 max-rel with no allowance at all. fp16's own rounding of O is at most
+  2^-11 of the largest element, so this bar shows the kernels' arithmetic error directly; the bf16 and fp16 calls run
+  the same kernel templates (the element type only changes the conversions at load and store).
+* bf16 I/O: rounding O to bf16 alone moves an element by up to 2^-9 of its value, i.e. up to 3.9e-3 of max|O| when
+  the largest element sits at the bottom of its binade, so a plain 2e-3 bar against the unrounded reference is not
+  reachable by ANY bf16-output kernel (the reference's Triton kernels included). The bf16 forward is therefore
+  asserted at 2e-3 beyond each element's own half-ulp, and the plain max-rel is reported in the message.
+* Gradients: 1e-2 beyond the half-ulp of the output type. float32 calls (IEEE CUDA-core kernels) within 1e-4, float64
+  within 1e-10.
 """
 
 from __future__ import annotations
@@ -53,7 +62,9 @@ def check_out(got: torch.Tensor, ref: np.ndarray, dtype, tol16: float, what: str
     assert np.isfinite(g).all(), f"{what}: non-finite output"
     denom = max(np.abs(r).max(), floor) if r.size else 1.0
     plain = float(np.abs(g - r).max() / denom) if r.size else 0.0
-    if dtype in HALF_ULP:
+    if dtype == torch.float16 and tol16 == FWD_TOL and ulps == 0.5:
+        assert plain <= FWD_TOL, f"{what}: fp16 plain max-rel {plain:.3e} > {FWD_TOL}"
+    elif dtype in HALF_ULP:
         allow = 2 * ulps * HALF_ULP[dtype]
         err = float(np.maximum(np.abs(g - r) - allow * np.abs(r), 0).max() / denom) if r.size else 0.0
         assert err <= tol16, f"{what}: {err:.3e} (plain max-rel {plain:.3e}) > {tol16}"
@@ -108,6 +119,11 @@ SHAPES_16 = [
     (2, 1, 320, 64),
     (1, 2, 384, 128),
     (2, 8, 1000, 64),
+    # the kernel sweep's long and D = 128 shapes: L = 2048 at both head dims, D = 128 at L = 256 and 900
+    (1, 1, 2048, 64),
+    (1, 1, 2048, 128),
+    (1, 1, 900, 128),
+    (1, 2, 256, 128),
 ]
 
 
@@ -219,6 +235,35 @@ def test_golden_cases_on_device(golden):
             check_out(got, c[n_], dtype, GRAD_TOL, f"{name}/{n_}", ulps=1.0)
         for n_, got in zip(("hq", "hk", "hv", "hdo"), hs):
             check_out(got, c[n_], dtype, GRAD_TOL, f"{name}/{n_}", ulps=1.0)
+
+
+def test_cfg1_golden_on_device(golden):
+    """BASELINE config 1 through the op chain on the device (fp32, B=4, L=81, H=8, D=64, seed 0: O, then dQ/dK/dV
+    with create_graph=True, then the gradient of sum(dQ * R)), against the reference's own outputs stored in the
+    golden file: 4096 sampled entries of every output and its per-(b, h) sums. The inputs are redrawn from the seed
+    and checked against the stored checksums first."""
+    from tests.golden.make_golden import cfg1_inputs
+
+    x = cfg1_inputs()
+    for name, t in x.items():
+        assert np.allclose(golden[f"cfg1/in_sum/{name}"], [t.double().sum().item(), t.double().abs().sum().item()],
+                           rtol=1e-12, atol=1e-9), name  # fmt: skip
+    q, k, v = (x[n].to(DEV).requires_grad_(True) for n in ("q", "k", "v"))
+    o = fused_attn.fused_attention(q, k, v)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), grad_outputs=x["do"].to(DEV), create_graph=True)
+    hq, hk, hv = torch.autograd.grad((dq * x["r"].to(DEV)).sum(), (q, k, v))
+    torch.cuda.synchronize()
+    _native.device_status()
+    idx = golden["cfg1/index"]
+    for name, t in {"o": o, "dq": dq, "dk": dk, "dv": dv, "hq": hq, "hk": hk, "hv": hv}.items():
+        got = t.detach().double().cpu()
+        ref = golden[f"cfg1/{name}/sample"].astype(np.float64)
+        err = float(np.abs(got.reshape(-1).numpy()[idx] - ref).max() / np.abs(ref).max())
+        assert err <= TOL32, f"cfg1 {name}: sampled max-rel {err:.3e}"
+        sums = got.sum(dim=(2, 3)).numpy()
+        ref_sums = golden[f"cfg1/{name}/bh_sum"]
+        scale = max(np.abs(ref_sums).max(), float(got.abs().sum(dim=(2, 3)).max()) * 1e-3)
+        assert np.abs(sums - ref_sums).max() <= 1e-4 * scale, f"cfg1 {name}: per-(b, h) sums"
 
 
 @pytest.mark.parametrize("shape", [(2, 2, 81, 64), (1, 2, 300, 64), (1, 2, 200, 128)], ids=str)
