@@ -225,7 +225,7 @@ class LatentEnergyNet(nn.Module):
                 v = v.detach().requires_grad_(True)
             e = self.energy(v, x, graded=create_graph)
             (g,) = torch.autograd.grad(e.sum(), v, create_graph=create_graph)
-        return e, g
+        return (e if create_graph else e.detach()), g
 
     # -- descent ----------------------------------------------------------------------------------------------------
 

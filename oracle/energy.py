@@ -139,3 +139,35 @@ def microstep(state, spec, z, x, noise=None, alpha: float = 250.0, attention=mat
         v = v + noise.to(v.dtype)
     e, g = energy_and_grad(state, spec, v, x, attention)
     return sphere(v - alpha * g).detach(), e.detach()
+
+
+class _ReferenceRounding(torch.autograd.Function):
+    """Softmax attention with the rounding choices of the reference's GPU kernels
+    (``models/fused_attn/triton_kernels.py:576-586``): P rounded to the input type before the P V product, P and dS
+    rounded before the backward's products, float32 elsewhere. First order only (enough for dE/dz)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v):
+        sc = q.shape[-1] ** -0.5
+        s = q.float() @ k.float().transpose(-1, -2) * sc
+        m = s.amax(-1, keepdim=True)
+        p = torch.exp(s - m)
+        den = p.sum(-1, keepdim=True)
+        o = ((p.to(q.dtype).float() @ v.float()) / den).to(q.dtype)
+        ctx.save_for_backward(q, k, v, o, m + torch.log(den))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        sc = q.shape[-1] ** -0.5
+        qf, kf, vf, dof = q.float(), k.float(), v.float(), do.to(q.dtype).float()
+        p = torch.exp(qf @ kf.transpose(-1, -2) * sc - lse)
+        dv = p.to(q.dtype).float().transpose(-1, -2) @ dof
+        dp = dof @ vf.transpose(-1, -2)
+        ds = (p * (dp - (dof * o.float()).sum(-1, keepdim=True))).to(q.dtype).float()
+        return (ds @ kf * sc).to(q.dtype), (ds.transpose(-1, -2) @ qf * sc).to(q.dtype), dv.to(q.dtype)
+
+
+def reference_rounding_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    return _ReferenceRounding.apply(q, k, v)

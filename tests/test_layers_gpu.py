@@ -34,6 +34,12 @@ def _tables(h=9, w=9, d=64):
     return cos.to(DEV), sin.to(DEV)
 
 
+def quarter_swap(x):
+    from oracle.rope import quarter_swap as qs
+
+    return qs(x)
+
+
 def ref_split(qkv, cos, sin, heads, qscale=None):
     from oracle.rope import split
 
@@ -404,7 +410,7 @@ def _ulp_diff(a, r):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_add_rms_norm_forward_and_backward(dtype):
-    from ebr_b200.energy import rms_norm
+    from oracle.energy import rms_norm
     from ebr_b200.layers import add_rms_norm
 
     g = torch.Generator(device="cpu").manual_seed(7)
@@ -424,7 +430,7 @@ def test_add_rms_norm_forward_and_backward(dtype):
 
 def test_add_rms_norm_second_order_matches_eager():
     """Under create_graph the backward is built from torch ops: d/dx <dy/dx gy, u> equals the eager ops' own."""
-    from ebr_b200.energy import rms_norm
+    from oracle.energy import rms_norm
     from ebr_b200.layers import add_rms_norm
 
     g = torch.Generator(device="cpu").manual_seed(8)
