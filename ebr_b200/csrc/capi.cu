@@ -14,6 +14,7 @@
 #include "tc_bob.cuh"
 #include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
+#include "tc_short.cuh"
 
 namespace {
 
@@ -175,6 +176,69 @@ int make_tile_map(CUtensorMap* map, const ebr_operand* op, int dtype, int64_t B,
   return EBR_OK;
 }
 
+// 16-bit 4-D tensor map with an explicit box: dims (D, N, hs, bs) with element strides (sn, sh, sb), box
+// (64, box_n, box_h, 1), 128-byte swizzle, zero fill outside the tensor (the short-sequence kernels' tiles).
+int make_box_map(CUtensorMap* map, const void* data, int dtype, int64_t D, int64_t N, int64_t hs, int64_t bs,
+                 int64_t sn, int64_t sh, int64_t sb, uint32_t box_n, uint32_t box_h) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
+  auto fix = [](int64_t stride, int64_t extent) -> cuuint64_t {
+    return static_cast<cuuint64_t>(extent <= 1 ? 16 : stride * 2);
+  };
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(hs),
+                              static_cast<cuuint64_t>(bs)};
+  const cuuint64_t strides[3] = {fix(sn, N), fix(sh, hs), fix(sb, bs)};
+  const cuuint32_t box[4] = {64, box_n, box_h, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled failed%s%s");
+  return EBR_OK;
+}
+
+// Tile geometry of a short-sequence (N <= 128) launch. Slices are packed floor(128 / N) per tile along one axis of
+// B * H when every operand reaches slice (b, h) at b * stride_b + h * stride_h with stride_b = H * stride_h (any
+// contiguous or head-major tensor); otherwise the tile holds a divisor of H slices of one batch row.
+struct ShortPlan {
+  ShortGeom geo;
+  int64_t hs, bs;  // tensor-map extents of the slice axes
+  bool flat;       // B * H slices read as one axis
+};
+
+ShortPlan short_plan(int64_t B, int64_t H, int64_t N, std::initializer_list<const ebr_operand*> ops) {
+  bool flat = true;
+  for (const ebr_operand* op : ops)
+    if (op && op->data && B > 1 && op->stride_b != H * op->stride_h) flat = false;
+  ShortPlan p{};
+  p.flat = flat;
+  p.hs = flat ? B * H : H;
+  p.bs = flat ? 1 : B;
+  int64_t per = kTile / N;
+  if (per > p.hs) per = p.hs;
+  if (!flat)
+    while (per > 1 && H % per) --per;
+  if (per < 1) per = 1;
+  p.geo.N = static_cast<int>(N);
+  p.geo.per = static_cast<int>(per);
+  p.geo.hs = static_cast<int>(p.hs);
+  p.geo.tiles_per_b = static_cast<int>((p.hs + per - 1) / per);
+  p.geo.tiles = static_cast<int>(p.geo.tiles_per_b * p.bs);
+  return p;
+}
+
+// An input operand's short-sequence map under `plan`.
+int make_short_map(CUtensorMap* map, const ebr_operand* op, int dtype, const ShortPlan& plan, int64_t D) {
+  return make_box_map(map, op->data, dtype, D, plan.geo.N, plan.hs, plan.bs, op->stride_n, op->stride_h,
+                      op->stride_b, static_cast<uint32_t>(plan.geo.N), static_cast<uint32_t>(plan.geo.per));
+}
+// A contiguous [B, H, N, D] output's map under `plan`.
+int make_short_out_map(CUtensorMap* map, void* data, int dtype, const ShortPlan& plan, int64_t H, int64_t D) {
+  const int64_t N = plan.geo.N;
+  return make_box_map(map, data, dtype, D, N, plan.hs, plan.bs, D, N * D, H * N * D, static_cast<uint32_t>(N),
+                      static_cast<uint32_t>(plan.geo.per));
+}
+
 bool tc_eligible(int dtype, int64_t D, std::initializer_list<const ebr_operand*> ops, int64_t B, int64_t H, int64_t N) {
   if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16) return false;
   if (D != 64 && D != 128) return false;
@@ -214,24 +278,22 @@ int sm_count(int device) {
 }
 
 template <typename T, int D>
-int launch_tc_fwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
-                       const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
-  using L = FwdPipeLayout<D>;
-  CUtensorMap tq, tk, tv;
-  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
-      make_tile_map(&tv, v, dtype, B, H, N, D))
+int launch_tc_fwd_short(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                        const ebr_operand* k, const ebr_operand* v, void* o, void* lse, cudaStream_t st) {
+  using L = FwdShortLayout<D>;
+  const ShortPlan plan = short_plan(B, H, N, {q, k, v});
+  CUtensorMap tq, tk, tv, to;
+  if (make_short_map(&tq, q, dtype, plan, D) || make_short_map(&tk, k, dtype, plan, D) ||
+      make_short_map(&tv, v, dtype, plan, D) || make_short_out_map(&to, o, dtype, plan, H, D))
     return kNoTensorMap;
-  const void* fn = reinterpret_cast<const void*>(tc_fwd_pipe_kernel<T, D>);
+  const void* fn = reinterpret_cast<const void*>(tc_fwd_short_kernel<T, D>);
   int s = prepare_tc_kernel(fn, device, L::kSmem, L::kTmemCols, L::kThreads);
   if (s) return s;
-  const int64_t items = B * H * ((N + kTile - 1) / kTile);
-  const int64_t cap = static_cast<int64_t>(L::kCtasPerSm) * sm_count(device);
-  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
-  tc_fwd_pipe_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, static_cast<T*>(o),
-                                                                 static_cast<float*>(lse), static_cast<int>(B * H),
-                                                                 static_cast<int>(H), static_cast<int>(N),
-                                                                 static_cast<float>(scale));
-  return check_launch("tc_fwd_pipe_kernel");
+  const int cap = L::kCtasPerSm * sm_count(device);
+  const unsigned grid = static_cast<unsigned>(plan.geo.tiles < cap ? plan.geo.tiles : cap);
+  tc_fwd_short_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, to, static_cast<float*>(lse), plan.geo,
+                                                                  static_cast<float>(scale));
+  return check_launch("tc_fwd_short_kernel");
 }
 
 template <typename T, int D>
@@ -578,15 +640,15 @@ int ebr_attn_fwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double s
         s = D == 64 ? launch_tc_fwd_pair<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
                     : launch_tc_fwd_pair<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
       else
-        s = D == 64 ? launch_tc_fwd_pipe<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                    : launch_tc_fwd_pipe<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+        s = D == 64 ? launch_tc_fwd_short<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_short<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
     } else {
       if (pair)
         s = D == 64 ? launch_tc_fwd_pair<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
                     : launch_tc_fwd_pair<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
       else
-        s = D == 64 ? launch_tc_fwd_pipe<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
-                    : launch_tc_fwd_pipe<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
+        s = D == 64 ? launch_tc_fwd_short<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, st)
+                    : launch_tc_fwd_short<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, st);
     }
     if (s != kNoTensorMap) return s;
   }

@@ -145,283 +145,6 @@ __device__ __forceinline__ void mma_tileT_x_rows(uint32_t d_tmem, const unsigned
     mma_ss(d_tmem, desc_mnmajor(a, kk), desc_mnmajor(b, kk), idesc, (kk > 0 || accumulate_first) ? 1u : 0u);
 }
 
-// ================================================================================================ forward (pipelined)
-
-template <int D>
-struct FwdPipeLayout {
-  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;  // one [128 x D] 16-bit tile
-  static constexpr int kStages = 2;                       // K / V ring depth
-  static constexpr uint32_t kQ0 = 0;                      // Q double buffer: kQ0, kQ0 + kOp
-  static constexpr uint32_t kKV = 2 * kOp;                // stage s: K at kKV + 2 s kOp, V at + kOp
-  static constexpr uint32_t kBytes = kKV + kStages * 2 * kOp;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 256;              // S / P: [0, 128), O: [128, 128 + D)
-  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kThreads = 320;
-};
-
-// Forward for any N, persistent and warp-specialized (2 CTAs per SM at D = 64, so one CTA's MMAs run under the
-// other's softmax):
-//   warps 0-7  softmax, two warpgroups: warp w owns query rows 32 (w % 4) .. + 31 of the current tile (TMEM lanes)
-//              and key columns 64 (w / 4) .. + 63 of each 128-key tile, so each row is shared by two threads, which
-//              exchange their partial row max per tile and their partial row sum per item through shared memory;
-//   warp 8     TMA producer: Q tile per item (double-buffered), K / V tiles into a 2-stage ring;
-//   warp 9     MMA issuer: S = Q K^T into TMEM, then O += P V with P read from TMEM (tcgen05.mma A-from-TMEM).
-// An item is one 128-row query tile of one (b, h) slice; a CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...
-// with the query tile fastest, so the CTAs working on one slice at the same time share its K / V through L2.
-// Per key tile the softmax warps write P as a 16-bit hi / lo pair over the S columns they have read (for keys
-// [16 k, 16 k + 16): P_hi in columns [16 k, 16 k + 8), P_lo in [16 k + 8, 16 k + 16)) and the MMA warp accumulates
-// O += P_hi V + P_lo V in TMEM. The running max is updated lazily: O and l are rescaled only when a tile's max exceeds
-// the max in use by more than 8 (in log2 units), so P stays below 256 and the common case touches O not at all.
-// O / l and lse = m + log l at the end of the item. Same math as the reference's _fwd_kernel
-// (triton_kernels.py:98-163).
-template <typename T, int D>
-__global__ void __launch_bounds__(320, (D == 64) ? 2 : 1)
-    tc_fwd_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, T* __restrict__ out, float* __restrict__ lse, int BH,
-                       int H, int N, float scale) {
-  using L = FwdPipeLayout<D>;
-  constexpr int NS = L::kStages;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  __shared__ uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, p_full, o_done, xch[2];
-  __shared__ float xval[2][2][128];  // [exchange parity][warpgroup][row]: partial row max (per tile) or sum (per item)
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_kt = (N + kTile - 1) / kTile;
-  const int64_t items = static_cast<int64_t>(BH) * n_kt;  // query tiles: ceil(N / 128) per slice
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdS = idesc_f16(kB, 0, 0, 128, 128);
-  constexpr uint32_t kIdPV = idesc_f16(kB, 0, 1, 128, D);
-  constexpr float kTau = 5.545177444479562f;  // 8 ln 2: lazy-rescale threshold in natural units
-  auto sQ = [&](int b) { return smem + L::kQ0 + b * L::kOp; };
-  auto sK = [&](int s) { return smem + L::kKV + s * 2 * L::kOp; };
-  auto sV = [&](int s) { return smem + L::kKV + s * 2 * L::kOp + L::kOp; };
-
-  if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&xch[i], 256);
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 256);
-    mbar_init(&o_done, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort = &abort_flag;
-
-  if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      uint32_t kv_use = 0;
-      int64_t li = 0;
-      for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++li) {
-        const int bh = static_cast<int>(it / n_kt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-        const int b = bh / H, h = bh - (bh / H) * H;
-        const int qb = static_cast<int>(li & 1);
-        if (!mbar_wait_or_abort(&q_empty[qb], ((li >> 1) & 1) ^ 1, 111, abort)) break;
-        mbar_arrive_expect_tx(&q_full[qb], L::kOp);
-        for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_4d(sQ(qb) + hh * kHalfBytes, &tq, &q_full[qb], hh * 64, qt * kTile, h, b);
-        bool ok = true;
-        for (int j = 0; j < n_kt && ok; ++j, ++kv_use) {
-          const int s = static_cast<int>(kv_use % NS);
-          const uint32_t u = kv_use / NS;
-          ok = mbar_wait_or_abort(&kv_empty[s], (u & 1) ^ 1, 112, abort);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::kOp);
-          for (int hh = 0; hh < D / 64; ++hh) {
-            tma_load_4d(sK(s) + hh * kHalfBytes, &tk, &kv_full[s], hh * 64, j * kTile, h, b);
-            tma_load_4d(sV(s) + hh * kHalfBytes, &tv, &kv_full[s], hh * 64, j * kTile, h, b);
-          }
-        }
-        if (!ok) break;
-      }
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t tS = tmem, tO = tmem + 128;
-      uint32_t kv_use = 0, t = 0;
-      int64_t li = 0;
-      bool ok = true;
-      for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
-        const int qb = static_cast<int>(li & 1);
-        ok = mbar_wait_or_abort(&q_full[qb], (li >> 1) & 1, 121, abort);
-        for (int j = 0; j < n_kt && ok; ++j, ++kv_use, ++t) {
-          const int s = static_cast<int>(kv_use % NS);
-          ok = mbar_wait_or_abort(&kv_full[s], (kv_use / NS) & 1, 122, abort);
-          if (ok && t > 0) ok = mbar_wait_or_abort(&o_done, (t - 1) & 1, 123, abort);  // S / P columns free
-          if (!ok) break;
-          tc_fence_after();
-          mma_rows_x_rows<D>(tS, sQ(qb), sK(s), kIdS, false);
-          mma_commit(&s_full);
-          if (j == n_kt - 1) mma_commit(&q_empty[qb]);
-          ok = mbar_wait_or_abort(&p_full, t & 1, 124, abort);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk) {
-            const uint32_t a_hi = tS + kk * 16;
-            const uint64_t bdesc = desc_mnmajor(sV(s), kk);
-            mma_ts(tO, a_hi, bdesc, kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
-            mma_ts(tO, a_hi + 8, bdesc, kIdPV, 1u);
-          }
-          mma_commit(&o_done);
-          mma_commit(&kv_empty[s]);
-        }
-      }
-    }
-  } else {
-    // ---------------------------------------------------------------- softmax / epilogue (warps 0-7)
-    const int half = warp >> 2, lrow = (warp & 3) * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + half * 64, tO = tmem + 128 + lane_off;
-    uint32_t t = 0, x = 0;  // tile counter, exchange counter
-    bool ok = true;
-    // Exchange a per-row partial value with the other warpgroup's thread of the same row; returns the partner's.
-    auto exchange = [&](float v) -> float {
-      const int b = static_cast<int>(x & 1);
-      xval[b][half][lrow] = v;
-      mbar_arrive(&xch[b]);
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&xch[b], (x >> 1) & 1, 133, abort));
-      ++x;
-      return xval[b][half ^ 1][lrow];
-    };
-    for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const int bh = static_cast<int>(it / n_kt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
-      const int row = qt * kTile + lrow;
-      float m_used = -INFINITY, l_run = 0.f;
-      for (int j = 0; j < n_kt; ++j, ++t) {
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&s_full, t & 1, 131, abort));
-        if (!ok) break;
-        tc_fence_after();
-        const int valid = min(kTile, N - j * kTile) - half * 64;  // this thread's keys inside [0, N)
-        // Pass 1: the row max of the raw scores over both halves, scaled once (rounding is monotonic, so this equals
-        // the max of the scaled scores; a negative scale turns it into the min).
-        float mraw = scale >= 0.f ? -INFINITY : INFINITY;
-#pragma unroll
-        for (int c = 0; c < 64; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tS + c, r);
-          tmem_wait_ld();
-          if (valid >= 64) {
-            if (scale >= 0.f) {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) mraw = fmaxf(mraw, __uint_as_float(r[e]));
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) mraw = fminf(mraw, __uint_as_float(r[e]));
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (c + e < valid) mraw = scale >= 0.f ? fmaxf(mraw, __uint_as_float(r[e])) : fminf(mraw, __uint_as_float(r[e]));
-          }
-        }
-        const float other = exchange(mraw);
-        if (!ok) break;
-        mraw = scale >= 0.f ? fmaxf(mraw, other) : fminf(mraw, other);
-        const float mx = mraw * scale;
-        // Lazy rescale. tcgen05.ld / st are warp-collective, so the decision is made per warp (both warpgroups see the
-        // same rows and make the same decision); each warpgroup rewrites its half of the O columns, alpha = 1 for the
-        // rows that keep their max. The previous P V product has completed (S of this tile was issued after it).
-        const bool need = (j == 0) || (mx > m_used + kTau);
-        if (j == 0) {
-          m_used = mx;
-        } else if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? exp_nat(m_used - mx) : 1.f;
-#pragma unroll 1
-          for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
-            uint32_t r[32];
-            tmem_ld32(tO + c, r);
-            tmem_wait_ld();
-            uint32_t a8[8], b8[8], c8[8], d8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              a8[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              b8[e] = __float_as_uint(__uint_as_float(r[8 + e]) * alpha);
-              c8[e] = __float_as_uint(__uint_as_float(r[16 + e]) * alpha);
-              d8[e] = __float_as_uint(__uint_as_float(r[24 + e]) * alpha);
-            }
-            tmem_st8(tO + c, a8);
-            tmem_st8(tO + c + 8, b8);
-            tmem_st8(tO + c + 16, c8);
-            tmem_st8(tO + c + 24, d8);
-          }
-          if (need) {
-            l_run *= alpha;
-            m_used = mx;
-          }
-        }
-        // Pass 2: P = exp(s * scale - m_used) as a 16-bit hi / lo pair over the S columns just read: for keys
-        // [16 k, 16 k + 16), P_hi in columns [16 k, 16 k + 8) and P_lo in [16 k + 8, 16 k + 16).
-        float psum = 0.f;
-#pragma unroll
-        for (int c = 0; c < 64; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tS + c, r);
-          tmem_wait_ld();
-          uint32_t hi[8], lo[8];
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            float p0 = exp_nat(fmaf(__uint_as_float(r[e]), scale, -m_used));
-            float p1 = exp_nat(fmaf(__uint_as_float(r[e + 1]), scale, -m_used));
-            if (valid < 64) {
-              if (c + e >= valid) p0 = 0.f;
-              if (c + e + 1 >= valid) p1 = 0.f;
-            }
-            psum += p0 + p1;
-            const uint32_t ph = pack2<T>(p0, p1);
-            const float h0 = unpack_lo<T>(ph), h1 = unpack_hi<T>(ph);
-            hi[e >> 1] = ph;
-            lo[e >> 1] = pack2<T>(p0 - h0, p1 - h1);
-          }
-          tmem_st8(tS + c, hi);
-          tmem_st8(tS + c + 8, lo);
-        }
-        l_run += psum;
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full);
-      }
-      if (!ok) break;
-      const float l_total = l_run + exchange(l_run);
-      if (!ok) break;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&o_done, (t - 1) & 1, 132, abort));
-      if (!ok) break;
-      tc_fence_after();
-      const bool row_ok = row < N;
-      const int64_t grow = static_cast<int64_t>(bh) * N + row;
-      T* dst = row_ok ? out + grow * D : nullptr;
-      store_cols_from_tmem<T, D / 2>(tO, half * (D / 2), 1.f / l_total, dst);
-      if (row_ok && half == 0) lse[grow] = m_used + logf(l_total);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-}
-
 // ================================================================================================ backward helpers
 
 // Shared helper: thread `row`'s D_i = <dO_i, O_i> from the TMA-staged dO tile and the stored (contiguous) O.

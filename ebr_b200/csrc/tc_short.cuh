@@ -1,0 +1,336 @@
+// tc_short.cuh: short-sequence (N <= 128) tensor-core kernels.
+//
+// At N <= 128 a whole (b, h) slice fits one 128-row tile, so the passes are bound by HBM, not by the tensor pipe
+// (4 N^2 D FLOP against 8 N D bytes in the forward: about N / 2 FLOP per byte, far below the B200's ~250). What
+// decides their speed is how many bytes each SM keeps in flight and how little each tile waits on the previous one.
+// So these kernels are persistent (one CTA per SM), keep a ring of input stages loading ahead, double-buffer every
+// tensor-memory accumulator so the tensor pipe works on tile t + 1 while tile t is in the pointwise code, and write
+// their outputs through shared memory with TMA stores.
+//
+// Packing. ``per`` = floor(128 / N) slices are stacked in one 128-row tile when their rows sit at a uniform stride
+// (B * H slices read as one axis of the tensor map; otherwise ``per`` divides H and the tile stays inside one batch
+// row). Row r of a tile belongs to slice r / N and attends only to the keys of that slice: the score tile is
+// block-diagonal and every other column is masked. Rows and key columns at or beyond per * N are zero in shared
+// memory (the stages are cleared once; the TMA boxes never reach them).
+//
+// Geometry. The 4-D tensor maps are (D, N, Hs, Bs) with boxes (64, N, per, 1): Hs = B * H and Bs = 1 when the
+// slices are packed along one axis, else Hs = H and Bs = B. Tile t covers Hs-indices [h0, h0 + per) of Bs-index b'
+// with h0 = (t mod ceil(Hs / per)) * per; its slice r / N is b' * Hs + h0 + r / N, valid while h0 + r / N < Hs (the
+// boxes read zeros past the end and the stores clip there).
+#pragma once
+
+#include "tc_attn.cuh"
+
+namespace ebr {
+
+struct ShortGeom {
+  int N;            // rows of a slice
+  int per;          // slices per tile
+  int hs;           // extent of the tensor maps' third axis (H, or B * H when packed along one axis)
+  int tiles_per_b;  // ceil(hs / per)
+  int tiles;        // tiles_per_b * Bs
+};
+
+__device__ __forceinline__ void short_tile_coords(const ShortGeom& g, int t, int& hb, int& h0) {
+  hb = t / g.tiles_per_b;
+  h0 = (t - hb * g.tiles_per_b) * g.per;
+}
+
+// ================================================================================================ forward
+
+template <int D>
+struct FwdShortLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;    // one [128 x D] 16-bit tile
+  static constexpr uint32_t kBytes = 3 * kOp;               // Q, K, V (O is staged over the spent V)
+  static constexpr uint32_t kSmem = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = D == 64 ? 128 : 256;  // S, then P (fp16) in [0, 64) and O in [64, 64 + D)
+  static constexpr int kCtasPerSm = D == 64 ? 4 : 2;
+  static constexpr int kThreads = 128;
+};
+
+// Forward for N <= 128. Each CTA is one 4-warp pipeline over its tiles (blockIdx.x, blockIdx.x + gridDim.x, ...),
+// and kCtasPerSm of them share an SM, so several tiles are always in different phases on one SM: the pass is bound by
+// HBM, and a single tile's chain (scores -> softmax -> P V -> store) is long, so overlap between tiles is what keeps
+// the memory system busy. Thread r owns row r of the tile (tensor-memory lane r); thread 0 also issues the TMA
+// loads, the tcgen05 products and the TMA store. Per tile:
+//   S = Q K^T into tensor memory; once it is done the next tile's Q and K are loaded over the spent ones;
+//   row max m of s scale over the row's slice; P = 2^(s scale log2 e - m log2 e) (0 outside the slice) written back as
+//   fp16 pairs into columns [0, kc / 2) (columns already read);
+//   V converted in place to fp16 times 2^e, e the one power of two that puts the tile's max |v| in [2^14, 2^15)
+//   (exact: a 16-bit input has at most 11 significant bits; nothing overflows, and entries below 2^-28 of the
+//   largest lose relative precision only); fp16 inputs are used as they are;
+//   O = P V (tcgen05 kind::f16, P from tensor memory) into columns [64, 64 + D); O 2^-e / l rounded over the spent V,
+//   one TMA store, lse = m + log l; the next tile's V is loaded once the store has read the buffer.
+// P keeps fp16's 11 significant bits in the P V product (the reference's kernels round P to the 16-bit input type,
+// models/fused_attn/triton_kernels.py:576-586); otherwise the math of the reference's _fwd_kernel (:98-163) with the
+// whole key range in one tile.
+template <typename T, int D>
+__global__ void __launch_bounds__(128, D == 64 ? 4 : 2)
+    tc_fwd_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                        float* __restrict__ lse, const ShortGeom geo, float scale) {
+  using L = FwdShortLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  unsigned char* sq = smem;
+  unsigned char* sk = smem + L::kOp;
+  unsigned char* sv = smem + 2 * L::kOp;
+  __shared__ uint64_t qk_full, v_full, s_full, o_full;
+  __shared__ uint32_t tmem_slot, vmax_slot[4];
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = geo.N, rows = geo.per * geo.N;
+  const int kc = (rows + 31) & ~31;  // key columns computed (the S product's N; the P V product's K)
+  constexpr bool kB = is_bf16<T>();
+  const uint32_t id_s = idesc_f16(kB, 0, 0, 128, kc);
+  constexpr uint32_t kIdPV = idesc_f16(false, 0, 1, 128, D);  // fp16 P (tensor memory) x fp16 V (shared, MN-major)
+  const int n_local = geo.tiles > static_cast<int>(blockIdx.x)
+                          ? (geo.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                          : 0;
+  const uint32_t box_bytes = 128u * static_cast<uint32_t>(rows);  // one 64-column box of `rows` rows
+
+  // Clear the tiles once: rows at or beyond `rows` (never written by the boxes) must be finite for the products.
+  for (uint32_t i = tid * 16u; i < L::kBytes; i += L::kThreads * 16u)
+    *reinterpret_cast<uint4*>(smem + i) = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    mbar_init(&qk_full, 1);
+    mbar_init(&v_full, 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&o_full, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+  const bool leader = tid == 0;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t tS = tmem + lane_off, tO = tmem + 64 + lane_off;
+  const int r = tid;
+  const bool row_ok = r < rows;
+  const int j0_row = row_ok ? (r / N) * N : 0;  // this row's key columns: [j0_row, j1_row)
+  const int j1_row = row_ok ? j0_row + N : 0;
+  const int wlo = __reduce_min_sync(0xffffffffu, row_ok ? j0_row : 1 << 20);
+  const int whi = __reduce_max_sync(0xffffffffu, j1_row);
+  bool chunk_any[4], chunk_all[4];  // the warp's 32-column chunks: reached by some row / wholly inside every row's
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    chunk_any[c] = 32 * c < kc && 32 * c < whi && 32 * c + 32 > wlo;
+    chunk_all[c] = __all_sync(0xffffffffu, row_ok && j0_row <= 32 * c && 32 * c + 32 <= j1_row);
+  }
+  const float sl2 = scale * 1.4426950408889634f;  // exp(s scale - m) = 2^(s sl2 - m log2 e)
+
+  auto coords = [&](int li, int& hb, int& h0) {
+    short_tile_coords(geo, static_cast<int>(blockIdx.x) + li * static_cast<int>(gridDim.x), hb, h0);
+  };
+  auto load_qk = [&](int li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    mbar_arrive_expect_tx(&qk_full, 2u * (D / 64) * box_bytes);
+    for (int hh = 0; hh < D / 64; ++hh) {
+      tma_load_4d(sq + hh * kHalfBytes, &tq, &qk_full, hh * 64, 0, h0, hb);
+      tma_load_4d(sk + hh * kHalfBytes, &tk, &qk_full, hh * 64, 0, h0, hb);
+    }
+  };
+  auto load_v = [&](int li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    mbar_arrive_expect_tx(&v_full, (D / 64) * box_bytes);
+    for (int hh = 0; hh < D / 64; ++hh) tma_load_4d(sv + hh * kHalfBytes, &tv, &v_full, hh * 64, 0, h0, hb);
+  };
+  if (leader && n_local > 0) {
+    tma_prefetch_desc(&tq), tma_prefetch_desc(&tk), tma_prefetch_desc(&tv), tma_prefetch_desc(&to);
+    load_qk(0);
+    load_v(0);
+  }
+
+  bool ok = true;
+  for (int li = 0; li < n_local && ok; ++li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    const uint32_t par = static_cast<uint32_t>(li) & 1u;
+    // ---- S = Q K^T
+    if (leader) {
+      ok = mbar_wait_or_abort(&qk_full, par, 441, abort);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem, desc_kmajor(sq, kk), desc_kmajor(sk, kk), id_s, kk > 0 ? 1u : 0u);
+        mma_commit(&s_full);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&s_full, par, 444, abort));
+    if (!ok) break;
+    tc_fence_after();
+    // Q and K are spent: the next tile's Q and K go in now.
+    if (leader && li + 1 < n_local) load_qk(li + 1);
+    int j0, j1;  // re-read per tile through an opaque move: keeps per-column masks from being hoisted and held
+    asm volatile("mov.b32 %0, %1;" : "=r"(j0) : "r"(j0_row));
+    asm volatile("mov.b32 %0, %1;" : "=r"(j1) : "r"(j1_row));
+    // ---- pass 1: row max of y = s scale log2(e) (any sign of scale), one chunk per tensor-memory round trip
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      if (!chunk_any[cc]) continue;
+      uint32_t x[32];
+      tmem_ld32(tS + 32 * cc, x);
+      tmem_wait_ld_regs(x);
+      if (chunk_all[cc]) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          mx[0] = fmax3(mx[0], __uint_as_float(x[e]) * sl2, __uint_as_float(x[e + 1]) * sl2);
+          mx[1] = fmax3(mx[1], __uint_as_float(x[e + 2]) * sl2, __uint_as_float(x[e + 3]) * sl2);
+          mx[2] = fmax3(mx[2], __uint_as_float(x[e + 4]) * sl2, __uint_as_float(x[e + 5]) * sl2);
+          mx[3] = fmax3(mx[3], __uint_as_float(x[e + 6]) * sl2, __uint_as_float(x[e + 7]) * sl2);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool in = 32 * cc + e >= j0 && 32 * cc + e < j1;
+          mx[e & 3] = in ? fmaxf(mx[e & 3], __uint_as_float(x[e]) * sl2) : mx[e & 3];
+        }
+      }
+      asm volatile("" : "+f"(mx[0]), "+f"(mx[1]), "+f"(mx[2]), "+f"(mx[3]));  // finish this chunk first
+    }
+    const float m2 = row_ok ? fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) : 0.f;  // max of y
+    // ---- pass 2: P = 2^(y - m2) as fp16 pairs: keys [32 c, 32 c + 32) into columns [16 c, 16 c + 16), which hold
+    // scores that are already read (chunk c writes over chunk c / 2)
+    float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      if (32 * cc >= kc) continue;
+      uint32_t pk[16];
+      if (!chunk_any[cc]) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+      } else {
+        uint32_t x[32];
+        tmem_ld32(tS + 32 * cc, x);
+        tmem_wait_ld_regs(x);
+        if (chunk_all[cc]) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = exp2_approx(fmaf(__uint_as_float(x[e]), sl2, -m2));
+            const float p1 = exp2_approx(fmaf(__uint_as_float(x[e + 1]), sl2, -m2));
+            ls[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_f16(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const bool in0 = 32 * cc + e >= j0 && 32 * cc + e < j1;
+            const bool in1 = 32 * cc + e + 1 >= j0 && 32 * cc + e + 1 < j1;
+            const float p0 = in0 ? exp2_approx(fmaf(__uint_as_float(x[e]), sl2, -m2)) : 0.f;
+            const float p1 = in1 ? exp2_approx(fmaf(__uint_as_float(x[e + 1]), sl2, -m2)) : 0.f;
+            ls[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_f16(p0, p1);
+          }
+        }
+      }
+      tmem_st16(tS + 16 * cc, pk);
+    }
+    const float l = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+    tmem_wait_st();
+    tc_fence_before();
+    // ---- V to fp16 times 2^e, in place (bf16 inputs; fp16 inputs are used as they are)
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&v_full, par, 443, abort));
+    if (!ok) break;
+    float vscale_inv = 1.f;
+    if (kB) {
+      // max |v| over the tile (16-bit magnitudes order like their bit patterns)
+      uint32_t vm = 0;
+      if (row_ok) {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4*>(sv + (c >> 3) * kHalfBytes + sw128_off(r, c & 7));
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) vm = max(vm, max(w[q] & 0x7FFFu, (w[q] >> 16) & 0x7FFFu));
+        }
+      }
+      vm = __reduce_max_sync(0xffffffffu, vm);
+      if (lane == 0) vmax_slot[warp] = vm;
+      __syncthreads();
+      const uint32_t vmax = max(max(vmax_slot[0], vmax_slot[1]), max(vmax_slot[2], vmax_slot[3]));
+      int e = 14 - (static_cast<int>(vmax >> 7) - 127);  // bf16 exponent of the largest |v|
+      e = max(-100, min(100, e));
+      const float vs = exp2f(static_cast<float>(e));
+      vscale_inv = exp2f(static_cast<float>(-e));
+      if (row_ok) {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          uint4* a = reinterpret_cast<uint4*>(sv + (c >> 3) * kHalfBytes + sw128_off(r, c & 7));
+          const uint4 u = *a;
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          uint32_t h[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) h[q] = pack_f16(unpack_lo<T>(w[q]) * vs, unpack_hi<T>(w[q]) * vs);
+          *a = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    __syncthreads();  // P stored by every thread; V converted
+    // ---- O = P V
+    if (leader) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        if (kk < kc / 16) mma_ts(tmem + 64, tmem + kk * 8, desc_mnmajor(sv, kk), kIdPV, kk > 0 ? 1u : 0u);
+      mma_commit(&o_full);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&o_full, par, 445, abort));
+    if (!ok) break;
+    tc_fence_after();
+    // ---- epilogue: O 2^-e / l over the spent V, rows >= `rows` as zeros; lse
+    const float inv = (row_ok && l > 0.f) ? vscale_inv / l : 0.f;
+    int rt;  // the row, re-read here so the staging addresses are formed here
+    asm volatile("mov.b32 %0, %1;" : "=r"(rt) : "r"(r));
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t v[32];
+      tmem_ld32(tO + c, v);
+      tmem_wait_ld_regs(v);
+      unsigned char* half = sv + (c >> 6) * kHalfBytes;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (row_ok) {
+          u.x = pack2<T>(__uint_as_float(v[8 * q + 0]) * inv, __uint_as_float(v[8 * q + 1]) * inv);
+          u.y = pack2<T>(__uint_as_float(v[8 * q + 2]) * inv, __uint_as_float(v[8 * q + 3]) * inv);
+          u.z = pack2<T>(__uint_as_float(v[8 * q + 4]) * inv, __uint_as_float(v[8 * q + 5]) * inv);
+          u.w = pack2<T>(__uint_as_float(v[8 * q + 6]) * inv, __uint_as_float(v[8 * q + 7]) * inv);
+        }
+        *reinterpret_cast<uint4*>(half + sw128_off(rt, ((c & 63) >> 3) + q)) = u;
+      }
+    }
+    if (row_ok && h0 + r / N < geo.hs) {
+      const int64_t slice = static_cast<int64_t>(hb) * geo.hs + h0 + r / N;
+      lse[slice * N + (r - j0_row)] = m2 * 0.6931471805599453f + logf(l);  // natural units: ln 2 * max of y
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (leader) {
+      for (int hh = 0; hh < D / 64; ++hh) tma_store_4d(&to, sv + hh * kHalfBytes, hh * 64, 0, h0, hb);
+      tma_store_commit();
+      tma_store_wait_read();  // V's buffer is free again
+      if (li + 1 < n_local) load_v(li + 1);
+    }
+  }
+  if (leader) tma_store_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+}  // namespace ebr

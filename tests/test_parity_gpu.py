@@ -164,6 +164,33 @@ def test_parity_16bit(shape, dtype):
         check_out(got, ref, dtype, GRAD_TOL, name)
 
 
+# Short-sequence packing: floor(128 / N) slices per 128-row tile, slice counts that do not divide evenly (the last
+# tile is partial), and strided views whose slices are not at a uniform stride (the tile then packs a divisor of H).
+PACKED = [
+    ((3, 8, 17, 64), "contiguous"),   # 7 slices per tile, 24 slices: 4 tiles, the last with 3
+    ((2, 5, 33, 64), "contiguous"),   # 3 per tile, 10 slices
+    ((1, 5, 64, 64), "contiguous"),   # 2 per tile, 5 slices
+    ((3, 3, 40, 128), "contiguous"),  # 3 per tile at D = 128, 9 slices
+    ((2, 8, 17, 64), "qkv"),          # strided views: 4 heads (a divisor of 8) of one batch row per tile
+    ((2, 6, 33, 64), "qkv"),          # 3 heads per tile
+    ((37, 3, 100, 64), "contiguous"),  # one slice per tile, many tiles per CTA
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape,layout", PACKED, ids=lambda x: "x".join(map(str, x)) if isinstance(x, tuple) else x)
+def test_parity_short_packed(shape, layout, dtype):
+    B, H, N, D = shape
+    scale = D**-0.5
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=N * 3 + H, layout=layout)
+    o, lse, grads, hs = run_all(q, k, v, do, gq, gk, gv, scale)
+    O, LSE, G, HS = oracle_all(q, k, v, do, gq, gk, gv, o, lse, scale)
+    check_out(o, O, dtype, FWD_TOL, "o")
+    assert _maxrel(lse, LSE) < 1e-5
+    for name, got, ref in zip(("dq", "dk", "dv", "hq", "hk", "hv", "hdo"), (*grads, *hs), (*G, *HS)):
+        check_out(got, ref, dtype, GRAD_TOL, name)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_parity_growing_logits(dtype):
     """Logits that grow from one key tile to the next, differently per row, so the forward's lazy rescale of O runs

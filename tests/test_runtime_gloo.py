@@ -1,5 +1,6 @@
-"""Data-parallel plumbing on CPU ranks (gloo, world size 2): the flat-bucket gradient all-reduce equals the
-reference's per-tensor all-reduce, weights broadcast from rank 0, the checksum check catches divergence, and a rank
+"""Data-parallel plumbing on CPU ranks (gloo, world size 2): the flat-bucket and the overlapped bucketed gradient
+all-reduces equal the reference's per-tensor all-reduce, a parameter no rank produced a gradient for stays without
+one (as the reference skips it), weights broadcast from rank 0, the checksum check catches divergence, and a rank
 that fails is seen by the others as an error instead of a hang."""
 
 from __future__ import annotations
@@ -49,6 +50,60 @@ def _worker_allreduce(rank, world, port, q):
         n = runtime.allreduce_gradients(list(m.parameters()))
         ok = all(torch.allclose(p.grad, r, atol=1e-6) for p, r in zip(m.parameters(), ref))
         q.put((rank, ok, n))
+    finally:
+        dist.destroy_process_group()
+
+
+class _TwoHeads(torch.nn.Module):
+    """A trunk and two heads; ``head_b`` is used only by rank 1, ``unused`` by no rank."""
+
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(7)
+        self.unused = torch.nn.Linear(16, 3)  # registered first: it lands in the last bucket
+        self.trunk = torch.nn.Linear(8, 16)
+        self.head_a = torch.nn.Linear(16, 3)
+        self.head_b = torch.nn.Linear(16, 3)
+
+    def forward(self, x, use_b):
+        h = torch.tanh(self.trunk(x))
+        y = self.head_a(h).square().sum()
+        return y + self.head_b(h).square().sum() if use_b else y
+
+
+def _worker_buckets(rank, world, port, q):
+    from ebr_b200 import runtime
+
+    _init(rank, world, port)
+    try:
+        results = {}
+        x = torch.randn(4, 8, generator=torch.Generator().manual_seed(rank))
+        # The reference's result: per-tensor SUM, a missing gradient counting as zero (from a plain backward).
+        m = _TwoHeads()
+        m(x, use_b=rank == 1).backward()
+        exp = []
+        for p in m.parameters():
+            t = torch.zeros_like(p) if p.grad is None else p.grad.clone()
+            dist.all_reduce(t)
+            exp.append(t)
+        for mode in ("flat", "buckets"):
+            m = _TwoHeads()
+            buckets = runtime.GradientBuckets(list(m.parameters()), bucket_mb=0.0003) if mode == "buckets" else None
+            if buckets:
+                buckets.start()  # no other collective may run between start() and finish()
+            m(x, use_b=rank == 1).backward()
+            if buckets:
+                buckets.finish()
+                results["early"] = buckets.launched_early
+                results["nbuckets"] = len(buckets.buckets)
+            else:
+                runtime.allreduce_gradients(list(m.parameters()))
+            for (n, p), e in zip(m.named_parameters(), exp):
+                if n.startswith("unused"):
+                    results[f"{mode}:{n}"] = p.grad is None
+                else:
+                    results[f"{mode}:{n}"] = p.grad is not None and torch.allclose(p.grad, e, atol=1e-6)
+        q.put((rank, results))
     finally:
         dist.destroy_process_group()
 
@@ -114,3 +169,16 @@ def test_param_sync_detects_divergence():
 def test_dead_rank_is_an_error_not_a_hang():
     res = _run(_worker_fail)
     assert len(res) == 1 and res[0][0] == 0 and res[0][1] != "completed", res
+
+
+def test_bucketed_overlapped_allreduce_and_missing_gradients():
+    """Both all-reduce forms give the per-tensor sums; a gradient only rank 1 has is summed onto both ranks; a
+    parameter no rank used keeps grad None; with tiny buckets several are launched from the hooks mid-backward."""
+    res = _run(_worker_buckets)
+    assert len(res) == 2, res
+    for rank, r in res:
+        bad = {k: v for k, v in r.items() if k not in ("early", "nbuckets") and not v}
+        assert not bad, (rank, bad)
+        assert r["nbuckets"] > 2, r
+        if rank == 1:  # every gradient but the unused one: buckets go out during the backward
+            assert r["early"] >= 1, r
