@@ -15,7 +15,9 @@ attention, torch CPU for the rest) timed on a bounded sample on this host.
 ``--impl reference`` times only that CPU path (rank 0) on the same config and prints its own line.
 ``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape), and with
 ``--passes qkv_rope,qkv_unfused`` the fused qkv projection against cuBLAS + the split kernel at the same shapes.
-``--mode train`` times BASELINE config 2's training step (double backward, flat-bucket NCCL all-reduce, AdamW).
+``--mode train`` times a training step (double backward, bucketed NCCL all-reduce overlapped with the backward,
+AdamW) on the sudoku-like 81-token workload or, with ``--train-workload sxm100``, the multi-solution 100-token
+workload with 8 candidate trajectories per input.
 """
 
 from __future__ import annotations
@@ -490,7 +492,9 @@ def run_ours(args) -> None:
 # --------------------------------------------------------------------------------------------------------- training
 
 
-TRAIN_ROWS, TRAIN_BOARD, TRAIN_MICROSTEPS, TRAIN_GRADED = 768, 9, 16, 7
+TRAIN_MICROSTEPS, TRAIN_GRADED = 16, 7
+SUDOKU_ROWS = 768                    # sudoku-like training (81 tokens): rows per GPU
+SXM_INPUTS, SXM_K, SXM_BOARD = 32, 8, 10  # multi-solution training: inputs per GPU (256 over 8 GPUs), candidates each
 
 
 def sudoku_like_tokens(n: int, gen: torch.Generator) -> torch.Tensor:
@@ -501,13 +505,37 @@ def sudoku_like_tokens(n: int, gen: torch.Generator) -> torch.Tensor:
     return torch.where(blank, torch.zeros_like(digits), digits).to(torch.int32), torch.randint(1, 10, (n, 81), generator=gen)
 
 
+def binary_grid_tokens(n: int, gen: torch.Generator, board: int = SXM_BOARD, ones: int = SXM_BOARD):
+    """Synthetic stand-in for the multi-solution boards (N-Queens 10 x 10 is not available offline): inputs are
+    binary grids with exactly ``ones`` ones at uniformly random cells; labels are binary grids with one 1 per row at
+    a random column (a permutation), so every label also has ``ones`` ones."""
+    cells = board * board
+    inputs = torch.zeros(n, cells, dtype=torch.int32)
+    for i in range(n):
+        inputs[i, torch.randperm(cells, generator=gen)[:ones]] = 1
+    cols = torch.stack([torch.randperm(board, generator=gen) for _ in range(n)])
+    labels = torch.zeros(n, board, board, dtype=torch.int64)
+    labels.scatter_(2, cols.unsqueeze(-1), 1)
+    return inputs, labels.view(n, cells)
+
+
 def run_train(args) -> None:
-    """BASELINE config 2 on each rank (weak scaling): 768 rows, L = 81, 16 microsteps per segment of which the last
-    7 carry a graph (create_graph=True, so the backward runs the attention's double backward), cross-entropy of the
-    decoded endpoint, backward, one flat-bucket NCCL all-reduce of all gradients, AdamW step."""
+    """A training step on each rank (weak scaling). Workloads:
+
+    * ``sudoku81``: 768 rows per GPU on a 9 x 9 board (81 tokens, vocab 10), 16 microsteps per segment of which the
+      last 7 carry a graph (create_graph=True: the backward runs the attention's double backward), stablemax cross
+      entropy of the decoded endpoint;
+    * ``sxm100``: multi-solution training on a 10 x 10 binary board (100 tokens): 32 inputs per GPU x 8 candidate
+      trajectories (256 latent rows over 8 GPUs gives the workload's 256 x 8), the candidates' 16-microstep segment
+      without a graph, each input's best candidate recomputed through its 7 graded microsteps (forward SXM);
+      ``--heads 4`` runs it at head dim 128 (the reference's multi-solution recipe: hidden 512, 4 heads).
+
+    Then the outer backward with the gradients all-reduced in buckets overlapped with it (NCCL; none at one GPU) and
+    an AdamW step. ``value`` counts latent rows x microsteps per second over all ranks: for sxm100 every candidate's
+    16 microsteps (the graded recompute of the winners is extra work, not counted)."""
     from ebr_b200 import _native, fused_attn, runtime
     from ebr_b200.build import build
-    from ebr_b200.energy import LatentEnergyNet, NetShape, train_segment_loss
+    from ebr_b200.energy import LatentEnergyNet, NetShape, sxm_explore_loss, train_segment_loss
 
     rank, world, local = runtime.init_distributed()
     device = torch.device("cuda", local)
@@ -517,23 +545,43 @@ def run_train(args) -> None:
     if world > 1:
         torch.distributed.barrier()
     torch.manual_seed(0)
-    model = LatentEnergyNet(NetShape(board=(TRAIN_BOARD, TRAIN_BOARD), vocab=10)).to(device)
+    gen = torch.Generator().manual_seed(2000 + rank)
+    sxm = args.train_workload == "sxm100"
+    if sxm:
+        shape = NetShape(board=(SXM_BOARD, SXM_BOARD), vocab=2, heads=args.heads)
+        tok, labels = binary_grid_tokens(SXM_INPUTS, gen)
+        rows, counted_rows = SXM_INPUTS, SXM_INPUTS * SXM_K
+    else:
+        shape = NetShape(board=(9, 9), vocab=10, heads=args.heads)
+        tok, labels = sudoku_like_tokens(SUDOKU_ROWS, gen)
+        rows, counted_rows = SUDOKU_ROWS, SUDOKU_ROWS
+    model = LatentEnergyNet(shape).to(device)
     runtime.broadcast_model(model)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
-    gen = torch.Generator().manual_seed(2000 + rank)
-    tok, labels = sudoku_like_tokens(TRAIN_ROWS, gen)
     tok, labels = tok.to(device), labels.to(device)
-    z0 = model.fresh_states(TRAIN_ROWS)
+    z0 = model.fresh_states(rows)
+    challengers = torch.stack([model.fresh_states(rows) for _ in range(SXM_K - 1)]) if sxm else None
     params = [p for p in model.parameters() if p.requires_grad]
+    buckets = runtime.GradientBuckets(params, bucket_mb=16.0)
+    exposed = []  # host-side wait for the collectives after the backward (ms), per step
 
     def step():
+        nonlocal challengers
         x = model.embed(tok)
-        loss = train_segment_loss(model, z0, x, labels, prefix=TRAIN_MICROSTEPS - TRAIN_GRADED, graded=TRAIN_GRADED)
+        if sxm:
+            loss, _, challengers = sxm_explore_loss(model, z0, challengers, x, labels, TRAIN_MICROSTEPS - TRAIN_GRADED,
+                                                    TRAIN_GRADED)  # fmt: skip
+        else:
+            loss = train_segment_loss(model, z0, x, labels, TRAIN_MICROSTEPS - TRAIN_GRADED, TRAIN_GRADED)
         opt.zero_grad(set_to_none=True)
-        (loss / (TRAIN_ROWS * world)).backward()
-        runtime.allreduce_gradients(params)
+        buckets.start()
+        (loss / world).backward()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        buckets.finish()
+        e1.record()
         opt.step()
-        return loss
+        return loss, (e0, e1)
 
     for _ in range(args.warmup):
         step()
@@ -543,19 +591,46 @@ def run_train(args) -> None:
         torch.distributed.barrier()
     launches0 = _native.launch_count()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = []
     with fused_attn.kernel_timer() as timer:
         a.record()
         for _ in range(args.steps):
-            loss = step()
+            loss, ev = step()
+            marks.append(ev)
         b.record()
         torch.cuda.synchronize()
     ms = runtime.max_over_ranks(a.elapsed_time(b))
+    tail_ms = runtime.max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in marks))
     ops = timer.summary()
     runtime.check_param_sync(model, rtol=1e-9)
-    value = world * TRAIN_ROWS * TRAIN_MICROSTEPS * args.steps / (ms / 1000.0)
+    # The gradient all-reduce alone, for the record: one flat bucket of every gradient, CUDA events (max over ranks).
+    nparam = sum(p.numel() for p in params)
+    ar_ms = None
+    if world > 1:
+        flat = torch.zeros(nparam, device=device)
+        for _ in range(3):
+            torch.distributed.all_reduce(flat)
+        torch.cuda.synchronize()
+        c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c.record()
+        for _ in range(10):
+            torch.distributed.all_reduce(flat)
+        d.record()
+        torch.cuda.synchronize()
+        ar_ms = runtime.max_over_ranks(c.elapsed_time(d) / 10)
+        del flat
+    value = world * counted_rows * TRAIN_MICROSTEPS * args.steps / (ms / 1000.0)
     if rank == 0:
+        head_dim = 512 // args.heads
+        if sxm:
+            workload = (f"multi-solution SXM training, 10x10 binary board (L=100), {SXM_INPUTS} inputs x {SXM_K} "
+                        f"candidates per GPU, {args.heads} heads x {head_dim}, 16 microsteps (last 7 graded, winners "
+                        "recomputed with a graph), double backward, AdamW")  # fmt: skip
+        else:
+            workload = (f"sudoku-like training (L=81), {SUDOKU_ROWS} rows per GPU, {args.heads} heads x {head_dim}, "
+                        "16 microsteps (last 7 graded), double backward, AdamW")  # fmt: skip
         line = {
-            "metric": "latent-descent training sample-steps/s (L=81, B=768)",
+            "metric": f"latent-descent training sample-steps/s ({args.train_workload})",
             "value": round(value, 3),
             "unit": "sample-steps/s",
             "n_gpus": world,
@@ -565,9 +640,13 @@ def run_train(args) -> None:
             "higher_is_better": True,
             "scaling": "weak",
             "dtype": "bf16",
-            "data": "synthetic (seeded sudoku-like boards; Sudoku-Extreme is not available offline), random-init weights",
-            "config": {"workload": "cfg2 training step (16 microsteps, last 7 graded, double backward, AdamW)",
-                       "rows_per_gpu": TRAIN_ROWS, "seq_len": 81, "parallelism": f"dp{world} (one flat NCCL all-reduce)"},
+            "data": "synthetic boards (the reference's datasets are not available offline), random-init weights",
+            "config": {"workload": workload, "rows_counted_per_gpu": counted_rows, "seq_len": shape.seq_len,
+                       "parallelism": f"dp{world}: gradients all-reduced in {len(buckets.buckets)} buckets overlapped "
+                                      "with the outer backward"},  # fmt: skip
+            "allreduce": {"params": nparam, "bytes": 4 * nparam, "buckets": len(buckets.buckets),
+                          "flat_allreduce_ms": None if ar_ms is None else round(ar_ms, 3),
+                          "exposed_after_backward_ms": round(tail_ms, 3)},  # fmt: skip
             "loss": float(loss.item()),
             "gpu_launches": int(_native.launch_count() - launches0),
             "attention_ms": {n: round(v["ms"], 3) for n, v in ops.items()},
@@ -724,6 +803,9 @@ def main() -> None:
     ap.add_argument("--head-dims", default="64,128")
     ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd",
                     help="sweep: which passes to time (also qkv_rope, qkv_unfused, o_proj, o_unfused: the projections)")
+    ap.add_argument("--train-workload", choices=["sudoku81", "sxm100"], default="sudoku81",
+                    help="train mode: sudoku81 (L=81, 768 rows per GPU) or sxm100 (L=100, 32 inputs x 8 candidates)")
+    ap.add_argument("--heads", type=int, default=8, help="train mode: attention heads (hidden 512; 4 heads = D 128)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

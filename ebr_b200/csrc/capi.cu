@@ -339,20 +339,26 @@ int launch_simt_bwd(int64_t B, int64_t H, int64_t N, int64_t D, double scale, co
 }
 
 template <typename T, int D>
-int launch_tc_bwd_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
-                         const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
-                         const ebr_operand* dout, void* dq, void* dk, void* dv, cudaStream_t st) {
-  using L = BwdSingleLayout<D>;
-  CUtensorMap tq, tk, tv, tdo;
-  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
-      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
+int launch_tc_bwd_short(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                        const ebr_operand* dout, void* dq, void* dk, void* dv, cudaStream_t st) {
+  using L = BwdShortLayout<D>;
+  const ShortPlan plan = short_plan(B, H, N, {q, k, v, dout});
+  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+  if (make_short_map(&tq, q, dtype, plan, D) || make_short_map(&tk, k, dtype, plan, D) ||
+      make_short_map(&tv, v, dtype, plan, D) || make_short_map(&tdo, dout, dtype, plan, D) ||
+      make_short_out_map(&tdq, dq, dtype, plan, H, D) || make_short_out_map(&tdk, dk, dtype, plan, H, D) ||
+      make_short_out_map(&tdv, dv, dtype, plan, H, D))
     return kNoTensorMap;
-  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_single_kernel<T, D>), device, L::kSmem, L::kTmemCols);
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bwd_short_kernel<T, D>), device, L::kSmem,
+                            L::kTmemCols, L::kThreads);
   if (s) return s;
-  tc_bwd_single_kernel<T, D><<<static_cast<unsigned>(B * H), 128, L::kSmem, st>>>(
-      tq, tk, tv, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(dq),
-      static_cast<T*>(dk), static_cast<T*>(dv), static_cast<int>(H), static_cast<int>(N), static_cast<float>(scale));
-  return check_launch("tc_bwd_single_kernel");
+  const int cap = L::kCtasPerSm * sm_count(device);
+  const unsigned grid = static_cast<unsigned>(plan.geo.tiles < cap ? plan.geo.tiles : cap);
+  tc_bwd_short_kernel<T, D><<<grid, L::kThreads, L::kSmem, st>>>(
+      tq, tk, tv, tdo, tdq, tdk, tdv, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(dq),
+      static_cast<T*>(dk), static_cast<T*>(dv), plan.geo, static_cast<float>(scale));
+  return check_launch("tc_bwd_short_kernel");
 }
 
 template <typename T, int D>
@@ -696,14 +702,14 @@ int ebr_attn_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, double s
   }
   if (N <= kTile && outs_ok && tc_eligible(dtype, D, {q, k, v, dout}, B, H, N)) {
     if (dtype == EBR_BFLOAT16)
-      s = D == 64 ? launch_tc_bwd_single<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
+      s = D == 64 ? launch_tc_bwd_short<__nv_bfloat16, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq,
                                                              dk, dv, st)
-                  : launch_tc_bwd_single<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout,
+                  : launch_tc_bwd_short<__nv_bfloat16, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout,
                                                               dq, dk, dv, st);
     else
-      s = D == 64 ? launch_tc_bwd_single<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+      s = D == 64 ? launch_tc_bwd_short<__half, 64>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
                                                      dv, st)
-                  : launch_tc_bwd_single<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
+                  : launch_tc_bwd_short<__half, 128>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, dq, dk,
                                                       dv, st);
     if (s != kNoTensorMap) return s;
   }

@@ -670,145 +670,6 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// ================================================================================================ backward, N <= 128
-
-template <int D>
-struct BwdSingleLayout {
-  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;
-  static constexpr uint32_t kQ = 0, kK = kQ + kOp, kV = kK + kOp, kDO = kV + kOp;
-  static constexpr uint32_t kP = kDO + kOp, kDS = kP + 2 * kHalfBytes;
-  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;
-  // TMEM columns: S [0,128), dP [128,256), dQ [256, 256+D), dK after it; dV after dK for D = 64, in S for D = 128.
-  static constexpr uint32_t cS = 0, cDP = 128, cDQ = 256, cDK = 256 + D, cDV = (D == 64) ? 384 : 0;
-};
-
-// One CTA per (b, h) slice with N <= 128: S and dP once, P and dS to shared memory, then dQ = dS K, dK = dS^T Q and
-// dV = P^T dO from the same tiles (the reference's SINGLE mode, triton_kernels.py:250-264, :742-768).
-template <typename T, int D>
-__global__ void __launch_bounds__(128, 1)
-    tc_bwd_single_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                         const T* __restrict__ o, const float* __restrict__ lse, T* __restrict__ dq,
-                         T* __restrict__ dk, T* __restrict__ dv, int H, int N, float scale) {
-  using L = BwdSingleLayout<D>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  unsigned char* sQ = smem + L::kQ;
-  unsigned char* sK = smem + L::kK;
-  unsigned char* sV = smem + L::kV;
-  unsigned char* sDO = smem + L::kDO;
-  unsigned char* sP = smem + L::kP;
-  unsigned char* sDS = smem + L::kDS;
-  __shared__ uint64_t bar_load, bar_mma;
-  __shared__ uint32_t tmem_slot;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);  // S, dP
-  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);    // dQ = dS K
-  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);    // dK = dS^T Q, dV = P^T dO
-
-  if (tid == 0) {
-    mbar_init(&bar_load, 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-    mbar_arrive_expect_tx(&bar_load, 4u * L::kOp);
-#pragma unroll
-    for (int hh = 0; hh < D / 64; ++hh) {
-      tma_load_4d(sQ + hh * kHalfBytes, &tq, &bar_load, hh * 64, 0, h, b);
-      tma_load_4d(sK + hh * kHalfBytes, &tk, &bar_load, hh * 64, 0, h, b);
-      tma_load_4d(sV + hh * kHalfBytes, &tv, &bar_load, hh * 64, 0, h, b);
-      tma_load_4d(sDO + hh * kHalfBytes, &tdo, &bar_load, hh * 64, 0, h, b);
-    }
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  // Row statistics of this thread's query row while the tiles land: lse and D = <dO, O> (stored O).
-  const int row = tid;
-  const bool row_ok = row < N;
-  const int64_t grow = static_cast<int64_t>(bh) * N + row;
-  const float Li = row_ok ? lse[grow] : 0.f;
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  bool fail = !mbar_wait(&bar_load, 0, 201);
-  if (!__syncthreads_or(fail)) {
-    if (tid == 0) {
-      tc_fence_after();
-      mma_rows_x_rows<D>(tmem + L::cS, sQ, sK, kIdNN, false);
-      mma_rows_x_rows<D>(tmem + L::cDP, sDO, sV, kIdNN, false);
-      mma_commit(&bar_mma);
-    }
-    float Di = 0.f;
-    if (row_ok) {
-      const T* orow = o + grow * D;
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        float x[8], y[8];
-        ld_row8<T>(sDO, row, c, x);
-        ld_global8<T>(orow + 8 * c, y);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) Di += x[i] * y[i];
-      }
-    }
-    fail |= !mbar_wait(&bar_mma, 0, 202);
-    if (!__syncthreads_or(fail)) {
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kTile; c += 32) {
-        uint32_t rs[32], rp[32];
-        tmem_ld32(tmem + L::cS + lane_off + c, rs);
-        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
-        tmem_wait_ld();
-        uint32_t pk[16], dk_[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p[2], ds[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const bool ok = row_ok && (c + e + u < N);
-            p[u] = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
-            ds[u] = p[u] * (__uint_as_float(rp[e + u]) - Di);
-          }
-          pk[e >> 1] = pack2<T>(p[0], p[1]);
-          dk_[e >> 1] = pack2<T>(ds[0], ds[1]);
-        }
-        st_row32(sP, row, c, pk);
-        st_row32(sDS, row, c, dk_);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        mma_tile_x_rows(tmem + L::cDQ, sDS, sK, kIdKM, false);
-        mma_tileT_x_rows(tmem + L::cDK, sDS, sQ, kIdMM, false);
-        mma_tileT_x_rows(tmem + L::cDV, sP, sDO, kIdMM, false);
-        mma_commit(&bar_mma);
-      }
-      fail |= !mbar_wait(&bar_mma, 1, 203);
-      if (!__syncthreads_or(fail)) {
-        tc_fence_after();
-        // Lane t holds query row t of dQ and key row t of dK, dV.
-        T* off = nullptr;
-        store_row_from_tmem<T, D>(tmem + L::cDQ + lane_off, scale, row_ok ? dq + grow * D : off);
-        store_row_from_tmem<T, D>(tmem + L::cDK + lane_off, scale, row_ok ? dk + grow * D : off);
-        store_row_from_tmem<T, D>(tmem + L::cDV + lane_off, 1.f, row_ok ? dv + grow * D : off);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-}
-
 // ================================================================================================ double backward, N <= 128
 
 struct BobSingleLayout {  // D = 64

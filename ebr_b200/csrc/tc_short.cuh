@@ -333,4 +333,282 @@ __global__ void __launch_bounds__(128, D == 64 ? 4 : 2)
   if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
 }
 
+// ================================================================================================ backward
+
+template <int D>
+struct BwdShortLayout {
+  static constexpr uint32_t kOp = (D / 64) * kHalfBytes;  // one [128 x D] 16-bit tile
+  // Q, K, V, dO; then P over the spent V (its first 64-key half; the second half has its own buffer at D = 64) and
+  // dS in its own [128 x 128] tile.
+  static constexpr uint32_t kQ = 0, kK = kOp, kV = 2 * kOp, kDO = 3 * kOp;
+  static constexpr uint32_t kP1 = 4 * kOp;                              // P keys [64, 128) (D = 64 only)
+  static constexpr uint32_t kDS = D == 64 ? kP1 + kHalfBytes : 4 * kOp;
+  static constexpr uint32_t kBytes = kDS + 2 * kHalfBytes;
+  // The barriers live after the tiles and there is no static shared memory, so the dynamic block starts on the
+  // CTA's shared-memory base (1024-byte aligned; checked at run time) and needs no alignment slack: two CTAs of
+  // 112 KiB + 64 B then fit one SM's 228 KiB.
+  static constexpr uint32_t kSmem = kBytes + 64;
+  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;
+  // S [0, 128), dP [128, 256); then dV [0, D), dK [D, 2 D), dQ [2 D, 3 D) over them.
+  static constexpr uint32_t cS = 0, cDP = 128, cDV = 0, cDK = D, cDQ = 2 * D;
+  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+  static constexpr int kThreads = 128;
+};
+
+// Backward for N <= 128 (packed tiles as in the forward), persistent; kCtasPerSm CTAs share an SM so that one tile's
+// loads and products overlap another's pointwise work. Thread r owns row r of the tile: query row r for S, dP and dQ,
+// key row r for dK and dV; thread 0 also issues the TMA loads and the tcgen05 products. Per tile:
+//   S = Q K^T and dP = dO V^T into tensor memory; meanwhile each thread reads lse and D = <dO, O> of its row (O, the
+//   stored forward output, from global memory);
+//   P = exp(s scale - lse) (0 outside the row's slice) and dS = P (dP - D), rounded to the input type, written as
+//   [query x key] tiles to shared memory (P over the spent V);
+//   dV = P^T dO, dK = dS^T Q, dQ = dS K into tensor memory over the spent S and dP; once they are done the next tile's
+//   inputs are loaded, and the three gradients (dK and dQ times scale) are rounded into the spent dS and P tiles and
+//   written with TMA stores at D = 64, or go to global memory row by row at D = 128.
+// The reference's SINGLE mode (models/fused_attn/triton_kernels.py:250-264, :742-768): D from the stored O
+// (reference.py:44-45), P and dS rounded to the input type before their products (:576-586).
+template <typename T, int D>
+__global__ void __launch_bounds__(128, D == 64 ? 2 : 1)
+    tc_bwd_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                        const __grid_constant__ CUtensorMap tdq, const __grid_constant__ CUtensorMap tdk,
+                        const __grid_constant__ CUtensorMap tdv, const T* __restrict__ o,
+                        const float* __restrict__ lse, T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv,
+                        const ShortGeom geo, float scale) {
+  using L = BwdShortLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sK = smem + L::kK;
+  unsigned char* sV = smem + L::kV;
+  unsigned char* sDO = smem + L::kDO;
+  unsigned char* sDS = smem + L::kDS;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBytes);
+  uint64_t& in_full = bars[0];
+  uint64_t& s_full = bars[1];
+  uint64_t& g_full = bars[2];
+  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(smem + L::kBytes + 24);
+  int& abort_flag = *reinterpret_cast<int*>(smem + L::kBytes + 28);
+  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need a 1024-byte-aligned base
+    if (threadIdx.x == 0) atomicExch(&g_device_error, 460);
+    return;
+  }
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int N = geo.N, rows = geo.per * geo.N;
+  const int kc = (rows + 31) & ~31;   // key columns computed (S / dP N; the dQ product's K)
+  const int kr = (rows + 15) & ~15;   // query rows reduced over (the dV / dK products' K)
+  constexpr bool kB = is_bf16<T>();
+  const uint32_t id_nn = idesc_f16(kB, 0, 0, 128, kc);      // S, dP
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);   // dQ = dS K
+  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);   // dK = dS^T Q, dV = P^T dO
+  const int n_local = geo.tiles > static_cast<int>(blockIdx.x)
+                          ? (geo.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                          : 0;
+  const uint32_t box_bytes = 128u * static_cast<uint32_t>(rows);
+  // P's two 64-key halves: the spent V (and at D = 64 its own buffer for the second half).
+  auto p_half = [&](int hh) -> unsigned char* { return (D == 64 && hh == 1) ? smem + L::kP1 : sV + hh * kHalfBytes; };
+
+  for (uint32_t i = tid * 16u; i < L::kBytes; i += L::kThreads * 16u)
+    *reinterpret_cast<uint4*>(smem + i) = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    mbar_init(&in_full, 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&g_full, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+  const bool leader = tid == 0;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const int r = tid;
+  const bool row_ok = r < rows;
+  const int j0_row = row_ok ? (r / N) * N : 0;
+  const int j1_row = row_ok ? j0_row + N : 0;
+
+  auto coords = [&](int li, int& hb, int& h0) {
+    short_tile_coords(geo, static_cast<int>(blockIdx.x) + li * static_cast<int>(gridDim.x), hb, h0);
+  };
+  auto load = [&](int li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    mbar_arrive_expect_tx(&in_full, 4u * (D / 64) * box_bytes);
+    for (int hh = 0; hh < D / 64; ++hh) {
+      tma_load_4d(sQ + hh * kHalfBytes, &tq, &in_full, hh * 64, 0, h0, hb);
+      tma_load_4d(sK + hh * kHalfBytes, &tk, &in_full, hh * 64, 0, h0, hb);
+      tma_load_4d(sV + hh * kHalfBytes, &tv, &in_full, hh * 64, 0, h0, hb);
+      tma_load_4d(sDO + hh * kHalfBytes, &tdo, &in_full, hh * 64, 0, h0, hb);
+    }
+  };
+  if (leader && n_local > 0) {
+    tma_prefetch_desc(&tq), tma_prefetch_desc(&tk), tma_prefetch_desc(&tv), tma_prefetch_desc(&tdo);
+    load(0);
+  }
+
+  constexpr bool kStaged = D == 64;  // gradients leave through TMA stores from the spent dS and P tiles
+  bool ok = true;
+  for (int li = 0; li < n_local && ok; ++li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    const uint32_t par = static_cast<uint32_t>(li) & 1u;
+    const bool mine = row_ok && h0 + r / N < geo.hs;  // this row is a real row of a real slice
+    const int64_t grow = mine ? (static_cast<int64_t>(hb) * geo.hs + h0 + r / N) * N + (r - j0_row) : 0;
+    // Row statistics while the inputs land and the products run: lse, and O's row for D = <dO, O>.
+    const float Li = mine ? lse[grow] : 0.f;
+    uint4 orow[D / 8];
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c)
+      orow[c] = mine ? *reinterpret_cast<const uint4*>(o + grow * D + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+    if (leader) {
+      ok = mbar_wait_or_abort(&in_full, par, 451, abort);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          mma_ss(tmem + L::cS, desc_kmajor(sQ, kk), desc_kmajor(sK, kk), id_nn, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + L::cDP, desc_kmajor(sDO, kk), desc_kmajor(sV, kk), id_nn, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&in_full, par, 452, abort));
+    if (!ok) break;
+    float Di = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      float x[8];
+      ld_row8<T>(sDO, r, c, x);
+      const uint32_t w[4] = {orow[c].x, orow[c].y, orow[c].z, orow[c].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) Di += x[2 * q] * unpack_lo<T>(w[q]) + x[2 * q + 1] * unpack_hi<T>(w[q]);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&s_full, par, 453, abort));
+    if (!ok) break;
+    if (kStaged && li > 0) {  // the previous tile's gradient stores must have read the dS and P tiles
+      if (leader) tma_store_wait_read();
+      __syncthreads();
+    }
+    tc_fence_after();
+    int j0, j1;  // re-read per tile through an opaque move: keeps per-column masks from being hoisted and held
+    asm volatile("mov.b32 %0, %1;" : "=r"(j0) : "r"(j0_row));
+    asm volatile("mov.b32 %0, %1;" : "=r"(j1) : "r"(j1_row));
+    // P and dS, 32 key columns at a time, as 16-bit [query x key] tiles (every row written: zeros where masked).
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t pk[16], dk16[16];
+      if (c < kc) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tmem + L::cS + lane_off + c, rs);
+        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
+        tmem_wait_ld_regs(rs);
+        tmem_wait_ld_regs(rp);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pp[2], ds[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool in = c + e + u >= j0 && c + e + u < j1;
+            pp[u] = in ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+            ds[u] = pp[u] * (__uint_as_float(rp[e + u]) - Di);
+          }
+          pk[e >> 1] = pack2<T>(pp[0], pp[1]);
+          dk16[e >> 1] = pack2<T>(ds[0], ds[1]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = dk16[e] = 0u;
+      }
+      unsigned char* ph = p_half(c >> 6);
+      unsigned char* dh = sDS + (c >> 6) * kHalfBytes;
+      const int c0 = (c & 63) >> 3;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        *reinterpret_cast<uint4*>(ph + sw128_off(r, c0 + q)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                                           pk[4 * q + 3]);
+        *reinterpret_cast<uint4*>(dh + sw128_off(r, c0 + q)) = make_uint4(dk16[4 * q], dk16[4 * q + 1],
+                                                                           dk16[4 * q + 2], dk16[4 * q + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (leader) {
+      tc_fence_after();
+      // dV = P^T dO and dK = dS^T Q (M = keys, K = queries), dQ = dS K (M = queries, K = keys).
+      for (int kk = 0; kk < kr / 16; ++kk) {
+        const uint32_t acc = kk > 0 ? 1u : 0u;
+        const uint32_t pa = smem_u32(p_half(0)) + kk * 2048u;  // P read MN-major: M = keys, K-step kk = queries
+        const uint64_t pdesc = sw128_desc(pa, D == 64 ? (smem_u32(p_half(1)) - smem_u32(p_half(0))) : kHalfBytes,
+                                          1024u);
+        mma_ss(tmem + L::cDV, pdesc, desc_mnmajor(sDO, kk), kIdMM, acc);
+        mma_ss(tmem + L::cDK, desc_mnmajor(sDS, kk), desc_mnmajor(sQ, kk), kIdMM, acc);
+      }
+      for (int kk = 0; kk < kc / 16; ++kk)
+        mma_ss(tmem + L::cDQ, desc_kmajor(sDS, kk), desc_mnmajor(sK, kk), kIdKM, kk > 0 ? 1u : 0u);
+      mma_commit(&g_full);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&g_full, par, 454, abort));
+    if (!ok) break;
+    tc_fence_after();
+    if (leader && li + 1 < n_local) load(li + 1);  // every input buffer is spent
+    if constexpr (kStaged) {
+      // Gradients rounded into the spent tiles (dQ, dK over the two dS halves, dV over P's second half), rows
+      // >= `rows` as zeros, then one TMA store each: key row r of dK and dV, query row r of dQ.
+      int rt;  // the row, re-read here so the staging addresses are formed here
+      asm volatile("mov.b32 %0, %1;" : "=r"(rt) : "r"(r));
+      unsigned char* const dst[3] = {sDS, sDS + kHalfBytes, smem + L::kP1};
+      const uint32_t col[3] = {L::cDQ, L::cDK, L::cDV};
+      const float mul[3] = {scale, scale, 1.f};
+#pragma unroll
+      for (int g = 0; g < 3; ++g) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + col[g] + lane_off + c, v);
+          tmem_wait_ld_regs(v);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u = make_uint4(0u, 0u, 0u, 0u);
+            if (row_ok) {
+              u.x = pack2<T>(__uint_as_float(v[8 * q + 0]) * mul[g], __uint_as_float(v[8 * q + 1]) * mul[g]);
+              u.y = pack2<T>(__uint_as_float(v[8 * q + 2]) * mul[g], __uint_as_float(v[8 * q + 3]) * mul[g]);
+              u.z = pack2<T>(__uint_as_float(v[8 * q + 4]) * mul[g], __uint_as_float(v[8 * q + 5]) * mul[g]);
+              u.w = pack2<T>(__uint_as_float(v[8 * q + 6]) * mul[g], __uint_as_float(v[8 * q + 7]) * mul[g]);
+            }
+            *reinterpret_cast<uint4*>(dst[g] + sw128_off(rt, (c >> 3) + q)) = u;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();  // staged, and tensor memory read out before the next tile's products overwrite it
+      if (leader) {
+        tma_store_4d(&tdq, dst[0], 0, 0, h0, hb);
+        tma_store_4d(&tdk, dst[1], 0, 0, h0, hb);
+        tma_store_4d(&tdv, dst[2], 0, 0, h0, hb);
+        tma_store_commit();
+      }
+    } else {
+      // Gradients to global memory: key row r of dK and dV, query row r of dQ.
+      store_row_from_tmem<T, D>(tmem + L::cDV + lane_off, 1.f, mine ? dv + grow * D : nullptr);
+      store_row_from_tmem<T, D>(tmem + L::cDK + lane_off, scale, mine ? dk + grow * D : nullptr);
+      store_row_from_tmem<T, D>(tmem + L::cDQ + lane_off, scale, mine ? dq + grow * D : nullptr);
+      tc_fence_before();
+      __syncthreads();  // tensor memory read out before the next tile's products overwrite it
+    }
+  }
+  if (kStaged && leader) tma_store_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
 }  // namespace ebr

@@ -312,6 +312,42 @@ def train_segment_loss(net: LatentEnergyNet, z: Tensor, x: Tensor, labels: Tenso
     return stablemax_cross_entropy(net.decode(z), labels).mean()
 
 
+def sxm_explore_loss(net: LatentEnergyNet, z: Tensor, challengers: Tensor, x: Tensor, labels: Tensor, prefix: int,
+                     graded: int, alpha=None, sigma: Optional[float] = None) -> tuple[Tensor, Tensor, Tensor]:  # fmt: skip
+    """Forward SXM for one training segment (the algorithm of the reference's ``InnerNetwork.explore``,
+    ``models/energy.py:669-733``): K candidate trajectories per input -- the input's own state ``z`` [B, L, C] and
+    ``challengers`` [K - 1, B, L, C] -- run the whole segment as one batch without a graph, with noise drawn once per
+    microstep; each input keeps the candidate whose decoded endpoint has the lowest stablemax cross entropy against
+    ``labels``; the winner's graded window is run again from its state at the window's start with the same noise and
+    ``create_graph=True`` (so only one trajectory per input is differentiated twice).
+
+    Returns (loss of the recomputed winners, their endpoints, the K - 1 losers' endpoints as the next challengers
+    [K - 1, B, L, C], best first). An input's candidates stay together in the batch, so the batch shards over ranks
+    by input."""
+    k, b = challengers.shape[0] + 1, z.shape[0]
+    sigma = net.shape.noise_scale if sigma is None else sigma
+    steps = prefix + graded
+    cand = torch.cat([z.detach(), challengers.reshape(-1, *z.shape[1:]).to(z.dtype)])
+    xk, lk = x.repeat(k, 1, 1), labels.repeat(k, 1)
+    noise = [torch.randn_like(cand) * sigma for _ in range(steps)] if sigma else None
+    with torch.no_grad():
+        zc, start = cand, cand
+        for t in range(steps):
+            if t == prefix:
+                start = zc
+            zc, _ = net.microstep(zc, xk, noise=None if noise is None else noise[t], alpha=alpha)
+        per_row = stablemax_cross_entropy(net.decode(zc), lk).mean(-1).view(k, b)
+        order = per_row.argsort(dim=0)  # best candidate first, per input
+    rows = torch.arange(b, device=z.device)
+    pick = lambda t: t.view(k, b, *t.shape[1:])[order[0], rows]  # noqa: E731
+    zw = pick(start)
+    for t in range(prefix, steps):
+        zw, _ = net.microstep(zw, x, graded=True, noise=None if noise is None else pick(noise[t]), alpha=alpha)
+    loss = stablemax_cross_entropy(net.decode(zw), labels).mean()
+    losers = zc.view(k, b, *z.shape[1:])[order[1:], rows.unsqueeze(0)]
+    return loss, zw.detach(), losers
+
+
 __all__ = [
     "LatentEnergyNet",
     "NetShape",
@@ -321,5 +357,6 @@ __all__ = [
     "lowest_energy_pick",
     "rope_tables",
     "stablemax_cross_entropy",
+    "sxm_explore_loss",
     "train_segment_loss",
 ]

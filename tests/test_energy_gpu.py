@@ -255,3 +255,44 @@ def test_second_order_self_test(dtype):
     rel = lambda a, r: float((a - r).abs().max() / r.abs().max().clamp_min(1e-12))
     assert rel(fg, rg) < 5e-2 and rel(fhz, rhz) < 5e-2
     assert max(rel(a, r) for a, r in zip(fht, rht)) < 5e-2
+
+
+def test_sxm_explore_keeps_each_inputs_best_candidate():
+    """Forward SXM (models/energy.py:669-733): K candidates per input run one segment without a graph; the winner is
+    each input's candidate with the lowest stablemax cross entropy, recomputed with a graph (its endpoint equals the
+    no-graph one within the bf16 network's noise), the losers come back best first, and the loss reaches every
+    parameter through the double backward."""
+    from ebr_b200.energy import LatentEnergyNet, NetShape, stablemax_cross_entropy, sxm_explore_loss
+
+    net = LatentEnergyNet(NetShape(board=(10, 10), vocab=2, layers=2)).cuda()
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    b, k = 6, 4
+    tok = torch.randint(0, 2, (b, 100), generator=gen, device="cuda")
+    labels = torch.randint(0, 2, (b, 100), generator=gen, device="cuda")
+    x = net.embed(tok)
+    z = net.fresh_states(b, gen)
+    ch = torch.stack([net.fresh_states(b, gen) for _ in range(k - 1)])
+    loss, zw, losers = sxm_explore_loss(net, z, ch, x, labels, prefix=2, graded=2, sigma=0.0)
+    # each candidate alone, no graph, no noise
+    cands = [z] + list(ch)
+    ends, ce = [], []
+    with torch.no_grad():
+        for c in cands:
+            zc = c
+            for _ in range(4):
+                zc, _ = net.microstep(zc, x, sigma=0.0)
+            ends.append(zc)
+            ce.append(stablemax_cross_entropy(net.decode(zc), labels).mean(-1))
+    ce = torch.stack(ce)  # [k, b]
+    best = ce.argmin(0)
+    for i in range(b):
+        w = int(best[i])
+        assert _normrel(zw[i].float().cpu().numpy(), ends[w][i].float().cpu().numpy()) < 2e-2, i
+        got = [int(torch.stack([((losers[j][i].float() - e[i].float()).norm()) for e in ends]).argmin())
+               for j in range(k - 1)]
+        assert w not in got and sorted(got) == sorted(set(range(k)) - {w}), (i, w, got)
+        assert [float(ce[g, i]) for g in got] == sorted(float(ce[g, i]) for g in got), (i, got)
+    loss.backward()
+    for n, p in net.named_parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all(), n
+    assert net.blocks[0].log_temp.grad.abs().sum() > 0
