@@ -529,34 +529,38 @@ int launch_tc_bob_split(int device, int dtype, int64_t B, int64_t H, int64_t N, 
 }
 
 template <typename T>
-int launch_tc_bob_single(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
-                         const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
-                         const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
-                         void* hq, void* hk, void* hv, void* hdo, cudaStream_t st) {
-  using L = BobSingleLayout;
+int launch_tc_bob_short(int device, int dtype, int64_t B, int64_t H, int64_t N, double scale, const ebr_operand* q,
+                        const ebr_operand* k, const ebr_operand* v, const void* o, const void* lse,
+                        const ebr_operand* dout, const ebr_operand* gq, const ebr_operand* gk, const ebr_operand* gv,
+                        void* hq, void* hk, void* hv, void* hdo, cudaStream_t st) {
+  using L = BobShortLayout;
   constexpr int D = 64;
-  CUtensorMap tq, tk, tv, tdo, tgq, tgk, tgv;
+  const ShortPlan plan = short_plan(B, H, N, {q, k, v, dout, gq, gk, gv});
+  CUtensorMap tq, tk, tv, tdo, tgq, tgk, tgv, thq, thk, thv, thdo;
   uint32_t zero_mask = 0;
   const ebr_operand* gs[3] = {gq, gk, gv};
   CUtensorMap* gm[3] = {&tgq, &tgk, &tgv};
-  if (make_tile_map(&tq, q, dtype, B, H, N, D) || make_tile_map(&tk, k, dtype, B, H, N, D) ||
-      make_tile_map(&tv, v, dtype, B, H, N, D) || make_tile_map(&tdo, dout, dtype, B, H, N, D))
+  if (make_short_map(&tq, q, dtype, plan, D) || make_short_map(&tk, k, dtype, plan, D) ||
+      make_short_map(&tv, v, dtype, plan, D) || make_short_map(&tdo, dout, dtype, plan, D) ||
+      make_short_out_map(&thq, hq, dtype, plan, H, D) || make_short_out_map(&thk, hk, dtype, plan, H, D) ||
+      make_short_out_map(&thv, hv, dtype, plan, H, D) || make_short_out_map(&thdo, hdo, dtype, plan, H, D))
     return kNoTensorMap;
   for (int i = 0; i < 3; ++i) {
     if (!gs[i] || !gs[i]->data) {
       zero_mask |= 1u << i;
       *gm[i] = tq;  // never read
-    } else if (make_tile_map(gm[i], gs[i], dtype, B, H, N, D)) {
+    } else if (make_short_map(gm[i], gs[i], dtype, plan, D)) {
       return kNoTensorMap;
     }
   }
-  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bob_single_kernel<T>), device, L::kSmem, L::kTmemCols);
+  int s = prepare_tc_kernel(reinterpret_cast<const void*>(tc_bob_short_kernel<T>), device, L::kSmem, L::kTmemCols);
   if (s) return s;
-  tc_bob_single_kernel<T><<<static_cast<unsigned>(B * H), 128, L::kSmem, st>>>(
-      tq, tk, tv, tdo, tgq, tgk, tgv, static_cast<const T*>(o), static_cast<const float*>(lse), static_cast<T*>(hq),
-      static_cast<T*>(hk), static_cast<T*>(hv), static_cast<T*>(hdo), static_cast<int>(H), static_cast<int>(N),
-      static_cast<float>(scale), zero_mask);
-  return check_launch("tc_bob_single_kernel");
+  const int cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(plan.geo.tiles < cap ? plan.geo.tiles : cap);
+  tc_bob_short_kernel<T><<<grid, 128, L::kSmem, st>>>(tq, tk, tv, tdo, tgq, tgk, tgv, thq, thk, thv, thdo,
+                                                      static_cast<const T*>(o), static_cast<const float*>(lse),
+                                                      plan.geo, static_cast<float>(scale), zero_mask);
+  return check_launch("tc_bob_short_kernel");
 }
 
 // Built-in row scratch of ebr_attn_bwd_noalloc (see include/ebr_attn.h). Host code must not pass the symbol itself
@@ -751,10 +755,10 @@ int ebr_attn_bwd_bwd(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, doub
   const bool outs_ok = aligned16(o) && aligned16(hq) && aligned16(hk) && aligned16(hv) && aligned16(hdout);
   if (N <= kTile && D == 64 && outs_ok && tc_eligible(dtype, D, {q, k, v, dout, gq, gk, gv}, B, H, N)) {
     if (dtype == EBR_BFLOAT16)
-      s = launch_tc_bob_single<__nv_bfloat16>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq,
+      s = launch_tc_bob_short<__nv_bfloat16>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq,
                                               hk, hv, hdout, st);
     else
-      s = launch_tc_bob_single<__half>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv,
+      s = launch_tc_bob_short<__half>(device, dtype, B, H, N, scale, q, k, v, o, lse, dout, gq, gk, gv, hq, hk, hv,
                                        hdout, st);
     if (s != kNoTensorMap) return s;
   }

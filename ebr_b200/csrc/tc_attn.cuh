@@ -670,218 +670,4 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// ================================================================================================ double backward, N <= 128
-
-struct BobSingleLayout {  // D = 64
-  static constexpr uint32_t kOp = kHalfBytes;
-  static constexpr uint32_t kQ = 0, kK = kQ + kOp, kV = kK + kOp, kDO = kV + kOp, kGQ = kDO + kOp,
-                            kGK = kGQ + kOp, kGV = kGK + kOp;
-  static constexpr uint32_t kGS = kGV + kOp, kDS = kGS + 2 * kHalfBytes, kA = kDS + 2 * kHalfBytes;
-  static constexpr uint32_t kBytes = kA + 2 * kHalfBytes;  // 7 * 16 KiB + 3 * 32 KiB = 208 KiB
-  static constexpr uint32_t kSmem = kBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;
-  // Phase 1: S [0,128), dP [128,256), G [256,384), R [384,512). Phase 2: packed 16-bit P in [0,64) (written over S
-  // after it is read), hQ [256,320), hdO [320,384), hK [384,448), hV [448,512).
-  static constexpr uint32_t cS = 0, cDP = 128, cG = 256, cR = 384;
-  static constexpr uint32_t cP16 = 0, cHQ = 256, cHDO = 320, cHK = 384, cHV = 448;
-};
-
-// One CTA per (b, h) slice with N <= 128, D = 64: the closed form of reference.py:61-91 in one pass.
-//   S = Q K^T, dP = dO V^T, G = gQ K^T + Q gK^T (scaled), R = dO gV^T           (4 tcgen05 products into TMEM)
-//   per query row: D, e = sum P G, t = sum P gp, then P, dS, A = P (G - e), gS = P (gp - t)
-//   hQ = scale (gS K + dS gK), hdO = A V + P gV, hK = scale (gS^T Q + dS^T gQ), hV = A^T dO   (7 products)
-// gS, dS and A go to shared memory (K-major for hQ / hdO, MN-major for hK / hV); P goes to TMEM for P gV.
-// The reference's Triton kernels do this as a SINGLE column pass (triton_kernels.py:448-551, :878-909).
-template <typename T>
-__global__ void __launch_bounds__(128, 1)
-    tc_bob_single_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                         const __grid_constant__ CUtensorMap tgq, const __grid_constant__ CUtensorMap tgk,
-                         const __grid_constant__ CUtensorMap tgv, const T* __restrict__ o,
-                         const float* __restrict__ lse, T* __restrict__ hq, T* __restrict__ hk,
-                         T* __restrict__ hv, T* __restrict__ hdo, int H, int N, float scale, uint32_t zero_mask) {
-  constexpr int D = 64;
-  using L = BobSingleLayout;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  unsigned char* sQ = smem + L::kQ;
-  unsigned char* sK = smem + L::kK;
-  unsigned char* sV = smem + L::kV;
-  unsigned char* sDO = smem + L::kDO;
-  unsigned char* sGQ = smem + L::kGQ;
-  unsigned char* sGK = smem + L::kGK;
-  unsigned char* sGV = smem + L::kGV;
-  unsigned char* sGS = smem + L::kGS;
-  unsigned char* sDS = smem + L::kDS;
-  unsigned char* sA = smem + L::kA;
-  __shared__ uint64_t bar_load, bar_mma;
-  __shared__ uint32_t tmem_slot;
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / H, h = bh - (bh / H) * H;
-  constexpr bool kB = is_bf16<T>();
-  constexpr uint32_t kIdNN = idesc_f16(kB, 0, 0, 128, 128);
-  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
-  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);
-
-  if (tid == 0) {
-    mbar_init(&bar_load, 1);
-    mbar_init(&bar_mma, 1);
-    fence_barrier_init();
-    // A zero cotangent (bit 0 gq, 1 gk, 2 gv of zero_mask) is not loaded; its tile is cleared below.
-    mbar_arrive_expect_tx(&bar_load, (7u - __popc(zero_mask & 7u)) * L::kOp);
-    tma_load_4d(sQ, &tq, &bar_load, 0, 0, h, b);
-    tma_load_4d(sK, &tk, &bar_load, 0, 0, h, b);
-    tma_load_4d(sV, &tv, &bar_load, 0, 0, h, b);
-    tma_load_4d(sDO, &tdo, &bar_load, 0, 0, h, b);
-    if (!(zero_mask & 1u)) tma_load_4d(sGQ, &tgq, &bar_load, 0, 0, h, b);
-    if (!(zero_mask & 2u)) tma_load_4d(sGK, &tgk, &bar_load, 0, 0, h, b);
-    if (!(zero_mask & 4u)) tma_load_4d(sGV, &tgv, &bar_load, 0, 0, h, b);
-  }
-  if (warp == 0) {
-    tmem_alloc(&tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-#pragma unroll
-  for (int z = 0; z < 3; ++z) {
-    if (zero_mask & (1u << z)) {
-      uint4* t = reinterpret_cast<uint4*>(z == 0 ? sGQ : (z == 1 ? sGK : sGV));
-      for (int i = tid; i < static_cast<int>(L::kOp / 16); i += 128) t[i] = make_uint4(0, 0, 0, 0);
-    }
-  }
-  fence_proxy_async_smem();
-  const int row = tid;
-  const bool row_ok = row < N;
-  const int64_t grow = static_cast<int64_t>(bh) * N + row;
-  const float Li = row_ok ? lse[grow] : 0.f;
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-  bool fail = !mbar_wait(&bar_load, 0, 301);
-  if (!__syncthreads_or(fail)) {
-    if (tid == 0) {
-      tc_fence_after();
-      mma_rows_x_rows<D>(tmem + L::cS, sQ, sK, kIdNN, false);
-      mma_rows_x_rows<D>(tmem + L::cDP, sDO, sV, kIdNN, false);
-      mma_rows_x_rows<D>(tmem + L::cG, sGQ, sK, kIdNN, false);
-      mma_rows_x_rows<D>(tmem + L::cG, sQ, sGK, kIdNN, true);
-      mma_rows_x_rows<D>(tmem + L::cR, sDO, sGV, kIdNN, false);
-      mma_commit(&bar_mma);
-    }
-    float Di = 0.f;
-    if (row_ok) {
-      const T* orow = o + grow * D;
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        float x[8], y[8];
-        ld_row8<T>(sDO, row, c, x);
-        ld_global8<T>(orow + 8 * c, y);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) Di += x[i] * y[i];
-      }
-    }
-    fail |= !mbar_wait(&bar_mma, 0, 302);
-    if (!__syncthreads_or(fail)) {
-      tc_fence_after();
-      // Pass 1: e = sum P g, and sum P gp = sum dS g - e sum P dP + sum P r.
-      float e_ = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kTile; c += 16) {
-        uint32_t rs[16], rp[16], rg[16], rr[16];
-        tmem_ld16(tmem + L::cS + lane_off + c, rs);
-        tmem_ld16(tmem + L::cDP + lane_off + c, rp);
-        tmem_ld16(tmem + L::cG + lane_off + c, rg);
-        tmem_ld16(tmem + L::cR + lane_off + c, rr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const bool ok = row_ok && (c + u < N);
-          const float p = ok ? exp_nat(fmaf(__uint_as_float(rs[u]), scale, -Li)) : 0.f;
-          const float g = __uint_as_float(rg[u]) * scale;
-          const float dp = __uint_as_float(rp[u]);
-          e_ += p * g;
-          c1 += p * (dp - Di) * g;
-          c2 += p * dp;
-          c3 += p * __uint_as_float(rr[u]);
-        }
-      }
-      const float t_ = c1 - e_ * c2 + c3;
-      // Pass 2: the derived tiles. P (16-bit) is packed into TMEM columns [c/2, c/2 + 16) over S columns this thread
-      // has already read.
-#pragma unroll 1
-      for (int c = 0; c < kTile; c += 32) {
-        uint32_t rs[32], rp[32], rg[32], rr[32];
-        tmem_ld32(tmem + L::cS + lane_off + c, rs);
-        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
-        tmem_ld32(tmem + L::cG + lane_off + c, rg);
-        tmem_ld32(tmem + L::cR + lane_off + c, rr);
-        tmem_wait_ld();
-        uint32_t pk_p[16], pk_gs[16], pk_ds[16], pk_a[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p[2], gs[2], ds[2], a[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const bool ok = row_ok && (c + e + u < N);
-            const float pp = ok ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
-            const float g = __uint_as_float(rg[e + u]) * scale;
-            const float dp = __uint_as_float(rp[e + u]);
-            const float gp = (dp - Di) * g - e_ * dp + __uint_as_float(rr[e + u]);
-            p[u] = pp;
-            ds[u] = pp * (dp - Di);
-            a[u] = pp * (g - e_);
-            gs[u] = pp * (gp - t_);
-          }
-          pk_p[e >> 1] = pack2<T>(p[0], p[1]);
-          pk_gs[e >> 1] = pack2<T>(gs[0], gs[1]);
-          pk_ds[e >> 1] = pack2<T>(ds[0], ds[1]);
-          pk_a[e >> 1] = pack2<T>(a[0], a[1]);
-        }
-        st_row32(sGS, row, c, pk_gs);
-        st_row32(sDS, row, c, pk_ds);
-        st_row32(sA, row, c, pk_a);
-        uint32_t lo[8], hi[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          lo[i] = pk_p[i];
-          hi[i] = pk_p[8 + i];
-        }
-        tmem_st8(tmem + L::cP16 + lane_off + (c >> 1), lo);
-        tmem_st8(tmem + L::cP16 + lane_off + (c >> 1) + 8, hi);
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        mma_tile_x_rows(tmem + L::cHQ, sGS, sK, kIdKM, false);
-        mma_tile_x_rows(tmem + L::cHQ, sDS, sGK, kIdKM, true);
-        mma_tile_x_rows(tmem + L::cHDO, sA, sV, kIdKM, false);
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_ts(tmem + L::cHDO, tmem + L::cP16 + kk * 8, desc_mnmajor(sGV, kk), kIdKM, 1u);
-        mma_tileT_x_rows(tmem + L::cHK, sGS, sQ, kIdMM, false);
-        mma_tileT_x_rows(tmem + L::cHK, sDS, sGQ, kIdMM, true);
-        mma_tileT_x_rows(tmem + L::cHV, sA, sDO, kIdMM, false);
-        mma_commit(&bar_mma);
-      }
-      fail |= !mbar_wait(&bar_mma, 1, 303);
-      if (!__syncthreads_or(fail)) {
-        tc_fence_after();
-        T* none = nullptr;
-        store_row_from_tmem<T, D>(tmem + L::cHQ + lane_off, scale, row_ok ? hq + grow * D : none);
-        store_row_from_tmem<T, D>(tmem + L::cHDO + lane_off, 1.f, row_ok ? hdo + grow * D : none);
-        store_row_from_tmem<T, D>(tmem + L::cHK + lane_off, scale, row_ok ? hk + grow * D : none);
-        store_row_from_tmem<T, D>(tmem + L::cHV + lane_off, 1.f, row_ok ? hv + grow * D : none);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-}
-
 }  // namespace ebr

@@ -611,4 +611,318 @@ __global__ void __launch_bounds__(128, D == 64 ? 2 : 1)
   if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
 }
 
+// ================================================================================================ double backward
+
+struct BobShortLayout {  // D = 64
+  static constexpr uint32_t kOp = kHalfBytes;
+  static constexpr uint32_t kQ = 0, kK = kOp, kV = 2 * kOp, kDO = 3 * kOp, kGQ = 4 * kOp, kGK = 5 * kOp,
+                            kGV = 6 * kOp;
+  static constexpr uint32_t kGS = 7 * kOp, kDS = kGS + 2 * kHalfBytes, kA = kDS + 2 * kHalfBytes;
+  static constexpr uint32_t kBytes = kA + 2 * kHalfBytes;  // 7 * 16 KiB + 3 * 32 KiB = 208 KiB
+  static constexpr uint32_t kSmem = kBytes + 64;           // barriers after the tiles; no static shared memory
+  static constexpr uint32_t kTmemCols = 512;
+  // Scores: S [0,128), dP [128,256), G [256,384), R [384,512). Outputs: packed 16-bit P in [0,64) (over S, once read),
+  // hQ [256,320), hdO [320,384), hK [384,448), hV [448,512).
+  static constexpr uint32_t cS = 0, cDP = 128, cG = 256, cR = 384;
+  static constexpr uint32_t cP16 = 0, cHQ = 256, cHDO = 320, cHK = 384, cHV = 448;
+};
+
+// Double backward for N <= 128 at D = 64 (packed tiles as in the forward), persistent, one CTA per SM (its four
+// score products fill the SM's tensor memory). Per tile, the closed form of reference.py:61-91:
+//   S = Q K^T, dP = dO V^T, G = scale (gQ K^T + Q gK^T), R = dO gV^T           (tcgen05, tensor memory)
+//   per query row (masked to its slice): D = <dO, O>, e = sum P G, t = sum P gp with gp = (dP - D) G - e dP + R;
+//   then P, dS = P (dP - D), A = P (G - e), gS = P (gp - t) rounded to the input type (gS, dS, A to shared memory,
+//   P to tensor memory);
+//   hQ = scale (gS K + dS gK), hdO = A V + P gV, hK = scale (gS^T Q + dS^T gQ), hV = A^T dO
+// Once the second products are done the next tile's inputs are loaded, while the outputs are rounded into the spent
+// gS and dS tiles and leave through TMA stores. A zero cotangent (bit 0 gq, 1 gk, 2 gv of zero_mask) is never
+// loaded: its tile stays cleared. The reference's Triton kernels do this as a SINGLE column pass
+// (models/fused_attn/triton_kernels.py:448-551, :878-909).
+template <typename T>
+__global__ void __launch_bounds__(128, 1)
+    tc_bob_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                        const __grid_constant__ CUtensorMap tgq, const __grid_constant__ CUtensorMap tgk,
+                        const __grid_constant__ CUtensorMap tgv, const __grid_constant__ CUtensorMap thq,
+                        const __grid_constant__ CUtensorMap thk, const __grid_constant__ CUtensorMap thv,
+                        const __grid_constant__ CUtensorMap thdo, const T* __restrict__ o,
+                        const float* __restrict__ lse, const ShortGeom geo, float scale, uint32_t zero_mask) {
+  constexpr int D = 64;
+  using L = BobShortLayout;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* sQ = smem + L::kQ;
+  unsigned char* sK = smem + L::kK;
+  unsigned char* sV = smem + L::kV;
+  unsigned char* sDO = smem + L::kDO;
+  unsigned char* sGQ = smem + L::kGQ;
+  unsigned char* sGK = smem + L::kGK;
+  unsigned char* sGV = smem + L::kGV;
+  unsigned char* sGS = smem + L::kGS;
+  unsigned char* sDS = smem + L::kDS;
+  unsigned char* sA = smem + L::kA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBytes);
+  uint64_t& in_full = bars[0];
+  uint64_t& s_full = bars[1];
+  uint64_t& g_full = bars[2];
+  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(smem + L::kBytes + 24);
+  int& abort_flag = *reinterpret_cast<int*>(smem + L::kBytes + 28);
+  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need a 1024-byte-aligned base
+    if (threadIdx.x == 0) atomicExch(&g_device_error, 470);
+    return;
+  }
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int N = geo.N, rows = geo.per * geo.N;
+  const int kc = (rows + 31) & ~31;  // key columns of the score products (and K of the key-side sums)
+  const int kr = (rows + 15) & ~15;  // query rows reduced over (K of hK, hV)
+  constexpr bool kB = is_bf16<T>();
+  const uint32_t id_nn = idesc_f16(kB, 0, 0, 128, kc);
+  constexpr uint32_t kIdKM = idesc_f16(kB, 0, 1, 128, D);
+  constexpr uint32_t kIdMM = idesc_f16(kB, 1, 1, 128, D);
+  const int n_local = geo.tiles > static_cast<int>(blockIdx.x)
+                          ? (geo.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                          : 0;
+  const uint32_t box_bytes = 128u * static_cast<uint32_t>(rows);
+  const uint32_t n_loaded = 7u - static_cast<uint32_t>(__popc(zero_mask & 7u));
+
+  for (uint32_t i = tid * 16u; i < L::kBytes; i += 128u * 16u)
+    *reinterpret_cast<uint4*>(smem + i) = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    mbar_init(&in_full, 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&g_full, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+  const bool leader = tid == 0;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const int r = tid;
+  const bool row_ok = r < rows;
+  const int j0_row = row_ok ? (r / N) * N : 0;
+  const int j1_row = row_ok ? j0_row + N : 0;
+
+  auto coords = [&](int li, int& hb, int& h0) {
+    short_tile_coords(geo, static_cast<int>(blockIdx.x) + li * static_cast<int>(gridDim.x), hb, h0);
+  };
+  auto load = [&](int li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    mbar_arrive_expect_tx(&in_full, n_loaded * box_bytes);
+    tma_load_4d(sQ, &tq, &in_full, 0, 0, h0, hb);
+    tma_load_4d(sK, &tk, &in_full, 0, 0, h0, hb);
+    tma_load_4d(sV, &tv, &in_full, 0, 0, h0, hb);
+    tma_load_4d(sDO, &tdo, &in_full, 0, 0, h0, hb);
+    if (!(zero_mask & 1u)) tma_load_4d(sGQ, &tgq, &in_full, 0, 0, h0, hb);
+    if (!(zero_mask & 2u)) tma_load_4d(sGK, &tgk, &in_full, 0, 0, h0, hb);
+    if (!(zero_mask & 4u)) tma_load_4d(sGV, &tgv, &in_full, 0, 0, h0, hb);
+  };
+  if (leader && n_local > 0) load(0);
+
+  bool ok = true;
+  for (int li = 0; li < n_local && ok; ++li) {
+    int hb, h0;
+    coords(li, hb, h0);
+    const uint32_t par = static_cast<uint32_t>(li) & 1u;
+    const bool mine = row_ok && h0 + r / N < geo.hs;
+    const int64_t grow = mine ? (static_cast<int64_t>(hb) * geo.hs + h0 + r / N) * N + (r - j0_row) : 0;
+    const float Li = mine ? lse[grow] : 0.f;
+    uint4 orow[D / 8];
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c)
+      orow[c] = mine ? *reinterpret_cast<const uint4*>(o + grow * D + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+    if (leader) {
+      ok = mbar_wait_or_abort(&in_full, par, 471, abort);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t acc = kk > 0 ? 1u : 0u;
+          mma_ss(tmem + L::cS, desc_kmajor(sQ, kk), desc_kmajor(sK, kk), id_nn, acc);
+          mma_ss(tmem + L::cDP, desc_kmajor(sDO, kk), desc_kmajor(sV, kk), id_nn, acc);
+          mma_ss(tmem + L::cG, desc_kmajor(sGQ, kk), desc_kmajor(sK, kk), id_nn, acc);
+          mma_ss(tmem + L::cR, desc_kmajor(sDO, kk), desc_kmajor(sGV, kk), id_nn, acc);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + L::cG, desc_kmajor(sQ, kk), desc_kmajor(sGK, kk), id_nn, 1u);
+        mma_commit(&s_full);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&in_full, par, 472, abort));
+    if (!ok) break;
+    float Di = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      float x[8];
+      ld_row8<T>(sDO, r, c, x);
+      const uint32_t w[4] = {orow[c].x, orow[c].y, orow[c].z, orow[c].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) Di += x[2 * q] * unpack_lo<T>(w[q]) + x[2 * q + 1] * unpack_hi<T>(w[q]);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&s_full, par, 473, abort));
+    if (!ok) break;
+    if (li > 0) {  // the previous tile's output stores must have read the gS and dS tiles
+      if (leader) tma_store_wait_read();
+      __syncthreads();
+    }
+    tc_fence_after();
+    int j0, j1;  // re-read per tile through an opaque move: keeps per-column masks from being hoisted and held
+    asm volatile("mov.b32 %0, %1;" : "=r"(j0) : "r"(j0_row));
+    asm volatile("mov.b32 %0, %1;" : "=r"(j1) : "r"(j1_row));
+    // Pass 1: e = sum P G, and sum P gp = sum dS G - e sum P dP + sum P R.
+    float e_ = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      if (c >= kc) continue;
+      uint32_t rs[32], rp[32], rg[32], rr[32];
+      tmem_ld32(tmem + L::cS + lane_off + c, rs);
+      tmem_ld32(tmem + L::cDP + lane_off + c, rp);
+      tmem_ld32(tmem + L::cG + lane_off + c, rg);
+      tmem_ld32(tmem + L::cR + lane_off + c, rr);
+      tmem_wait_ld_regs(rs);
+      tmem_wait_ld_regs(rp);
+      tmem_wait_ld_regs(rg);
+      tmem_wait_ld_regs(rr);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const bool in = c + u >= j0 && c + u < j1;
+        const float p = in ? exp_nat(fmaf(__uint_as_float(rs[u]), scale, -Li)) : 0.f;
+        const float g = __uint_as_float(rg[u]) * scale;
+        const float dp = __uint_as_float(rp[u]);
+        e_ += p * g;
+        c1 += p * (dp - Di) * g;
+        c2 += p * dp;
+        c3 += p * __uint_as_float(rr[u]);
+      }
+    }
+    const float t_ = c1 - e_ * c2 + c3;
+    // Pass 2: the derived tiles (every row and column written: zeros where masked); P packed to 16 bits into
+    // tensor-memory columns [c / 2, c / 2 + 16), over S columns this thread has already read.
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t pk_p[16], pk_gs[16], pk_ds[16], pk_a[16];
+      if (c < kc) {
+        uint32_t rs[32], rp[32], rg[32], rr[32];
+        tmem_ld32(tmem + L::cS + lane_off + c, rs);
+        tmem_ld32(tmem + L::cDP + lane_off + c, rp);
+        tmem_ld32(tmem + L::cG + lane_off + c, rg);
+        tmem_ld32(tmem + L::cR + lane_off + c, rr);
+        tmem_wait_ld_regs(rs);
+        tmem_wait_ld_regs(rp);
+        tmem_wait_ld_regs(rg);
+        tmem_wait_ld_regs(rr);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], gs[2], ds[2], a[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool in = c + e + u >= j0 && c + e + u < j1;
+            const float pp = in ? exp_nat(fmaf(__uint_as_float(rs[e + u]), scale, -Li)) : 0.f;
+            const float g = __uint_as_float(rg[e + u]) * scale;
+            const float dp = __uint_as_float(rp[e + u]);
+            const float gp = (dp - Di) * g - e_ * dp + __uint_as_float(rr[e + u]);
+            pv[u] = pp;
+            ds[u] = pp * (dp - Di);
+            a[u] = pp * (g - e_);
+            gs[u] = pp * (gp - t_);
+          }
+          pk_p[e >> 1] = pack2<T>(pv[0], pv[1]);
+          pk_gs[e >> 1] = pack2<T>(gs[0], gs[1]);
+          pk_ds[e >> 1] = pack2<T>(ds[0], ds[1]);
+          pk_a[e >> 1] = pack2<T>(a[0], a[1]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk_p[e] = pk_gs[e] = pk_ds[e] = pk_a[e] = 0u;
+      }
+      st_row32(sGS, r, c, pk_gs);
+      st_row32(sDS, r, c, pk_ds);
+      st_row32(sA, r, c, pk_a);
+      uint32_t lo[8], hi[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        lo[i] = pk_p[i];
+        hi[i] = pk_p[8 + i];
+      }
+      tmem_st8(tmem + L::cP16 + lane_off + (c >> 1), lo);
+      tmem_st8(tmem + L::cP16 + lane_off + (c >> 1) + 8, hi);
+    }
+    tmem_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (leader) {
+      tc_fence_after();
+      for (int kk = 0; kk < kc / 16; ++kk) {  // K = keys
+        const uint32_t acc = kk > 0 ? 1u : 0u;
+        mma_ss(tmem + L::cHQ, desc_kmajor(sGS, kk), desc_mnmajor(sK, kk), kIdKM, acc);
+        mma_ss(tmem + L::cHQ, desc_kmajor(sDS, kk), desc_mnmajor(sGK, kk), kIdKM, 1u);
+        mma_ss(tmem + L::cHDO, desc_kmajor(sA, kk), desc_mnmajor(sV, kk), kIdKM, acc);
+        mma_ts(tmem + L::cHDO, tmem + L::cP16 + kk * 8, desc_mnmajor(sGV, kk), kIdKM, 1u);
+      }
+      for (int kk = 0; kk < kr / 16; ++kk) {  // K = queries
+        const uint32_t acc = kk > 0 ? 1u : 0u;
+        mma_ss(tmem + L::cHK, desc_mnmajor(sGS, kk), desc_mnmajor(sQ, kk), kIdMM, acc);
+        mma_ss(tmem + L::cHK, desc_mnmajor(sDS, kk), desc_mnmajor(sGQ, kk), kIdMM, 1u);
+        mma_ss(tmem + L::cHV, desc_mnmajor(sA, kk), desc_mnmajor(sDO, kk), kIdMM, acc);
+      }
+      mma_commit(&g_full);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_or_abort(&g_full, par, 474, abort));
+    if (!ok) break;
+    tc_fence_after();
+    if (leader && li + 1 < n_local) load(li + 1);  // every input tile is spent
+    // Outputs rounded into the spent gS (hQ, hdO) and dS (hK, hV) tiles, rows >= `rows` as zeros; TMA stores.
+    int rt;  // the row, re-read here so the staging addresses are formed here
+    asm volatile("mov.b32 %0, %1;" : "=r"(rt) : "r"(r));
+    unsigned char* const dst[4] = {sGS, sGS + kHalfBytes, sDS, sDS + kHalfBytes};
+    const uint32_t col[4] = {L::cHQ, L::cHDO, L::cHK, L::cHV};
+    const float mul[4] = {scale, 1.f, scale, 1.f};
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + col[g] + lane_off + c, v);
+        tmem_wait_ld_regs(v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          if (row_ok) {
+            u.x = pack2<T>(__uint_as_float(v[8 * q + 0]) * mul[g], __uint_as_float(v[8 * q + 1]) * mul[g]);
+            u.y = pack2<T>(__uint_as_float(v[8 * q + 2]) * mul[g], __uint_as_float(v[8 * q + 3]) * mul[g]);
+            u.z = pack2<T>(__uint_as_float(v[8 * q + 4]) * mul[g], __uint_as_float(v[8 * q + 5]) * mul[g]);
+            u.w = pack2<T>(__uint_as_float(v[8 * q + 6]) * mul[g], __uint_as_float(v[8 * q + 7]) * mul[g]);
+          }
+          *reinterpret_cast<uint4*>(dst[g] + sw128_off(rt, (c >> 3) + q)) = u;
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();  // staged, and tensor memory read out before the next tile's products overwrite it
+    if (leader) {
+      tma_store_4d(&thq, dst[0], 0, 0, h0, hb);
+      tma_store_4d(&thdo, dst[1], 0, 0, h0, hb);
+      tma_store_4d(&thk, dst[2], 0, 0, h0, hb);
+      tma_store_4d(&thv, dst[3], 0, 0, h0, hb);
+      tma_store_commit();
+    }
+  }
+  if (leader) tma_store_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
+}
+
 }  // namespace ebr
