@@ -567,6 +567,8 @@ def run_train(args) -> None:
 
     def step():
         nonlocal challengers
+        s0 = torch.cuda.Event(enable_timing=True)
+        s0.record()
         x = model.embed(tok)
         if sxm:
             loss, _, challengers = sxm_explore_loss(model, z0, challengers, x, labels, TRAIN_MICROSTEPS - TRAIN_GRADED,
@@ -581,7 +583,7 @@ def run_train(args) -> None:
         buckets.finish()
         e1.record()
         opt.step()
-        return loss, (e0, e1)
+        return loss, (s0, e0, e1)
 
     for _ in range(args.warmup):
         step()
@@ -600,7 +602,11 @@ def run_train(args) -> None:
         b.record()
         torch.cuda.synchronize()
     ms = runtime.max_over_ranks(a.elapsed_time(b))
-    tail_ms = runtime.max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in marks))
+    tail_ms = runtime.max_over_ranks(statistics.median(e0.elapsed_time(e1) for _, e0, e1 in marks))
+    # This rank's own work per step (forward segment + backward, up to the wait for the collectives): the spread of
+    # it over ranks is what the others wait for in finish().
+    own_ms = statistics.median(s0.elapsed_time(e0) for s0, e0, _ in marks)
+    own_max, own_min = runtime.max_over_ranks(own_ms), -runtime.max_over_ranks(-own_ms)
     ops = timer.summary()
     runtime.check_param_sync(model, rtol=1e-9)
     # The gradient all-reduce alone, for the record: one flat bucket of every gradient, CUDA events (max over ranks).
@@ -646,7 +652,8 @@ def run_train(args) -> None:
                                       "with the outer backward"},  # fmt: skip
             "allreduce": {"params": nparam, "bytes": 4 * nparam, "buckets": len(buckets.buckets),
                           "flat_allreduce_ms": None if ar_ms is None else round(ar_ms, 3),
-                          "exposed_after_backward_ms": round(tail_ms, 3)},  # fmt: skip
+                          "exposed_after_backward_ms": round(tail_ms, 3),
+                          "rank_compute_ms_min": round(own_min, 3), "rank_compute_ms_max": round(own_max, 3)},  # fmt: skip
             "loss": float(loss.item()),
             "gpu_launches": int(_native.launch_count() - launches0),
             "attention_ms": {n: round(v["ms"], 3) for n, v in ops.items()},

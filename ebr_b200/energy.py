@@ -335,14 +335,15 @@ def sxm_explore_loss(net: LatentEnergyNet, z: Tensor, challengers: Tensor, x: Te
         for t in range(steps):
             if t == prefix:
                 start = zc
-            zc, _ = net.microstep(zc, xk, noise=None if noise is None else noise[t], alpha=alpha)
+            zc, _ = net.microstep(zc, xk, noise=None if noise is None else noise[t], sigma=0.0, alpha=alpha)
         per_row = stablemax_cross_entropy(net.decode(zc), lk).mean(-1).view(k, b)
         order = per_row.argsort(dim=0)  # best candidate first, per input
     rows = torch.arange(b, device=z.device)
     pick = lambda t: t.view(k, b, *t.shape[1:])[order[0], rows]  # noqa: E731
     zw = pick(start)
     for t in range(prefix, steps):
-        zw, _ = net.microstep(zw, x, graded=True, noise=None if noise is None else pick(noise[t]), alpha=alpha)
+        zw, _ = net.microstep(zw, x, graded=True, noise=None if noise is None else pick(noise[t]), sigma=0.0,
+                              alpha=alpha)  # fmt: skip
     loss = stablemax_cross_entropy(net.decode(zw), labels).mean()
     losers = zc.view(k, b, *z.shape[1:])[order[1:], rows.unsqueeze(0)]
     return loss, zw.detach(), losers
