@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: latent-descent sample-steps/s of the EBR energy network at L = 900.
+"""Benchmark: latent-descent sample-steps/s of the EBR energy network on 30 x 30 maze boards (L = 900).
 
 Workload (per rank, weak scaling): 128 synthetic 30 x 30 maze inputs x 5 samples = 640 latent rows, L = 900, the
 4-layer / hidden 512 / 8 x 64 / SwiGLU 4x energy network in bf16 with random-init weights. One step = one segment of
@@ -9,11 +9,13 @@ Workload (per rank, weak scaling): 128 synthetic 30 x 30 maze inputs x 5 samples
 Output (rank 0, one JSON line): ``value`` = sample-steps/s over all ranks with inputs resident on the device;
 ``e2e`` = the same through the public API with the puzzles copied from pinned host memory and the energies / picks
 copied back inside the timed region; ``roofline`` = the dominant attention op's achieved TFLOP/s (algorithmic FLOPs
-per call / CUDA-event duration) against the measured bf16 peak; ``cpu_baseline`` = the reference's CPU path (oracle
-attention, torch CPU for the rest) timed on a bounded sample on this host.
+per call / CUDA-event duration) against the measured bf16 peak; ``cpu_baseline`` = the reference's own eager CPU path
+(its models/energy.py with math attention, installed under baseline/_ref; this repository's CPU port when it is
+absent) timed on a bounded sample on this host.
 
 ``--impl reference`` times only that CPU path (rank 0) on the same config and prints its own line.
-``--mode sweep`` times the three attention passes alone at BASELINE config 5's shapes (one line per shape), and with
+``--mode sweep`` times the three attention passes alone at L in {64, 81, 100, 256, 900, 2048} and D in {64, 128} (one
+line per shape), and with
 ``--passes qkv_rope,qkv_unfused`` the fused qkv projection against cuBLAS + the split kernel at the same shapes.
 ``--mode train`` times a training step (double backward, bucketed NCCL all-reduce overlapped with the backward,
 AdamW) on the sudoku-like 81-token workload or, with ``--train-workload sxm100``, the multi-solution 100-token
@@ -202,7 +204,7 @@ def reference_energy_config(ref_energy, *, board: int, vocab: int, softplus: boo
 
 
 def reference_network(ref_energy, device, gpu_fast: bool):
-    """The reference's ``InnerNetwork`` (embeddings, energy, descent) for the cfg3 workload, in eval mode."""
+    """The reference's ``InnerNetwork`` (embeddings, energy, descent) for the maze-30x30 workload, in eval mode."""
     torch.manual_seed(0)
     cfg = reference_energy_config(ref_energy, board=BOARD, vocab=5, softplus=True, gpu_fast=gpu_fast)
     with torch.device(device):
@@ -211,7 +213,7 @@ def reference_network(ref_energy, device, gpu_fast: bool):
 
 
 def cpu_reference_sample(seconds: float = 10.0, rows: int = 2, min_steps: int = 1) -> dict:
-    """The reference's CPU path timed on ``rows`` rows of the cfg3 workload until ``seconds`` have passed: its own
+    """The reference's CPU path timed on ``rows`` rows of the maze-30x30 workload until ``seconds`` have passed: its own
     eager modules from the installed reference (math attention, ``EBR_FUSED_ATTN_IMPL=reference``, no compilation,
     one ``EnergyDescent`` microstep per step), else this repository's CPU port (oracle attention inside the oracle's
     restatement of the network). Returns sample-steps/s and what was run."""

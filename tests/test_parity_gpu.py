@@ -212,6 +212,32 @@ def test_parity_growing_logits(dtype):
         check_out(got, ref, dtype, GRAD_TOL, "grad")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_parity_forward_v_scale(D):
+    """V whose magnitude changes across the key tiles of one slice and leaves fp16's range at both ends, each head
+    judged on its own scale (a P V product carried in a 16-bit format with one fixed scale would lose these):
+    h0: |v| rising 4x per 64-key tile up to 4^7 and falling back; h1: the first 200 keys' v all zero;
+    h2: v x 3e5 (above fp16's largest finite 65504); h3: v x 1e-6 (fp16 subnormal)."""
+    B, H, N = 1, 4, 900
+    dtype = torch.bfloat16
+    q, k, v, do, gq, gk, gv = make_inputs(B, H, N, D, dtype, seed=900 + D)
+    tile = torch.arange(N, device=DEV) // 64
+    f = torch.ones(H, N, device=DEV)
+    f[0] = 4.0 ** torch.minimum(tile, 14 - tile).clamp(min=0).float()
+    f[1, :200] = 0.0
+    f[2] = 3e5
+    f[3] = 1e-6
+    v = (v.float() * f[None, :, :, None]).to(dtype)
+    o, lse = torch.ops.ebr_fused.attn_fwd(q, k, v, D**-0.5)
+    torch.cuda.synchronize()
+    _native.device_status()
+    n = lambda t: _np(t).astype(np.float32)
+    O, LSE = oracle.attn_fwd(n(q), n(k), n(v), D**-0.5)
+    for h in range(H):
+        check_out(o[:, h], O[:, h], dtype, FWD_TOL, f"o head {h}", floor=0.0)
+    assert _maxrel(lse, LSE) < 1e-5
+
+
 @pytest.mark.parametrize("layout", ["qkv", "odd"])
 def test_parity_strided_operands(layout):
     B, H, N, D = 2, 4, 81, 64
