@@ -31,7 +31,6 @@ EXPORTED = (
     "ebr_attn_launch_count",
     "ebr_attn_bwd_noalloc",
     "ebr_attn_test_bounded_wait",
-    "ebr_attn_test_exp2",
 )
 
 # include/ebr_layers.h: the fused kernels on either side of the attention.
@@ -98,9 +97,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ebr_attn_launch_count.argtypes = []
     lib.ebr_attn_launch_count.restype = ctypes.c_uint64
     lib.ebr_attn_test_bounded_wait.argtypes = [i64, vp]
-    lib.ebr_attn_test_exp2.argtypes = [vp, vp, vp, i64, vp]
     for name in ("ebr_attn_fwd", "ebr_attn_bwd", "ebr_attn_bwd_bwd", "ebr_attn_uses_tensor_cores",
-                 "ebr_attn_device_status", "ebr_attn_test_bounded_wait", "ebr_attn_test_exp2"):  # fmt: skip
+                 "ebr_attn_device_status", "ebr_attn_test_bounded_wait"):  # fmt: skip
         getattr(lib, name).restype = ctypes.c_int
     dbl, fp = ctypes.c_double, ctypes.c_void_p
     lib.ebr_rope_split.argtypes = dims + [vp, i64, i64, fp, fp, fp, vp, vp, vp, vp]

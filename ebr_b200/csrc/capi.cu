@@ -619,16 +619,6 @@ __global__ void bounded_wait_test_kernel(uint64_t limit_ns, int site) {
   mbar_wait_limited(&bar, 0, site, limit_ns);
 }
 
-// 2^x by both of the kernels' exponentials (ebr_attn_test_exp2).
-__global__ void exp2_test_kernel(const float* __restrict__ x, float* __restrict__ sfu, float* __restrict__ poly,
-                                 int64_t n) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    sfu[i] = exp2_approx(x[i]);
-    poly[i] = exp2_poly(x[i]);
-  }
-}
-
 }  // namespace
 
 // ================================================================================================ C ABI
@@ -850,18 +840,6 @@ int ebr_attn_test_bounded_wait(int64_t limit_ns, void* stream) {
   bounded_wait_test_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(limit_ns),
                                                                           kBoundedWaitTestSite);
   return check_launch("bounded_wait_test_kernel");
-}
-
-int ebr_attn_test_exp2(const float* x, float* sfu, float* poly, int64_t n, void* stream) {
-  if (n < 0 || n > (int64_t{1} << 31)) return set_error(EBR_ERR_SHAPE, "n must be in [0, 2^31]%s%s");
-  if (n == 0) return EBR_OK;
-  if (!x || !sfu || !poly) return set_error(EBR_ERR_NULL, "null pointer%s%s");
-  int device = 0, s;
-  if ((s = check_device(&device))) return s;
-  const int64_t blocks = (n + 255) / 256;
-  exp2_test_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, sfu, poly, n);
-  return check_launch("exp2_test_kernel");
 }
 
 const char* ebr_attn_status_string(int status) {

@@ -403,24 +403,6 @@ __device__ __forceinline__ float exp2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA / integer pipes, for the softmax's arguments (x <= 8): Cody-Waite range reduction x = n + f with
-// n = round(x) taken by the 1.5 * 2^23 shifter and f in [-1/2, 1/2], a degree-4 minimax polynomial for 2^f on that
-// interval (coefficients fitted for these kernels by the Remez exchange algorithm on the relative error: 2.6e-6, 2.7e-6
-// when evaluated in float32), and 2^n applied by adding n to the exponent field. Arguments below -126 (masked keys:
-// -inf) give a non-negative value below 2^-125 instead of 0. The softmax sends a fixed share of its exponentials here
-// so the SFU (ex2) and the FMA pipes share the work.
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23: x + kShift rounds x to an integer in the low mantissa bits
-  x = fmaxf(x, -126.0f);
-  const float t = x + kShift;
-  const float f = x - (t - kShift);
-  float p = fmaf(f, 9.570102207362652e-3f, 5.591785907745361e-2f);
-  p = fmaf(f, p, 2.402474433183670e-1f);
-  p = fmaf(f, p, 6.931217908859253e-1f);
-  p = fmaf(f, p, 9.999992847442627e-1f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ float exp_nat(float x) { return exp2_approx(x * 1.4426950408889634f); }
 __device__ __forceinline__ double exp_nat(double x) { return exp(x); }
 

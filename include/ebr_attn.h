@@ -131,12 +131,6 @@ int ebr_attn_device_status(void);
  * the context stays usable. */
 int ebr_attn_test_bounded_wait(int64_t limit_ns, void* stream);
 
-/* Test support, with no counterpart in the reference: for n float32 arguments x (device memory), writes 2^x as the
- * kernels' two exponentials compute it -- the SFU instruction ex2.approx.ftz.f32 into `sfu` and the FMA-pipe
- * polynomial the softmax uses for a share of its elements into `poly` -- so a test can hold the polynomial to the
- * SFU's error bound. */
-int ebr_attn_test_exp2(const float* x, float* sfu, float* poly, int64_t n, void* stream);
-
 /* Human-readable text of a status code, and of the last CUDA error seen by this thread. */
 const char* ebr_attn_status_string(int status);
 const char* ebr_attn_last_error(void);

@@ -177,28 +177,3 @@ def test_bounded_wait_reports_a_timeout_and_the_context_survives(lib):
     x = torch.arange(1024, device="cuda", dtype=torch.float32)
     assert float(x.sum()) == 1023 * 1024 / 2
 
-
-@pytest.mark.gpu
-def test_fma_pipe_exp2_is_held_to_the_sfu_error_bound(lib):
-    """The softmax's second exponential -- Cody-Waite range reduction and a degree-4 minimax polynomial on the FMA
-    pipes, used for a share of the forward's elements -- against float64 2^x and the SFU's ex2.approx.ftz on a dense
-    grid of the softmax's argument range [-126, 8] plus -inf (masked keys): within 4e-6 relative where 2^x is a
-    normal float (the SFU's own error is ~2^-22; either is far below the 2^-11 of the tf32 P V product that consumes
-    P), and non-negative below 2^-125 where it is not."""
-    import torch
-
-    grid = torch.linspace(-126.0, 8.0, 2_000_001, dtype=torch.float64)
-    x = torch.cat([grid, torch.tensor([-float("inf"), -1000.0, -126.5, 0.0, -0.5, 0.5, 7.999])]).float().cuda()
-    sfu, poly = torch.empty_like(x), torch.empty_like(x)
-    stream = torch.cuda.current_stream().cuda_stream
-    assert lib.ebr_attn_test_exp2(x.data_ptr(), sfu.data_ptr(), poly.data_ptr(), x.numel(), stream) == _native.OK
-    torch.cuda.synchronize()
-    exact = torch.exp2(x.double())
-    normal = exact >= 2.0**-125
-    rel_poly = float(((poly.double() - exact).abs() / exact)[normal].max())
-    rel_sfu = float(((sfu.double() - exact).abs() / exact)[normal].max())
-    print(f"max relative error: FMA-pipe exp2 {rel_poly:.2e}, SFU ex2.approx {rel_sfu:.2e}")
-    assert rel_poly <= 4e-6 and rel_sfu <= 2e-6
-    tiny = poly[~normal.to(poly.device)]
-    assert bool((tiny >= 0).all()) and bool((tiny < 2.0**-124).all())
-    assert lib.ebr_attn_test_exp2(x.data_ptr(), sfu.data_ptr(), poly.data_ptr(), -1, stream) == _native.ERR_SHAPE
