@@ -740,8 +740,8 @@ def run_sweep(args) -> None:
                              "gbs": round(gbs, 0), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}  # fmt: skip
             del q, k, v, do, gq, gk, gv, o, lse, dq
             torch.cuda.empty_cache()
-            proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused", "gate_up", "gate_up_unfused")
-                    if p in args.passes.split(",")]
+            proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused", "gate_up", "gate_up_unfused",
+                                "rope_merge", "swiglu_bwd") if p in args.passes.split(",")]
             if proj and args.impl == "ours":
                 out.update(sweep_qkv(args, proj, B, L, H, D, pk))
             _native.device_status()
@@ -749,16 +749,23 @@ def run_sweep(args) -> None:
             torch.cuda.empty_cache()
 
 
+def _no_grad_call(fn, *a):
+    with torch.no_grad():
+        return fn(*a)
+
+
 def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     """The projections of one block at the sweep shape: qkv (x [B, L, H D], W [3 H D, H D]) as the tcgen05 GEMM with
     the RoPE split as its epilogue (``qkv_rope``) and as cuBLAS + the split kernel (``qkv_unfused``); the output
     projection from the head-major attention output (``o_proj``) and as transpose copy + cuBLAS (``o_unfused``); the
     MLP's gate / up projection with the SwiGLU activation as its epilogue (``gate_up``) and as cuBLAS + the activation
-    kernel (``gate_up_unfused``)."""
+    kernel (``gate_up_unfused``); the two HBM-bound kernels of the dE/dz backward, the RoPE merge of dq / dk / dv into
+    d(qkv) (``rope_merge``) and the SwiGLU backward (``swiglu_bwd``)."""
     import torch.nn.functional as F
 
     from ebr_b200.energy import NetShape, rope_tables
-    from ebr_b200.layers import gate_up_swiglu_op, o_proj_op, qkv_rope_split_op, rope_split_op, swiglu_act
+    from ebr_b200.layers import _swiglu_grad, gate_up_swiglu_op, o_proj_op, qkv_rope_split_op, rope_merge_op, \
+        rope_split_op, swiglu_act
 
     side = int(round(L**0.5))
     hh, ww = (side, side) if side * side == L else (32, L // 32)
@@ -772,6 +779,12 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     wo = (torch.randn(C, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     inter = NetShape(hidden=C, heads=H).mlp_width  # the energy network's SwiGLU width (expansion 4)
     wgu = (torch.randn(2 * inter, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
+    need = set(passes)
+    if "rope_merge" in need:
+        dq3 = [torch.randn(B, H, L, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3)]
+    if "swiglu_bwd" in need:
+        hgu = torch.randn(B, L, 2 * inter, device="cuda", generator=g).to(torch.bfloat16)
+        gact = torch.randn(B, L, inter, device="cuda", generator=g).to(torch.bfloat16)
     fns = {
         "qkv_rope": lambda: qkv_rope_split_op(x, w, cos_t, sin_t, e, H),
         "qkv_unfused": lambda: rope_split_op(F.linear(x, w), cos_t, sin_t, e, H),
@@ -779,6 +792,8 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         "o_unfused": lambda: F.linear(o.transpose(1, 2).reshape(B, L, C), wo),
         "gate_up": lambda: gate_up_swiglu_op(x, wgu),
         "gate_up_unfused": lambda: swiglu_act(F.linear(x, wgu)),
+        "rope_merge": lambda: rope_merge_op(*dq3, cos_t, sin_t, e),
+        "swiglu_bwd": lambda: _no_grad_call(_swiglu_grad, hgu, gact),  # the fused kernel (no higher-order graph)
     }
     res = {}
     for name in passes:
@@ -789,12 +804,16 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         elif name.startswith("gate_up"):
             flop = 2.0 * B * L * C * 2 * inter
             byt = 2.0 * (B * L * C + 2 * inter * C + 3 * B * L * inter)  # x, W, h, act
+        elif name == "rope_merge":
+            flop, byt = 0.0, 2.0 * 6 * B * L * C  # dq, dk, dv in, d(qkv) out
+        elif name == "swiglu_bwd":
+            flop, byt = 0.0, 2.0 * 5 * B * L * inter  # h (gate, up) and d act in, d h out
         else:
             flop = 2.0 * B * L * C * C
             byt = 2.0 * (2 * B * L * C + C * C)  # O, W, y
         tf = flop / ms / 1e9
         res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "tc_frac": round(tf / pk["tf_burst"], 4),
-                     "gbs": round(byt / ms / 1e6, 0)}  # fmt: skip
+                     "gbs": round(byt / ms / 1e6, 0), "hbm_frac": round(byt / ms / 1e6 / pk["hbm_gbs"], 4)}  # fmt: skip
     del x, w, o, wo, wgu
     return res
 

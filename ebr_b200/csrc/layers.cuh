@@ -222,6 +222,77 @@ __global__ void rope_merge_kernel(ebr_operand dq, ebr_operand dk, ebr_operand dv
   }
 }
 
+// The merge for 16-byte slots (V * sizeof(T) == 16) whose quarter partner lies in the same warp (D / V divides 32
+// and D >= 4 V): slot = threadIdx.x, the partner slot is slot ^ (D / 4 V). Each thread loads only its own 16 bytes
+// per token -- the partner's arrive by a shuffle -- and issues the loads of kTok tokens (blockIdx.x + u gridDim.x)
+// before it computes or stores any, so each SM keeps kTok times the bytes of the one-token walk in flight (the merge
+// is bound by the latency of its loads, not by HBM bandwidth, with one token in flight). Same arithmetic as
+// rope_merge_one.
+template <typename T, int V, int kTok>
+__global__ void rope_merge_wide_kernel(ebr_operand dq, ebr_operand dk, ebr_operand dv, int64_t N, int H, int D,
+                                       int64_t tokens, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                       const float* __restrict__ qscale, T* __restrict__ out) {
+  static_assert(V * sizeof(T) == 16, "one 16-byte access per slot");
+  using C = typename Elem<T>::C;
+  const int cpr = D / V, slots = 3 * H * cpr;
+  const int slot = static_cast<int>(threadIdx.x);
+  const bool live = slot < slots;  // the block is rounded up to whole warps
+  const RopeSlot sl = rope_slot(live ? slot : 0, H, cpr, V);
+  const ebr_operand op = sl.part == 0 ? dq : sl.part == 1 ? dk : dv;
+  const T* src = static_cast<const T*>(op.data) + sl.h * op.stride_h + sl.d0;
+  const int64_t row3 = 3 * static_cast<int64_t>(H) * D;
+  const int64_t col = static_cast<int64_t>(sl.part * H + sl.h) * D + sl.d0;
+  const int lane_off = D / (4 * V);
+  const int p0 = swap_index(sl.d0, D / 4);
+  const bool scaled = sl.part == 0 && qscale != nullptr;
+  const C s = scaled ? static_cast<C>(__ldg(qscale + sl.h)) : C(1);
+  for (int64_t tok0 = blockIdx.x; tok0 < tokens; tok0 += kTok * static_cast<int64_t>(gridDim.x)) {
+    Pack<T, V> raw[kTok];
+#pragma unroll
+    for (int u = 0; u < kTok; ++u) {
+      const int64_t tok = tok0 + u * static_cast<int64_t>(gridDim.x);
+      if (live && tok < tokens) {
+        const int64_t b = tok / N, n = tok - b * N;
+        raw[u] = *reinterpret_cast<const Pack<T, V>*>(src + b * op.stride_b + n * op.stride_n);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) raw[u].e[i] = T();
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kTok; ++u) {
+      const int64_t tok = tok0 + u * static_cast<int64_t>(gridDim.x);
+      uint4 w = *reinterpret_cast<const uint4*>(&raw[u]);  // every lane shuffles (the partner may be any live lane)
+      w.x = __shfl_xor_sync(0xffffffffu, w.x, lane_off);
+      w.y = __shfl_xor_sync(0xffffffffu, w.y, lane_off);
+      w.z = __shfl_xor_sync(0xffffffffu, w.z, lane_off);
+      w.w = __shfl_xor_sync(0xffffffffu, w.w, lane_off);
+      if (!live || tok >= tokens) continue;
+      T* dst = out + tok * row3 + col;
+      if (sl.part == 2) {
+        *reinterpret_cast<Pack<T, V>*>(dst) = raw[u];
+        continue;
+      }
+      const Pack<T, V> pw = *reinterpret_cast<const Pack<T, V>*>(&w);
+      const int64_t n = tok - (tok / N) * N;
+      float cs[V], sp[V];
+      load_table_v<V>(cos_t + n * D + sl.d0, cs);
+      load_table_v<V>(sin_t + n * D + p0, sp);
+      C res[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        C own = static_cast<C>(raw[u].e[e]), partner = static_cast<C>(pw.e[e]);
+        if (scaled) {
+          own = rnd<T>(mul_rn(own, s));
+          partner = rnd<T>(mul_rn(partner, s));
+        }
+        res[e] = add_rn(mul_rn(own, static_cast<C>(cs[e])), mul_rn(partner, static_cast<C>(sp[e])));
+      }
+      store_c<T, V>(dst, res);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ residual + rms_norm
 
 // One warp per row of C elements, two passes over the row (the second hits L1 / L2): the sum of squares of

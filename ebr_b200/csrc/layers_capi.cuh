@@ -151,6 +151,18 @@ int ebr_rope_merge(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, const 
       vec = vec && aligned16(op->data) && op->stride_b % V == 0 && op->stride_h % V == 0 && op->stride_n % V == 0;
     const int Vr = vec ? V : 1;
     const int64_t tokens = B * N;
+    if constexpr (V * sizeof(T) == 16) {
+      // Partner slot in the same warp: D / V divides 32 and the partner offset D / 4 V is a power of two.
+      const int64_t cpr = D / V, off = D / (4 * V);
+      constexpr int kTok = 4;
+      if (vec && off >= 1 && 32 % cpr == 0 && (off & (off - 1)) == 0 && 3 * H * cpr <= 1024) {
+        const RopeGrid g = rope_grid(device, 3 * H * cpr, (tokens + kTok - 1) / kTok);
+        ebr::layers::rope_merge_wide_kernel<T, V, kTok><<<g.blocks, g.threads, 0, st>>>(
+            *dq, *dk, *dv, N, static_cast<int>(H), static_cast<int>(D), tokens, cos_table, sin_table, qscale,
+            static_cast<T*>(dqkv));
+        return check_launch("rope_merge");
+      }
+    }
     const RopeGrid g = rope_grid(device, 3 * H * (D / Vr), tokens);
     if (vec)
       ebr::layers::rope_merge_kernel<T, V><<<g.blocks, g.threads, 0, st>>>(

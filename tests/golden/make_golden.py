@@ -11,7 +11,7 @@ the tests only read the committed ``.npz``.
 
 Cases
 -----
-* ``cfg1``: BASELINE config 1. fp32, B=4, L=81, H=8, D=64, ``torch.manual_seed(0)``, drawn in the order q, k, v
+* ``cfg1``: the benchmark's fp32 parity case, B=4, L=81, H=8, D=64, ``torch.manual_seed(0)``, drawn in the order q, k, v
   ~ N(0,1)/8, dO ~ N(0,1), R ~ N(0,1). O, then (dQ, dK, dV) with ``create_graph=True``, then the gradient of
   sum(dQ * R) w.r.t. (Q, K, V). Too large to store whole: the inputs are re-drawn from the seed by the tests (their
   checksums are stored), the outputs are stored as 4096 fixed random entries each plus per-(b, h) sums.
@@ -66,7 +66,7 @@ def _np(t: torch.Tensor) -> np.ndarray:
 
 
 def cfg1_inputs() -> dict[str, torch.Tensor]:
-    """BASELINE config 1 inputs, drawn exactly as the config states (also used by the tests)."""
+    """The fp32 parity case's inputs, drawn in the stated order (also used by the tests)."""
     torch.manual_seed(0)
     shape = (4, 8, 81, 64)
     q = torch.randn(shape) / 8

@@ -63,7 +63,8 @@ def cfg1_inputs():
 
 
 def test_oracle_cfg1_against_reference_autograd(golden):
-    """O, first-order grads, and grad of sum(dQ * R) through the reference's autograd chain."""
+    """The fp32 B=4, L=81, H=8, D=64 case: O, first-order grads, and grad of sum(dQ * R) through the reference's
+    autograd chain."""
     x = cfg1_inputs()
     for name, arr in x.items():
         want = golden[f"cfg1/in_sum/{name}"]
