@@ -11,6 +11,7 @@
 #include "layers.cuh"
 #include "gate_up.cuh"
 #include "o_proj.cuh"
+#include "merge_gemm.cuh"
 #include "qkv_rope.cuh"
 
 namespace {
@@ -397,6 +398,48 @@ int ebr_o_proj(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t C_
                    : launch(ebr::tc_o_proj_kernel<__nv_bfloat16, 128>, static_cast<__nv_bfloat16*>(nullptr));
   return D == 64 ? launch(ebr::tc_o_proj_kernel<__half, 64>, static_cast<__half*>(nullptr))
                  : launch(ebr::tc_o_proj_kernel<__half, 128>, static_cast<__half*>(nullptr));
+}
+
+int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, int64_t C, const ebr_operand* dq,
+                          const ebr_operand* dk, const ebr_operand* dv, const void* w, const float* cos_table,
+                          const float* sin_table, const float* qscale, void* dx, void* stream) {
+  using L = ebr::MergeGemmLayout;
+  if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
+    return set_error(EBR_ERR_DTYPE, "qkv_rope_merge_dx: bfloat16 or float16 only%s%s");
+  if (B < 0 || N < 0 || H < 1 || D != 64 || C != L::kC || B > INT32_MAX || N > INT32_MAX || H > 4096)
+    return set_error(EBR_ERR_SHAPE, "qkv_rope_merge_dx: needs D = 64 and C = 512%s%s");
+  if (B * N == 0) return EBR_OK;
+  int rc = check_operand(dq, "dq");
+  if (rc == EBR_OK) rc = check_operand(dk, "dk");
+  if (rc == EBR_OK) rc = check_operand(dv, "dv");
+  if (rc != EBR_OK) return rc;
+  if (!w || !dx || !cos_table || !sin_table) return set_error(EBR_ERR_NULL, "qkv_rope_merge_dx: NULL pointer%s%s");
+  if (!tc_operand_ok(dq, B, H, N) || !tc_operand_ok(dk, B, H, N) || !tc_operand_ok(dv, B, H, N) ||
+      !all_aligned16({w, dx, cos_table, sin_table}))
+    return set_error(EBR_ERR_STRIDE, "qkv_rope_merge_dx: 16-byte aligned data and strides needed%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tq, tk, tv, tw;
+  if (make_tile_map(&tq, dq, dtype, B, H, N, D) || make_tile_map(&tk, dk, dtype, B, H, N, D) ||
+      make_tile_map(&tv, dv, dtype, B, H, N, D))
+    return set_error(EBR_ERR_CUDA, "qkv_rope_merge_dx: tensor map for dq / dk / dv%s%s");
+  if ((rc = make_matrix_map(&tw, w, dtype, 3 * H * D, C, C, L::kBK)) != EBR_OK) return rc;
+  const int64_t m_tiles = B * ((N + L::kBM - 1) / L::kBM);
+  const int64_t cap = sm_count(device);
+  const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
+  auto launch = [&](auto kernel, auto* out_tag) -> int {
+    using T = std::remove_pointer_t<decltype(out_tag)>;
+    if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))
+      return rc;
+    kernel<<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, tw, static_cast<int>(B), static_cast<int>(H),
+                                                static_cast<int>(N), cos_table, sin_table, qscale,
+                                                static_cast<T*>(dx));
+    return check_launch("tc_merge_gemm_kernel");
+  };
+  if (dtype == EBR_BFLOAT16)
+    return launch(ebr::tc_merge_gemm_kernel<__nv_bfloat16>, static_cast<__nv_bfloat16*>(nullptr));
+  return launch(ebr::tc_merge_gemm_kernel<__half>, static_cast<__half*>(nullptr));
 }
 
 int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void* x, int64_t x_stride, const void* w,

@@ -248,6 +248,45 @@ def _engine_needs(node) -> bool:
         return True
 
 
+@torch.library.custom_op("ebr_fused::qkv_rope_merge_dx", mutates_args=())
+def qkv_rope_merge_dx_op(dq: Tensor, dk: Tensor, dv: Tensor, weight: Tensor, cos: Tensor, sin: Tensor,
+                         qscale: Tensor) -> Tensor:  # fmt: skip
+    """``rope_merge(dq, dk, dv, cos, sin, qscale) @ weight`` as one tensor-core GEMM whose A operand is merged in shared
+    memory (``ebr_qkv_rope_merge_dx``): the input gradient of the qkv projection. Shapes ``merge_dx_fusable`` takes."""
+    _require_cuda(dq, "qkv_rope_merge_dx")
+    dk, dv = dk.to(dq.dtype), dv.to(dq.dtype)
+    dq, dk, dv = (t if t.stride(-1) == 1 else t.contiguous() for t in (dq, dk, dv))
+    b, h, n, d = dq.shape
+    w = weight.to(dq.dtype).contiguous()
+    out = torch.empty((b, n, w.shape[1]), device=dq.device, dtype=dq.dtype)
+    cos, sin = _table(cos, dq.device), _table(sin, dq.device)
+    qs, qs_ptr = _qscale_arg(qscale)
+    ops = [_native.Operand(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)) for t in (dq, dk, dv)]
+    r = ctypes.byref
+    _native.check(
+        _native.lib().ebr_qkv_rope_merge_dx(_DTYPES[dq.dtype], b, n, h, d, w.shape[1], r(ops[0]), r(ops[1]),
+                                            r(ops[2]), w.data_ptr(), cos.data_ptr(), sin.data_ptr(), qs_ptr,
+                                            out.data_ptr(), _stream()),  # fmt: skip
+        "qkv_rope_merge_dx",
+    )
+    return out
+
+
+@qkv_rope_merge_dx_op.register_fake
+def _(dq, dk, dv, weight, cos, sin, qscale):
+    b, h, n, d = dq.shape
+    return dq.new_empty((b, n, weight.shape[1]))
+
+
+def merge_dx_fusable(g: Tensor, weight: Tensor) -> bool:
+    """Whether ``ebr_qkv_rope_merge_dx`` serves a qkv projection's input gradient: 16-bit CUDA head-major gradients
+    [B, H, N, 64] and a [3 H 64, 512] weight."""
+    if g.dim() != 4 or not g.is_cuda or g.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    h, d = g.shape[1], g.shape[3]
+    return d == 64 and weight.dim() == 2 and tuple(weight.shape) == (3 * h * d, 512)
+
+
 class _QkvSplit(torch.autograd.Function):
     """Forward: the projection with the split as its epilogue. Backward: the merge (the split's exact adjoint), then
     the projection's two products, all differentiable ops, so every higher order follows."""
@@ -274,6 +313,9 @@ class _QkvSplit(torch.autograd.Function):
             z = torch.zeros(ctx.shape, dtype=ref.dtype, device=ref.device)
         gq, gk, gv = (z if g is None else g for g in (gq, gk, gv))
         need_x, need_w = (_engine_needs(n) for n in ctx.nodes)
+        if need_x and not need_w and not torch.is_grad_enabled() and merge_dx_fusable(gq, weight):
+            # dE/dz only, no higher-order graph: the merge folded into the GEMM's A operand.
+            return qkv_rope_merge_dx_op(gq, gk, gv, weight, cos, sin, qscale), None, None, None, None, None
         gqkv = _Merge.apply(gq, gk, gv, cos, sin, qscale)
         gx = gqkv @ weight.to(gqkv.dtype) if need_x else None
         gw = gqkv.flatten(0, 1).t() @ x.flatten(0, 1) if need_w else None
