@@ -384,9 +384,13 @@ int launch_tc_bwd_pipe(int device, int dtype, int64_t B, int64_t H, int64_t N, d
   const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
   float* di = static_cast<float*>(scratch);
   const int BH = static_cast<int>(B * H), Hi = static_cast<int>(H), Ni = static_cast<int>(N);
+  // O is contiguous [B, H, N, D]: the row pass stages it by TMA with Q and dO (for D_i = <dO_i, O_i>).
+  const ebr_operand oo{o, H * N * D, N * D, D};
+  CUtensorMap to;
+  if (make_tile_map(&to, &oo, dtype, B, H, N, D)) return kNoTensorMap;
   tc_bwd_dq_split_kernel<T, D><<<grid, LR::kThreads, LR::kSmem, st>>>(
-      tq, tk64, tv64, tdo, static_cast<const T*>(o), static_cast<const float*>(lse), di, static_cast<T*>(dq), BH, Hi,
-      Ni, static_cast<float>(scale));
+      tq, tk64, tv64, tdo, to, static_cast<const float*>(lse), di, static_cast<T*>(dq), BH, Hi, Ni,
+      static_cast<float>(scale));
   if ((s = check_launch("tc_bwd_dq_split_kernel"))) return s;
   tc_bwd_dkdv_split_kernel<T, D><<<grid, LC::kThreads, LC::kSmem, st>>>(
       tk, tv, tq64, tdo64, static_cast<const float*>(lse), di, static_cast<T*>(dk), static_cast<T*>(dv), BH, Hi, Ni,

@@ -162,6 +162,21 @@ __device__ __forceinline__ float row_delta(const unsigned char* sDO, int row, co
   return di;
 }
 
+// row_delta with both rows in shared memory ([128 x D] SW128 tiles of dO and O).
+template <typename T, int D>
+__device__ __forceinline__ float row_delta_smem(const unsigned char* sDO, const unsigned char* sO, int row) {
+  float di = 0.f;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    float x[8], y[8];
+    ld_row8<T>(sDO, row, c, x);
+    ld_row8<T>(sO, row, c, y);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) di += x[i] * y[i];
+  }
+  return di;
+}
+
 // ================================================================================================ tile descriptors for 64- and 128-row tiles
 
 // Descriptors for tiles of `rows` rows (64 or 128): the 64-column halves of a D = 128 tile are rows * 128 B apart.

@@ -29,27 +29,32 @@ struct BwdRowLayout {
   static constexpr uint32_t kSmall = (D / 64) * kHalf64;   // [64 x D] tile (K, V)
   static constexpr int kQBufs = D == 64 ? 2 : 1;
   static constexpr int kStages = 4;
-  static constexpr uint32_t kQ = 0;                     // buffer b: Q at kQ + 2 b kBig, dO at + kBig
-  static constexpr uint32_t kRing = 2 * kQBufs * kBig;  // stage s: K at kRing + 2 s kSmall, V at + kSmall
+  static constexpr uint32_t kQ = 0;                     // buffer b: Q at kQ + 3 b kBig, dO at + kBig, O at + 2 kBig
+  static constexpr uint32_t kRing = 3 * kQBufs * kBig;  // stage s: K at kRing + 2 s kSmall, V at + kSmall
   static constexpr uint32_t kBytes = kRing + kStages * 2 * kSmall;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kThreads = 352;
   static constexpr int kSBufs = 3;  // score buffers of 128 columns; dQ after them
+  // dQ accumulators: two at D = 64 (3 x 128 + 2 x 64 = 512 columns), so an item's first dQ products need not wait
+  // until the previous item's dQ has been read out; one at D = 128.
+  static constexpr int kDqBufs = D == 64 ? 2 : 1;
 };
 
 template <typename T, int D>
 __global__ void __launch_bounds__(352, 1)
     tc_bwd_dq_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk64,
                            const __grid_constant__ CUtensorMap tv64, const __grid_constant__ CUtensorMap tdo,
-                           const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ di_out,
+                           const __grid_constant__ CUtensorMap to, const float* __restrict__ lse,
+                           float* __restrict__ di_out,
                            T* __restrict__ dq, int BH, int H, int N, float scale) {
   using L = BwdRowLayout<D>;
   constexpr int NS = L::kStages, QB = L::kQBufs, NB = L::kSBufs;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
+  constexpr int DB = L::kDqBufs;
   __shared__ uint64_t q_full[QB], q_empty[QB], kv_full[NS], kv_empty[NS], s_full[NB], p_full[NB], ds_free[NB],
-      dq_done, dq_free;
+      dq_done[DB], dq_free[DB];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -57,8 +62,9 @@ __global__ void __launch_bounds__(352, 1)
   const int n_qt = (N + kTile - 1) / kTile, n_ks = (N + 63) / 64;
   const int64_t items = static_cast<int64_t>(BH) * n_qt;
   constexpr bool kB = is_bf16<T>();
-  auto sQ = [&](int b) { return smem + L::kQ + b * 2 * L::kBig; };
-  auto sDO = [&](int b) { return smem + L::kQ + b * 2 * L::kBig + L::kBig; };
+  auto sQ = [&](int b) { return smem + L::kQ + b * 3 * L::kBig; };
+  auto sDO = [&](int b) { return smem + L::kQ + b * 3 * L::kBig + L::kBig; };
+  auto sO = [&](int b) { return smem + L::kQ + b * 3 * L::kBig + 2 * L::kBig; };
   auto sK = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall; };
   auto sV = [&](int s) { return smem + L::kRing + s * 2 * L::kSmall + L::kSmall; };
 
@@ -76,8 +82,10 @@ __global__ void __launch_bounds__(352, 1)
       mbar_init(&p_full[b], 128);
       mbar_init(&ds_free[b], 1);
     }
-    mbar_init(&dq_done, 1);
-    mbar_init(&dq_free, 256);
+    for (int i = 0; i < DB; ++i) {
+      mbar_init(&dq_done[i], 1);
+      mbar_init(&dq_free[i], 256);
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -99,6 +107,7 @@ __global__ void __launch_bounds__(352, 1)
       tma_prefetch_desc(&tk64);
       tma_prefetch_desc(&tv64);
       tma_prefetch_desc(&tdo);
+      tma_prefetch_desc(&to);
       uint32_t kv_use = 0, quse = 0;
       bool ok = true;
       for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++quse) {
@@ -107,10 +116,11 @@ __global__ void __launch_bounds__(352, 1)
         const int qb = static_cast<int>(quse % QB);
         ok = mbar_wait_or_abort(&q_empty[qb], ((quse / QB) & 1) ^ 1, 311, abort);
         if (!ok) break;
-        mbar_arrive_expect_tx(&q_full[qb], 2 * L::kBig);
+        mbar_arrive_expect_tx(&q_full[qb], 3 * L::kBig);
         for (int hh = 0; hh < D / 64; ++hh) {
           tma_load_4d(sQ(qb) + hh * kHalfBytes, &tq, &q_full[qb], hh * 64, qt * kTile, h, b);
           tma_load_4d(sDO(qb) + hh * kHalfBytes, &tdo, &q_full[qb], hh * 64, qt * kTile, h, b);
+          tma_load_4d(sO(qb) + hh * kHalfBytes, &to, &q_full[qb], hh * 64, qt * kTile, h, b);
         }
         for (int j = 0; j < n_ks && ok; ++j, ++kv_use) {
           const int s = static_cast<int>(kv_use % NS);
@@ -135,7 +145,7 @@ __global__ void __launch_bounds__(352, 1)
       for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++quse) {
         const int qb = static_cast<int>(quse % QB);
         ok = mbar_wait_or_abort(&q_full[qb], (quse / QB) & 1, 321, abort);
-        const uint64_t aq = dQ0 + static_cast<uint64_t>(qb * ((2 * L::kBig) >> 4));
+        const uint64_t aq = dQ0 + static_cast<uint64_t>(qb * ((3 * L::kBig) >> 4));
         const uint64_t ado = aq + (L::kBig >> 4);
         for (int j = 0; j < n_ks && ok; ++j, ++kv_use) {
           const int b = static_cast<int>(kv_use % NB), s = static_cast<int>(kv_use % NS);
@@ -168,8 +178,10 @@ __global__ void __launch_bounds__(352, 1)
       const uint64_t dK0 = sw128_desc(smem_u32(sK(0)), L::kHalf64, 1024u);
       const uint32_t idKM = idesc_f16(kB, 0, 1, 128, D);
       for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++icnt) {
-        // The previous item's dQ must have been read out before this item's first product overwrites it.
-        ok = mbar_wait_or_abort(&dq_free, (icnt & 1) ^ 1, 331, abort);
+        // The dQ buffer's previous item must have been read out before this item's first product overwrites it.
+        const int db = static_cast<int>(icnt % DB);
+        const uint32_t tDQb = tDQ + db * D;
+        ok = mbar_wait_or_abort(&dq_free[db], ((icnt / DB) & 1) ^ 1, 331, abort);
         for (int j = 0; j < n_ks && ok; ++j, ++kv_use) {
           const int b = static_cast<int>(kv_use % NB), s = static_cast<int>(kv_use % NS);
           ok = mbar_wait_or_abort(&p_full[b], (kv_use / NB) & 1, 332, abort);
@@ -179,11 +191,11 @@ __global__ void __launch_bounds__(352, 1)
           const uint32_t tA = tmem + b * 128;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tDQ, tA + kk * 8, bk + ((kk * 2048) >> 4), idKM, (j > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tDQb, tA + kk * 8, bk + ((kk * 2048) >> 4), idKM, (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&ds_free[b]);
           mma_commit(&kv_empty[s]);
         }
-        if (ok) mma_commit(&dq_done);
+        if (ok) mma_commit(&dq_done[db]);
       }
     }
   } else if (warp < 8) {
@@ -192,18 +204,28 @@ __global__ void __launch_bounds__(352, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     uint32_t g0 = 0, icnt = 0, quse = 0;  // global step of the item's first step, items
     bool ok = true;
+    // This thread's lse of the next item is loaded while the current item runs (O and dO arrive by TMA with Q).
+    float l_nx = 0.f;
+    auto prefetch = [&](int64_t it_) {
+      if (it_ >= items) return;
+      const int bh_ = static_cast<int>(it_ / n_qt);
+      const int row_ = static_cast<int>(it_ - static_cast<int64_t>(bh_) * n_qt) * kTile + lrow;
+      if (row_ < N) l_nx = __ldg(lse + static_cast<int64_t>(bh_) * N + row_);
+    };
+    prefetch(blockIdx.x);
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++icnt, ++quse, g0 += n_ks) {
       const int bh = static_cast<int>(it / n_qt), qt = static_cast<int>(it - static_cast<int64_t>(bh) * n_qt);
       const int qb = static_cast<int>(quse % QB);
       const int row = qt * kTile + lrow;
       const bool row_ok = row < N;
       const int64_t grow = static_cast<int64_t>(bh) * N + row;
-      const float Li = row_ok ? lse[grow] : 0.f;
+      const float Li = row_ok ? l_nx : 0.f;
+      prefetch(it + gridDim.x);
       ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_full[qb], (quse / QB) & 1, 341, abort));
       if (!ok) break;
       float Di = 0.f;
       if (row_ok) {
-        Di = row_delta<T, D>(sDO(qb), lrow, o + grow * D);
+        Di = row_delta_smem<T, D>(sDO(qb), sO(qb), lrow);
         if (w == 0) di_out[grow] = Di;
       }
       // This group takes the steps whose global index has its parity (so the groups alternate across items too).
@@ -259,13 +281,14 @@ __global__ void __launch_bounds__(352, 1)
         mbar_arrive(&p_full[b]);
       }
       if (!ok) break;
-      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&dq_done, icnt & 1, 343, abort));
+      const int db = static_cast<int>(icnt % DB);
+      ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&dq_done[db], (icnt / DB) & 1, 343, abort));
       if (!ok) break;
       tc_fence_after();
       T* dst = row_ok ? dq + grow * D : nullptr;
-      store_cols_from_tmem<T, D / 2>(tDQ + lane_off, w * (D / 2), scale, dst);
+      store_cols_from_tmem<T, D / 2>(tDQ + db * D + lane_off, w * (D / 2), scale, dst);
       tc_fence_before();
-      mbar_arrive(&dq_free);
+      mbar_arrive(&dq_free[db]);
     }
   }
   tc_fence_before();
