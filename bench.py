@@ -715,7 +715,7 @@ def run_sweep(args) -> None:
     Ls = [int(v) for v in args.lengths.split(",")]
     for D in [int(v) for v in args.head_dims.split(",")]:
         for L in Ls:
-            B, H = 262144 // L, 8
+            B, H = (args.sweep_batch or 262144 // L), 8
             g = torch.Generator(device="cuda").manual_seed(0)
             mk = lambda s: (torch.randn(B, H, L, D, device="cuda", generator=g) * s).to(torch.bfloat16)
             q, k, v, do, gq, gk, gv = mk(0.5), mk(0.5), mk(0.5), mk(1.0), mk(1.0), mk(1.0), mk(1.0)
@@ -835,6 +835,8 @@ def main() -> None:
     ap.add_argument("--mode", choices=["descent", "sweep", "train"], default="descent")
     ap.add_argument("--lengths", default="64,81,100,256,900,2048")
     ap.add_argument("--head-dims", default="64,128")
+    ap.add_argument("--sweep-batch", type=int, default=0,
+                    help="sweep mode: batch B per shape (default 262144 // L: 268 MB per tensor at D = 64)")
     ap.add_argument("--passes", default="attn_fwd,attn_bwd,attn_bwd_bwd",
                     help="sweep: which passes to time (also qkv_rope, qkv_unfused, o_proj, o_unfused: the projections)")
     ap.add_argument("--train-workload", choices=["sudoku81", "sxm100"], default="sudoku81",
