@@ -357,12 +357,29 @@ __global__ void __launch_bounds__(320, 1)
     }
     const CUtensorMap* amap[4] = {&ta0, &ta1, &ta2, &ta3};
     const CUtensorMap* bmap[4] = {&tb0, &tb1, &tb2, &tb3};
+    // Column pass: this lane's (lse, D, E, T) of queries lane and lane + 32 of a step, loaded while the previous
+    // step is staged. Queries past N get zeros: with their zero Q / dO / gQ rows every derived value is 0.
+    auto load_stats = [&](int64_t base_, int j_, float4 (&v)[2]) {
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int qi = j_ * 64 + lane + 32 * k2;
+        v[k2] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (qi < N) {
+          v[k2].x = __ldg(lse + base_ + qi);
+          v[k2].y = __ldg(stats + base_ + qi);
+          v[k2].z = __ldg(stats + rows_total + base_ + qi);
+          v[k2].w = __ldg(stats + 2 * rows_total + base_ + qi);
+        }
+      }
+    };
     int64_t li = 0;
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++li) {
       const int bh = static_cast<int>(it / n_it), t = static_cast<int>(it - static_cast<int64_t>(bh) * n_it);
       const int b = bh / H, h = bh - (bh / H) * H;
       const int64_t base = static_cast<int64_t>(bh) * N;
       const int ib = static_cast<int>(li % NI);
+      float4 cur[2];
+      if (kCol) load_stats(base, 0, cur);
       if (lane == 0) {
         ok = mbar_wait_or_abort(&it_empty[ib], (static_cast<uint32_t>(li / NI) & 1) ^ 1, 541, abort);
         if (ok) {
@@ -375,6 +392,8 @@ __global__ void __launch_bounds__(320, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       for (int j = 0; j < n_st && ok; ++j, ++g) {
         const int s = static_cast<int>(g % NS);
+        float4 nxt[2];
+        if (kCol && j + 1 < n_st) load_stats(base, j + 1, nxt);
         ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&rg_empty[s], ((g / NS) & 1) ^ 1, 542, abort));
         if (!ok) break;
         if (lane == 0) {
@@ -384,19 +403,11 @@ __global__ void __launch_bounds__(320, 1)
             if (ring_has[i]) tma_load_4d(ring(s, i), bmap[i], &rg_full[s], 0, j * 64, h, b);
         }
         if (kCol) {
-          // Queries past N get lse = D = E = T = 0: with their zero Q / dO / gQ rows every derived value is 0.
           float4* st = reinterpret_cast<float4*>(stg) + s * 64;
 #pragma unroll
-          for (int k2 = lane; k2 < 64; k2 += 32) {
-            const int qi = j * 64 + k2;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (qi < N) {
-              v.x = lse[base + qi];
-              v.y = stats[base + qi];
-              v.z = stats[rows_total + base + qi];
-              v.w = stats[2 * rows_total + base + qi];
-            }
-            st[k2] = v;
+          for (int k2 = 0; k2 < 2; ++k2) {
+            st[lane + 32 * k2] = cur[k2];
+            cur[k2] = nxt[k2];
           }
           mbar_arrive(&rg_full[s]);
         }

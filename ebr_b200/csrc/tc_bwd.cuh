@@ -386,11 +386,24 @@ __global__ void __launch_bounds__(352, 1)
     // ---------------------------------------------------------------- producer (lane 0: TMA; all lanes: lse / D)
     uint32_t q_use = 0, kuse = 0;
     bool ok = true;
+    // This lane's lse / D of a query step (queries lane and lane + 32). Queries past N get lse = D = 0: with their
+    // zero Q / dO rows this makes P^T = 1 and dS^T = 0 there, and dO = 0 keeps them out of dV, so the compute warps
+    // need no mask. A step's values are loaded while the previous step is staged, so their latency stays off the ring.
+    auto load_stats = [&](int64_t base_, int i_, float (&l)[2], float (&d)[2]) {
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int qi = i_ * 64 + lane + 32 * k2;
+        l[k2] = qi < N ? __ldg(lse + base_ + qi) : 0.f;
+        d[k2] = qi < N ? __ldg(di + base_ + qi) : 0.f;
+      }
+    };
     for (int64_t it = blockIdx.x; it < items && ok; it += gridDim.x, ++kuse) {
       const int bh = static_cast<int>(it / n_kt), kt = static_cast<int>(it - static_cast<int64_t>(bh) * n_kt);
       const int b = bh / H, h = bh - (bh / H) * H;
       const int64_t base = static_cast<int64_t>(bh) * N;
       const int kb = static_cast<int>(kuse % KB);
+      float cl[2], cd[2];
+      load_stats(base, 0, cl, cd);
       if (lane == 0) {
         ok = mbar_wait_or_abort(&k_empty[kb], ((kuse / KB) & 1) ^ 1, 411, abort);
         if (ok) {
@@ -404,6 +417,8 @@ __global__ void __launch_bounds__(352, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       for (int i = 0; i < n_qs && ok; ++i, ++q_use) {
         const int s = static_cast<int>(q_use % NS);
+        float nl[2] = {0.f, 0.f}, nd[2] = {0.f, 0.f};
+        if (i + 1 < n_qs) load_stats(base, i + 1, nl, nd);
         ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&q_empty[s], ((q_use / NS) & 1) ^ 1, 412, abort));
         if (!ok) break;
         if (lane == 0) {
@@ -413,14 +428,13 @@ __global__ void __launch_bounds__(352, 1)
             tma_load_4d(sDO(s) + hh * L::kHalf64, &tdo64, &q_full[s], hh * 64, i * 64, h, b);
           }
         }
-        // Queries past N get lse = D = 0: with their zero Q / dO rows this makes P^T = 1 and dS^T = 0 there, and
-        // dO = 0 keeps them out of dV, so the compute warps need no mask.
         float* st = stats + s * 128;
 #pragma unroll
-        for (int k2 = lane; k2 < 64; k2 += 32) {
-          const int qi = i * 64 + k2;
-          st[k2] = qi < N ? lse[base + qi] : 0.f;
-          st[64 + k2] = qi < N ? di[base + qi] : 0.f;
+        for (int k2 = 0; k2 < 2; ++k2) {
+          st[lane + 32 * k2] = cl[k2];
+          st[64 + lane + 32 * k2] = cd[k2];
+          cl[k2] = nl[k2];
+          cd[k2] = nd[k2];
         }
         mbar_arrive(&q_full[s]);
       }
