@@ -44,6 +44,8 @@ EXPORTED_LAYERS = (
     "ebr_rms_norm_bwd",
     "ebr_swiglu_fwd",
     "ebr_swiglu_bwd",
+    "ebr_swiglu_bwd2",
+    "ebr_rms_norm_bwd2",
     "ebr_gate_up_swiglu",
     "ebr_descent_step",
     "ebr_descent_step_scratch_floats",
@@ -111,6 +113,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ebr_rms_norm_bwd.argtypes = [ctypes.c_int, i64, i64, vp, fp, vp, vp, vp]
     lib.ebr_swiglu_fwd.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp]
     lib.ebr_swiglu_bwd.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp, vp]
+    lib.ebr_swiglu_bwd2.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp, vp, vp, vp]
+    lib.ebr_rms_norm_bwd2.argtypes = [ctypes.c_int, i64, i64, vp, fp, vp, vp, vp, vp, vp]
     lib.ebr_gate_up_swiglu.argtypes = [ctypes.c_int, i64, i64, i64, vp, i64, vp, vp, vp, vp]
     lib.ebr_descent_step.argtypes = [ctypes.c_int, i64, i64, dbl, dbl, vp, vp, vp, fp, sz, vp]
     lib.ebr_descent_step_scratch_floats.argtypes = [i64, i64]

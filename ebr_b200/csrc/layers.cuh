@@ -380,6 +380,58 @@ __global__ void __launch_bounds__(kThreads) rms_norm_bwd_kernel(int64_t rows, in
   }
 }
 
+// The double backward of rms_norm, for a graph built through the backward above (second-order training). With
+// n = C, r = rstd (a function of s: dr/ds_k = -r^3 s_k / n), gs = r (g - xh mean(g xh)), xh = s r, and the
+// upstream gradient u = dL/dgs, the row sums U_g = sum u g, U_s = sum u s, G = sum g s give
+//   dL/dg_k = r u_k - (r^3 / n) s_k U_s,
+//   dL/ds_k = (r^3 / n) (-s_k U_g + 3 r^2 s_k G U_s / n - G u_k - g_k U_s).
+// One warp per row, two passes; fp32 throughout and one rounding to the I/O type per output.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) rms_norm_bwd2_kernel(int64_t rows, int C_, const T* __restrict__ s,
+                                                                 const float* __restrict__ rstd,
+                                                                 const T* __restrict__ gy, const T* __restrict__ u,
+                                                                 T* __restrict__ ds, T* __restrict__ dgy) {
+  using C = typename Elem<T>::C;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = grid_stride() >> 5;
+  for (int64_t row = global_tid() >> 5; row < rows; row += warps) {
+    const int64_t base = row * C_;
+    const C r = static_cast<C>(rstd[row]);
+    C ug = 0, us = 0, gs_ = 0;
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V], g[V], uu[V];
+      load_c<T, V>(s + base + c, xs);
+      load_c<T, V>(gy + base + c, g);
+      load_c<T, V>(u + base + c, uu);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        ug += uu[e] * g[e];
+        us += uu[e] * xs[e];
+        gs_ += g[e] * xs[e];
+      }
+    }
+    ug = warp_sum(ug);
+    us = warp_sum(us);
+    gs_ = warp_sum(gs_);
+    const C n = static_cast<C>(C_);
+    const C r3n = r * r * r / n;
+    const C k3 = C(3) * r * r * gs_ * us / n;
+    for (int c = lane * V; c < C_; c += 32 * V) {
+      C xs[V], g[V], uu[V], o_s[V], o_g[V];
+      load_c<T, V>(s + base + c, xs);
+      load_c<T, V>(gy + base + c, g);
+      load_c<T, V>(u + base + c, uu);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        o_s[e] = r3n * (xs[e] * (k3 - ug) - gs_ * uu[e] - g[e] * us);
+        o_g[e] = r * uu[e] - r3n * xs[e] * us;
+      }
+      store_c<T, V>(ds + base + c, o_s);
+      store_c<T, V>(dgy + base + c, o_g);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ SwiGLU
 
 template <typename C>
@@ -426,6 +478,43 @@ __global__ void __launch_bounds__(kThreads) swiglu_bwd_kernel(int64_t rows, int6
     }
     store_c<T, V>(gh + r * 2 * I + j, dg);
     store_c<T, V>(gh + r * 2 * I + I + j, du);
+  }
+}
+
+// The double backward of swiglu_bwd, for a graph built through it (second-order training). swiglu_bwd gives
+// dg = da s1 (da = round(gout up), s1 = silu'(g) = sg (1 + g (1 - sg)), sg = sigmoid(g)) and du = gout act
+// (act = round(silu(g))); with the upstream gradients ug = dL/d(dg), uu = dL/d(du) and s2 = silu''(g) =
+// sg (1 - sg) (2 + g (1 - 2 sg)):
+//   dL/dgout = ug up s1 + uu act,   dL/dup = ug gout s1,   dL/dg = ug da s2 + uu gout s1.
+// The roundings of da and act are taken as the identity in the derivative, as autograd does for a cast.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) swiglu_bwd2_kernel(int64_t rows, int64_t I, const T* __restrict__ h,
+                                                               const T* __restrict__ gout, const T* __restrict__ u,
+                                                               T* __restrict__ dh, T* __restrict__ dgout) {
+  using C = typename Elem<T>::C;
+  const int64_t cpr = I / V, total = rows * cpr;
+  for (int64_t i = global_tid(); i < total; i += grid_stride()) {
+    const int64_t r = i / cpr, j = (i - r * cpr) * V;
+    C g[V], up[V], go[V], ug[V], uu[V], o_g[V], o_u[V], o_go[V];
+    load_c<T, V>(h + r * 2 * I + j, g);
+    load_c<T, V>(h + r * 2 * I + I + j, up);
+    load_c<T, V>(gout + r * I + j, go);
+    load_c<T, V>(u + r * 2 * I + j, ug);
+    load_c<T, V>(u + r * 2 * I + I + j, uu);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const C sg = C(1) / (C(1) + exp_c(-g[e]));
+      const C s1 = sg * (C(1) + g[e] * (C(1) - sg));
+      const C s2 = sg * (C(1) - sg) * (C(2) + g[e] * (C(1) - C(2) * sg));
+      const C act = rnd<T>(silu_c(g[e]));
+      const C da = rnd<T>(mul_rn(go[e], up[e]));
+      o_go[e] = ug[e] * up[e] * s1 + uu[e] * act;
+      o_u[e] = ug[e] * go[e] * s1;
+      o_g[e] = ug[e] * da * s2 + uu[e] * go[e] * s1;
+    }
+    store_c<T, V>(dh + r * 2 * I + j, o_g);
+    store_c<T, V>(dh + r * 2 * I + I + j, o_u);
+    store_c<T, V>(dgout + r * I + j, o_go);
   }
 }
 

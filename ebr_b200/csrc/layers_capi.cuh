@@ -253,6 +253,58 @@ int ebr_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* h, void* out,
   });
 }
 
+int ebr_rms_norm_bwd2(int dtype, int64_t rows, int64_t C, const void* s, const float* rstd, const void* gy,
+                      const void* u, void* ds, void* dgy, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || C < 1 || C > (1 << 20)) return set_error(EBR_ERR_SHAPE, "rms_norm_bwd2: bad rows / row length%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!s || !rstd || !gy || !u || !ds || !dgy) return set_error(EBR_ERR_NULL, "rms_norm_bwd2: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    const dim3 grid = flat_grid(device, rows * 32);
+    auto go = [&](auto kernel) {
+      kernel<<<grid, kThreads, 0, st>>>(rows, static_cast<int>(C), static_cast<const T*>(s), rstd,
+                                        static_cast<const T*>(gy), static_cast<const T*>(u), static_cast<T*>(ds),
+                                        static_cast<T*>(dgy));
+    };
+    if (C % V == 0 && all_aligned16({s, gy, u, ds, dgy}))
+      go(ebr::layers::rms_norm_bwd2_kernel<T, V>);
+    else
+      go(ebr::layers::rms_norm_bwd2_kernel<T, 1>);
+    return check_launch("rms_norm_bwd2");
+  });
+}
+
+int ebr_swiglu_bwd2(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, const void* u, void* dh,
+                    void* dgout, void* stream) {
+  int rc = check_layer_dtype(dtype, false);
+  if (rc != EBR_OK) return rc;
+  if (rows < 0 || I < 1) return set_error(EBR_ERR_SHAPE, "swiglu_bwd2: bad rows / width%s%s");
+  if (rows == 0) return EBR_OK;
+  if (!h || !gout || !u || !dh || !dgout) return set_error(EBR_ERR_NULL, "swiglu_bwd2: NULL pointer%s%s");
+  int device = 0;
+  if ((rc = check_device(&device)) != EBR_OK) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
+  return with_type(dtype, [&](auto* tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    constexpr int V = vec_width<T>();
+    if (I % V == 0 && all_aligned16({h, gout, u, dh, dgout}))
+      ebr::layers::swiglu_bwd2_kernel<T, V><<<flat_grid(device, rows * (I / V)), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<const T*>(gout), static_cast<const T*>(u),
+          static_cast<T*>(dh), static_cast<T*>(dgout));
+    else
+      ebr::layers::swiglu_bwd2_kernel<T, 1><<<flat_grid(device, rows * I), kThreads, 0, st>>>(
+          rows, I, static_cast<const T*>(h), static_cast<const T*>(gout), static_cast<const T*>(u),
+          static_cast<T*>(dh), static_cast<T*>(dgout));
+    return check_launch("swiglu_bwd2");
+  });
+}
+
 int ebr_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, void* gh, void* stream) {
   int rc = check_layer_dtype(dtype, false);
   if (rc != EBR_OK) return rc;

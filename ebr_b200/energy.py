@@ -246,7 +246,7 @@ class LatentEnergyNet(nn.Module):
                 v = fl.noisy_point(z, torch.randn_like(z) if sigma else None, float(sigma), s.eps)
             e, g = self.energy_and_grad(v, x)
             return fl.step_and_project(v, g, float(alpha), s.eps), e.detach()
-        v = cell_unit_rms(z, s.eps)
+        v = fl.add_rms_norm(z, None, s.eps)  # cell_unit_rms as one kernel, differentiable to second order
         if noise is not None:
             v = v + noise.to(v.dtype)
         elif sigma:

@@ -23,6 +23,7 @@ from typing import Optional, Tuple
 
 import torch
 import torch.nn.functional as F
+from torch.autograd.function import once_differentiable
 from torch.autograd.graph import get_gradient_edge
 
 from ebr_b200 import _native
@@ -443,14 +444,43 @@ def _rows(x: Tensor) -> Tuple[int, int]:
     return x.numel() // c if c else 0, c
 
 
-def _rms_norm_bwd_graph(x: Tensor, a: Optional[Tensor], gy: Tensor, eps: float) -> Tensor:
-    """The backward of rms_norm(x + a) as differentiable torch ops (for create_graph)."""
-    s = x if a is None else x + a
-    xf = s.to(torch.float32)
-    r = torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
-    xh = xf * r
-    g = gy.to(torch.float32)
-    return (r * (g - xh * (g * xh).mean(-1, keepdim=True))).to(x.dtype)
+def _rms_norm_bwd_kernel(s: Tensor, rstd: Tensor, gy: Tensor) -> Tensor:
+    gy = gy.to(s.dtype).contiguous()
+    rows, c = _rows(s)
+    gs = torch.empty_like(s)
+    _native.check(
+        _native.lib().ebr_rms_norm_bwd(_DTYPES[s.dtype], rows, c, s.data_ptr(), rstd.data_ptr(), gy.data_ptr(),
+                                       gs.data_ptr(), _stream()),  # fmt: skip
+        "rms_norm_bwd",
+    )
+    return gs
+
+
+class _RmsNormBwd(torch.autograd.Function):
+    """The rms_norm backward gs = r (gy - xh mean(gy xh)) as one kernel, differentiable once more by the closed-form
+    double backward (``ebr_rms_norm_bwd2``): the graph a second-order training step builds through it. ``x`` / ``a``
+    only carry the graph (s = x + a was formed by the forward kernel); ds is the gradient of both."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, a: Optional[Tensor], s: Tensor, rstd: Tensor, gy: Tensor) -> Tensor:
+        gy = gy.to(s.dtype).contiguous()
+        ctx.save_for_backward(s, rstd, gy)
+        ctx.has_a = a is not None
+        return _rms_norm_bwd_kernel(s, rstd, gy)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, u: Tensor):
+        s, rstd, gy = ctx.saved_tensors
+        u = u.to(s.dtype).contiguous()
+        rows, c = _rows(s)
+        ds, dgy = torch.empty_like(s), torch.empty_like(s)
+        _native.check(
+            _native.lib().ebr_rms_norm_bwd2(_DTYPES[s.dtype], rows, c, s.data_ptr(), rstd.data_ptr(), gy.data_ptr(),
+                                            u.data_ptr(), ds.data_ptr(), dgy.data_ptr(), _stream()),  # fmt: skip
+            "rms_norm_bwd2",
+        )
+        return ds, (ds if ctx.has_a else None), None, None, dgy
 
 
 class _AddRMSNorm(torch.autograd.Function):
@@ -477,22 +507,16 @@ class _AddRMSNorm(torch.autograd.Function):
     def backward(ctx, gy: Tensor):
         x, a, s, rstd = ctx.saved_tensors
         if torch.is_grad_enabled():
-            gs = _rms_norm_bwd_graph(x, a, gy, ctx.eps)
+            gs = _RmsNormBwd.apply(x, a, s, rstd, gy)  # a graph for the double backward
         else:
-            gy = gy.to(x.dtype).contiguous()
-            rows, c = _rows(x)
-            gs = torch.empty_like(x)
-            _native.check(
-                _native.lib().ebr_rms_norm_bwd(_DTYPES[x.dtype], rows, c, s.data_ptr(), rstd.data_ptr(),
-                                               gy.data_ptr(), gs.data_ptr(), _stream()),  # fmt: skip
-                "rms_norm_bwd",
-            )
+            gs = _rms_norm_bwd_kernel(s, rstd, gy)
         return gs, (gs if ctx.has_a else None), None
 
 
 def add_rms_norm(x: Tensor, a: Optional[Tensor] = None, eps: float = 1e-5) -> Tensor:
     """``rms_norm(x + a)`` (``a`` optional): the residual add rounded to the I/O type, then the row norm in float32
-    (``models/layers.py:37-42``). Differentiable; the double backward goes through torch ops."""
+    (``models/layers.py:37-42``). Differentiable to second order: the backward and its own backward are fused
+    kernels."""
     return _AddRMSNorm.apply(x, a, float(eps))
 
 
@@ -520,16 +544,7 @@ class _SwiGLUAct(torch.autograd.Function):
         return _swiglu_grad(h, gout)
 
 
-def _swiglu_grad(h: Tensor, gout: Tensor) -> Tensor:
-    """d act / d h applied to gout: the fused kernel, or (building a higher-order graph) differentiable torch ops."""
-    if torch.is_grad_enabled():
-        # Differentiable torch ops (aten's silu_backward has no derivative of its own).
-        gate, up = h.chunk(2, dim=-1)
-        gf = gate.to(torch.float32)
-        sg = torch.sigmoid(gf)
-        ga = (gout * up).to(torch.float32)
-        gg = (ga * sg * (1.0 + gf * (1.0 - sg))).to(h.dtype)
-        return torch.cat([gg, gout * F.silu(gate)], dim=-1)
+def _swiglu_bwd_kernel(h: Tensor, gout: Tensor) -> Tensor:
     gout = gout.to(h.dtype).contiguous()
     rows, c2 = _rows(h)
     gh = torch.empty_like(h)
@@ -539,6 +554,39 @@ def _swiglu_grad(h: Tensor, gout: Tensor) -> Tensor:
         "swiglu_bwd",
     )
     return gh
+
+
+class _SwigluBwd(torch.autograd.Function):
+    """d act / d h applied to gout as one kernel, differentiable once more by the closed-form double backward
+    (``ebr_swiglu_bwd2``): the graph a second-order training step builds through it."""
+
+    @staticmethod
+    def forward(ctx, h: Tensor, gout: Tensor) -> Tensor:
+        h = h.contiguous()
+        gout = gout.to(h.dtype).contiguous()
+        ctx.save_for_backward(h, gout)
+        return _swiglu_bwd_kernel(h, gout)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, u: Tensor):
+        h, gout = ctx.saved_tensors
+        u = u.to(h.dtype).contiguous()
+        rows, c2 = _rows(h)
+        dh, dgout = torch.empty_like(h), torch.empty_like(gout)
+        _native.check(
+            _native.lib().ebr_swiglu_bwd2(_DTYPES[h.dtype], rows, c2 // 2, h.data_ptr(), gout.data_ptr(), u.data_ptr(),
+                                          dh.data_ptr(), dgout.data_ptr(), _stream()),  # fmt: skip
+            "swiglu_bwd2",
+        )
+        return dh, dgout
+
+
+def _swiglu_grad(h: Tensor, gout: Tensor) -> Tensor:
+    """d act / d h applied to gout: the fused kernel, differentiable once more when a higher-order graph is built."""
+    if torch.is_grad_enabled():
+        return _SwigluBwd.apply(h, gout)
+    return _swiglu_bwd_kernel(h.contiguous(), gout)
 
 
 @torch.library.custom_op("ebr_fused::gate_up_swiglu", mutates_args=())

@@ -86,6 +86,12 @@ int ebr_add_rms_norm(int dtype, int64_t rows, int64_t C, double eps, const void*
 int ebr_rms_norm_bwd(int dtype, int64_t rows, int64_t C, const void* s, const float* rstd, const void* gy, void* gs,
                      void* stream);
 
+/* Double backward of ebr_rms_norm_bwd, for second-order training: given the upstream gradient u of gs, with n = C,
+ * r = rstd and the row sums U_g = sum u gy, U_s = sum u s, G = sum gy s: dgy = r u - (r^3 / n) s U_s and
+ * ds = (r^3 / n) (-s U_g + 3 r^2 s G U_s / n - G u - gy U_s) (ds is the gradient of both x and a). */
+int ebr_rms_norm_bwd2(int dtype, int64_t rows, int64_t C, const void* s, const float* rstd, const void* gy,
+                      const void* u, void* ds, void* dgy, void* stream);
+
 /* SwiGLU activation over rows of 2 I: out[r, j] = round(round(silu(h[r, j])) * h[r, I + j]), out [rows, I].
  * Replaces: F.silu(gate) * up after gate_up_proj(x).chunk(2) (models/layers.py:82-84). */
 int ebr_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* h, void* out, void* stream);
@@ -101,6 +107,12 @@ int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void
 
 /* Its backward: gh [rows, 2 I] = (silu'(gate) * round(gout * up), round(gout * round(silu(gate)))). */
 int ebr_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, void* gh, void* stream);
+
+/* Double backward of ebr_swiglu_bwd, for second-order training (a graph built through the backward): given the
+ * upstream gradient u [rows, 2 I] of gh, dh [rows, 2 I] = (u_g da s2 + u_u gout s1, u_g gout s1) and dgout [rows, I]
+ * = u_g up s1 + u_u act, with s1 = silu'(gate), s2 = silu''(gate), da = round(gout up), act = round(silu(gate)). */
+int ebr_swiglu_bwd2(int dtype, int64_t rows, int64_t I, const void* h, const void* gout, const void* u, void* dh,
+                    void* dgout, void* stream);
 
 /* One descent step and projection, z' = sphere(v - alpha * g) over rows of `row_elems` elements (a whole board:
  * N * C): u = round(v - round(alpha * g)), z' = round(u / max(sqrt(mean(u^2)), eps)). `partial` is float32 scratch
