@@ -300,13 +300,70 @@ def stablemax_cross_entropy(logits: Tensor, labels: Tensor) -> Tensor:
     return -logp.gather(-1, labels.long().unsqueeze(-1)).squeeze(-1)
 
 
+class MicrostepGraph:
+    """One no-graph descent microstep of a fixed batch shape, captured once as a CUDA graph and then replayed.
+
+    Training rollouts -- a segment's ungraded prefix, forward SXM's candidate trajectories -- run a few hundred rows
+    of 81-100 tokens: every microstep is a few hundred kernels of a few microseconds each, and launched one by one from
+    Python their host cost exceeds their GPU time. A replay issues the whole microstep (forward, dE/dv, step) as one
+    graph launch. The graph reads the parameters in place (the optimizer updates them in place), so one capture serves
+    every training step. ``step`` copies its inputs into the graph's buffers and returns the graph's output tensor,
+    which the next replay overwrites. Noise is an input (drawn by the caller), so the graph consumes no random
+    numbers."""
+
+    def __init__(self, net: LatentEnergyNet, z: Tensor, x: Tensor, alpha) -> None:
+        self.net = net
+        self.z, self.x = z.detach().clone(), x.detach().clone()
+        self.noise = torch.zeros_like(self.z)
+        self.alpha = alpha.detach().clone() if torch.is_tensor(alpha) else alpha
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(2):  # first launches outside the capture (kernel attributes, the allocator's pool)
+                self._run()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.out = self._run()
+
+    def _run(self) -> Tensor:
+        z_next, _ = self.net.microstep(self.z, self.x, noise=self.noise, sigma=0.0, alpha=self.alpha)
+        return z_next
+
+    def step(self, z: Tensor, x: Tensor, noise: Tensor, alpha=None) -> Tensor:
+        self.z.copy_(z)
+        self.x.copy_(x)
+        self.noise.copy_(noise)
+        if torch.is_tensor(self.alpha):
+            self.alpha.copy_(alpha)
+        self.graph.replay()
+        return self.out
+
+
+def graphed_microstep(net: LatentEnergyNet, z: Tensor, x: Tensor, noise: Tensor, alpha=None) -> Tensor:
+    """``net.microstep(z, x, noise=noise, sigma=0, alpha=alpha)[0]`` without a graph, through the net's cached
+    ``MicrostepGraph`` for this shape (captured on first use). The result is the graph's buffer: clone it to keep it
+    past the next graphed microstep of the same shape."""
+    alpha = net.shape.step_size if alpha is None else alpha
+    key = (tuple(z.shape), z.dtype, tuple(x.shape), tuple(alpha.shape) if torch.is_tensor(alpha) else float(alpha))
+    cache = net.__dict__.setdefault("_microstep_graphs", {})
+    graph = cache.get(key)
+    if graph is None:
+        graph = cache[key] = MicrostepGraph(net, z, x, alpha)
+    return graph.step(z, x, noise, alpha)
+
+
 def train_segment_loss(net: LatentEnergyNet, z: Tensor, x: Tensor, labels: Tensor, prefix: int, graded: int,
                        alpha=None) -> Tensor:  # fmt: skip
     """A training segment: ``prefix`` microsteps without a graph, then ``graded`` with ``create_graph=True`` (so the
     backward runs the attention's double backward), and the mean stablemax cross entropy of the decoded endpoint
     against ``labels`` (``models/energy.py:582-636`` rollout, ``models/losses.py`` loss)."""
-    for _ in range(prefix):
-        z, _ = net.microstep(z, x, alpha=alpha)
+    sigma = net.shape.noise_scale
+    with torch.no_grad():
+        for _ in range(prefix):
+            noise = torch.randn_like(z) * sigma if sigma else torch.zeros_like(z)
+            z = graphed_microstep(net, z, x, noise, alpha)
+        z = z.clone()
     for _ in range(graded):
         z, _ = net.microstep(z, x, graded=True, alpha=alpha)
     return stablemax_cross_entropy(net.decode(z), labels).mean()
@@ -334,8 +391,9 @@ def sxm_explore_loss(net: LatentEnergyNet, z: Tensor, challengers: Tensor, x: Te
         zc, start = cand, cand
         for t in range(steps):
             if t == prefix:
-                start = zc
-            zc, _ = net.microstep(zc, xk, noise=None if noise is None else noise[t], sigma=0.0, alpha=alpha)
+                start = zc.clone()
+            zc = graphed_microstep(net, zc, xk, torch.zeros_like(cand) if noise is None else noise[t], alpha)
+        zc = zc.clone()
         per_row = stablemax_cross_entropy(net.decode(zc), lk).mean(-1).view(k, b)
         order = per_row.argsort(dim=0)  # best candidate first, per input
     rows = torch.arange(b, device=z.device)
@@ -355,6 +413,7 @@ __all__ = [
     "board_unit_rms",
     "cell_unit_rms",
     "descend",
+    "graphed_microstep",
     "lowest_energy_pick",
     "rope_tables",
     "stablemax_cross_entropy",
