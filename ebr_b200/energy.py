@@ -323,7 +323,8 @@ class MicrostepGraph:
                 self._run()
         torch.cuda.current_stream().wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.no_grad(), torch.cuda.graph(self.graph):
+        # thread_local: CUDA calls of other threads (NCCL's, under torchrun) do not invalidate this capture
+        with torch.no_grad(), torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
             self.out = self._run()
 
     def _run(self) -> Tensor:
