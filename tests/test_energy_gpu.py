@@ -296,3 +296,33 @@ def test_sxm_explore_keeps_each_inputs_best_candidate():
     for n, p in net.named_parameters():
         assert p.grad is not None and torch.isfinite(p.grad).all(), n
     assert net.blocks[0].log_temp.grad.abs().sum() > 0
+
+
+def test_graphed_microstep_equals_the_eager_one():
+    """The CUDA-graph microstep of training rollouts (captured once per batch shape) gives the eager microstep's result
+    on every replay with new inputs -- equal elements but for a GEMM that cuBLAS may plan differently on the capture
+    stream -- for a per-row step-size tensor (the torch path of training) and a float step (the fused path), and reads
+    the parameters in place (an optimizer's update is seen)."""
+
+    def same(a, b):
+        return float((a != b).double().mean()) < 0.01 and float((a.float() - b.float()).norm() / b.float().norm()) < 1e-2
+
+    from ebr_b200.energy import LatentEnergyNet, NetShape, graphed_microstep
+
+    net = LatentEnergyNet(NetShape(board=(9, 9), vocab=10, layers=2)).cuda()
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    rows = 6
+    x = net.embed(torch.randint(0, 10, (rows, 81), generator=gen, device="cuda"))
+    for alpha in (torch.full((rows, 1, 1), 230.0, device="cuda"), 250.0):
+        for rep in range(3):
+            z = net.fresh_states(rows, gen)
+            noise = torch.randn(z.shape, generator=gen, device="cuda").to(z.dtype) * 0.05
+            with torch.no_grad():
+                got = graphed_microstep(net, z, x, noise, alpha).clone()
+                want, _ = net.microstep(z, x, noise=noise, sigma=0.0, alpha=alpha)
+            assert same(got, want), (alpha if not torch.is_tensor(alpha) else "tensor", rep)
+        with torch.no_grad():
+            net.blocks[0].w_qkv.mul_(1.5)  # an in-place parameter update (a stale read would differ everywhere)
+            got = graphed_microstep(net, z, x, noise, alpha).clone()
+            want, _ = net.microstep(z, x, noise=noise, sigma=0.0, alpha=alpha)
+        assert same(got, want)
