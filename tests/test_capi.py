@@ -89,6 +89,23 @@ def test_layer_entry_points_reject_bad_arguments_before_device(lib):
     assert gu(_native.BFLOAT16, 4, 64, 128, t, 60, t, t, t, None) == _native.ERR_STRIDE
     assert gu(_native.BFLOAT16, 0, 64, 128, None, 64, None, None, None, None) == 0
     assert lib.ebr_add_rms_norm(_native.BFLOAT16, 0, 8, 1e-5, None, None, None, None, None, None, 0.0, None) == 0
+    # The qkv input gradient with the merge in the GEMM: 16-bit only, D = 64 and C = 512, aligned operands.
+    md = lib.ebr_qkv_rope_merge_dx
+    g8 = _op(t, 8 * 4 * 64, 4 * 64, 64)  # [1, 8, 4, 64] contiguous
+    assert md(_native.FLOAT32, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_DTYPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 128, 512, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_SHAPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 256, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_SHAPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), None, t, t, None, t, None) == _native.ERR_NULL
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t + 2, t, t, None, t, None) == _native.ERR_STRIDE
+    assert md(_native.BFLOAT16, 0, 4, 8, 64, 512, None, None, None, None, None, None, None, None, None) == 0
+    # The double backwards of rms_norm and SwiGLU: layer dtypes only, a row length, every buffer.
+    assert lib.ebr_rms_norm_bwd2(_native.FLOAT64, 4, 8, t, t, t, t, t, t, None) == _native.ERR_DTYPE
+    assert lib.ebr_rms_norm_bwd2(_native.BFLOAT16, 4, 0, t, t, t, t, t, t, None) == _native.ERR_SHAPE
+    assert lib.ebr_rms_norm_bwd2(_native.BFLOAT16, 4, 8, t, t, t, None, t, t, None) == _native.ERR_NULL
+    assert lib.ebr_rms_norm_bwd2(_native.BFLOAT16, 0, 8, None, None, None, None, None, None, None) == 0
+    assert lib.ebr_swiglu_bwd2(_native.BFLOAT16, 4, 0, t, t, t, t, t, None) == _native.ERR_SHAPE
+    assert lib.ebr_swiglu_bwd2(_native.BFLOAT16, 4, 8, t, t, t, t, None, None) == _native.ERR_NULL
+    assert lib.ebr_swiglu_bwd2(_native.BFLOAT16, 0, 8, None, None, None, None, None, None) == 0
 
 
 def _op(ptr=0x1000, sb=0, sh=0, sn=64):
