@@ -108,7 +108,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.ebr_rope_merge.argtypes = dims + [op, op, op, fp, fp, fp, vp, vp]
     lib.ebr_qkv_rope_split.argtypes = dims + [i64, vp, i64, vp, fp, fp, fp, vp, vp, vp, vp]
     lib.ebr_o_proj.argtypes = dims + [i64, op, vp, vp, vp]
-    lib.ebr_qkv_rope_merge_dx.argtypes = dims + [i64, op, op, op, vp, fp, fp, fp, vp, vp]
+    lib.ebr_qkv_rope_merge_dx.argtypes = dims + [i64, op, op, op, vp, fp, fp, fp, vp, vp, vp]
     lib.ebr_add_rms_norm.argtypes = [ctypes.c_int, i64, i64, dbl, vp, vp, vp, vp, fp, vp, dbl, vp]
     lib.ebr_rms_norm_bwd.argtypes = [ctypes.c_int, i64, i64, vp, fp, vp, vp, vp]
     lib.ebr_swiglu_fwd.argtypes = [ctypes.c_int, i64, i64, vp, vp, vp]

@@ -454,7 +454,7 @@ int ebr_o_proj(int dtype, int64_t B, int64_t H, int64_t N, int64_t D, int64_t C_
 
 int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, int64_t C, const ebr_operand* dq,
                           const ebr_operand* dk, const ebr_operand* dv, const void* w, const float* cos_table,
-                          const float* sin_table, const float* qscale, void* dx, void* stream) {
+                          const float* sin_table, const float* qscale, const void* addend, void* dx, void* stream) {
   using L = ebr::MergeGemmLayout;
   if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
     return set_error(EBR_ERR_DTYPE, "qkv_rope_merge_dx: bfloat16 or float16 only%s%s");
@@ -467,7 +467,7 @@ int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
   if (rc != EBR_OK) return rc;
   if (!w || !dx || !cos_table || !sin_table) return set_error(EBR_ERR_NULL, "qkv_rope_merge_dx: NULL pointer%s%s");
   if (!tc_operand_ok(dq, B, H, N) || !tc_operand_ok(dk, B, H, N) || !tc_operand_ok(dv, B, H, N) ||
-      !all_aligned16({w, dx, cos_table, sin_table}))
+      !all_aligned16({w, dx, cos_table, sin_table, addend}))
     return set_error(EBR_ERR_STRIDE, "qkv_rope_merge_dx: 16-byte aligned data and strides needed%s%s");
   int device = 0;
   if ((rc = check_device(&device)) != EBR_OK) return rc;
@@ -486,7 +486,7 @@ int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
       return rc;
     kernel<<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, tw, static_cast<int>(B), static_cast<int>(H),
                                                 static_cast<int>(N), cos_table, sin_table, qscale,
-                                                static_cast<T*>(dx));
+                                                static_cast<const T*>(addend), static_cast<T*>(dx));
     return check_launch("tc_merge_gemm_kernel");
   };
   if (dtype == EBR_BFLOAT16)

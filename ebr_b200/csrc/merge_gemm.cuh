@@ -79,13 +79,15 @@ __device__ __forceinline__ void merge_rotate_row(unsigned char* tile, int r, int
 }
 
 // tq / tk / tv: 4-D TMA maps over dq / dk / dv (D, N, H, B), box 64 x 128; tw: W [3 H D, C] (box 64 columns x 64
-// rows); dx: [B, N, C]. cos / sin: fp32 [N, D]; qscale: NULL or fp32 [H].
+// rows); dx: [B, N, C]. cos / sin: fp32 [N, D]; qscale: NULL or fp32 [H]. addend: NULL or [B, N, C]: then
+// dx = round(round(merge W) + addend), the value a separate add of the two 16-bit tensors gives (a block input's
+// residual gradient joined to its qkv-projection gradient).
 template <typename T>
 __global__ void __launch_bounds__(320, 1)
     tc_merge_gemm_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tw, int B, int H,
                          int N, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                         const float* __restrict__ qscale, T* __restrict__ dx) {
+                         const float* __restrict__ qscale, const T* __restrict__ addend, T* __restrict__ dx) {
   using L = MergeGemmLayout;
   constexpr int NA = L::kAStages, NB = L::kBStages, D = 64;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -221,7 +223,9 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) break;
       tc_fence_after();
       const int row = nb * L::kBM + wq * 32 + lane;
-      T* out = row < N ? dx + (static_cast<int64_t>(b) * N + row) * L::kC + half * L::kBN : nullptr;
+      const int64_t orow = (static_cast<int64_t>(b) * N + row) * L::kC + half * L::kBN;
+      T* out = row < N ? dx + orow : nullptr;
+      const T* add = (row < N && addend) ? addend + orow : nullptr;
       const uint32_t tacc = tmem + (static_cast<uint32_t>(wq * 32) << 16) + half * 256;
 #pragma unroll 1
       for (int c = 0; c < L::kBN; c += 32) {
@@ -230,12 +234,20 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_ld_regs(v);
         if (out) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(out + c + 8 * q) =
-                make_uint4(pack2<T>(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])),
-                           pack2<T>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
-                           pack2<T>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
-                           pack2<T>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[e] = pack2<T>(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+            if (add) {
+              const uint4 a = *reinterpret_cast<const uint4*>(add + c + 8 * q);
+              const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w[e] = pack2<T>(layers::add_rn(unpack_lo<T>(w[e]), unpack_lo<T>(aw[e])),
+                                layers::add_rn(unpack_hi<T>(w[e]), unpack_hi<T>(aw[e])));
+            }
+            *reinterpret_cast<uint4*>(out + c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
         }
       }
       tc_fence_before();

@@ -219,13 +219,64 @@ class LatentEnergyNet(nn.Module):
         return cell.float().squeeze(-1).sum(dim=1)
 
     def energy_and_grad(self, v: Tensor, x: Tensor, create_graph: bool = False) -> tuple[Tensor, Tensor]:
-        """(E per row, dE/dv); with ``create_graph`` the gradient is itself differentiable (double backward)."""
+        """(E per row, dE/dv); with ``create_graph`` the gradient is itself differentiable (double backward). Without
+        it, on the shapes every fused kernel takes, the blocks' backward runs explicitly (``_energy_and_grad_dz``)."""
+        if not create_graph and self._dz_fusable(v):
+            return self._energy_and_grad_dz(v, x)
         with torch.enable_grad():
             if not v.requires_grad:
                 v = v.detach().requires_grad_(True)
             e = self.energy(v, x, graded=create_graph)
             (g,) = torch.autograd.grad(e.sum(), v, create_graph=create_graph)
         return (e if create_graph else e.detach()), g
+
+    def _dz_fusable(self, v: Tensor) -> bool:
+        """Whether the explicit dE/dv path serves this call: the default attention, 16-bit CUDA activations, head dim 64
+        and hidden 512 (the shapes of the merge GEMM; the other fused kernels take them too)."""
+        s = self.shape
+        return (self._attention is None and v.is_cuda and v.dtype in (torch.bfloat16, torch.float16)
+                and s.head_dim == 64 and s.hidden == 512 and (2 * s.mlp_width) % 256 == 0)  # fmt: skip
+
+    def _energy_and_grad_dz(self, v: Tensor, x: Tensor) -> tuple[Tensor, Tensor]:
+        """(E, dE/dv) with the blocks' backward run explicitly, not through autograd. Each block's forward runs the same
+        fused ops as ``_block`` and keeps what its backward needs; the backward then runs the fused kernels in reverse.
+        A block input's residual gradient joins its branch gradient inside a product instead of a separate add:
+        through the merge GEMM's addend at the attention input (rounded as the add would be) and cuBLAS's beta = 1
+        accumulate at the MLP input (one rounding instead of two). Only dE/dv: no parameter gradients."""
+        s, dt = self.shape, v.dtype
+        b, n, c = v.shape
+        hh, d = s.heads, s.head_dim
+        scale = d**-0.5
+        saved = []
+        with torch.no_grad():
+            h = v + x
+            for blk in self.blocks:
+                folded = blk.log_temp.detach().exp().to(dt)
+                w_qkv, w_out, w_gu, w_down = (w.detach().to(dt) for w in (blk.w_qkv, blk.w_out, blk.w_gate_up,
+                                                                              blk.w_down))  # fmt: skip
+                q, k, vv = fl.qkv_rope_split_op(h, w_qkv, self.rope_cos, self.rope_sin, folded, hh)
+                o, lse = torch.ops.ebr_fused.attn_fwd(q, k, vv, scale)
+                h1, s1, r1 = fl.add_rms_norm_fwd(h, fl.o_proj_op(o, w_out), s.eps)
+                gu, act = fl.gate_up_swiglu_op(h1, w_gu)
+                h, s2, r2 = fl.add_rms_norm_fwd(h1, F.linear(act, w_down), s.eps)
+                saved.append((q, k, vv, o, lse, s1, r1, gu, s2, r2, w_qkv, w_out, w_gu, w_down, folded))
+        with torch.enable_grad():  # the energy head (small): autograd
+            hd = h.detach().requires_grad_(True)
+            cell = F.linear(F.silu(F.linear(hd, self.cell_w1.to(dt), self.cell_b1.to(dt))), self.cell_w2.to(dt))
+            if s.cell_softplus:
+                cell = F.softplus(cell.float())
+            e = cell.float().squeeze(-1).sum(dim=1)
+            (g,) = torch.autograd.grad(e.sum(), hd)
+        with torch.no_grad():
+            for q, k, vv, o, lse, s1, r1, gu, s2, r2, w_qkv, w_out, w_gu, w_down, folded in reversed(saved):
+                ds2 = fl.rms_norm_bwd(s2, r2, g)
+                d_gu = fl.swiglu_bwd(gu, ds2 @ w_down)
+                g1 = torch.addmm(ds2.reshape(-1, c), d_gu.reshape(-1, d_gu.shape[-1]), w_gu).view(b, n, c)
+                ds1 = fl.rms_norm_bwd(s1, r1, g1)
+                d_o = (ds1 @ w_out).view(b, n, hh, d).transpose(1, 2)
+                dq, dk, dv = torch.ops.ebr_fused.attn_bwd(q, k, vv, o, lse, d_o, scale)
+                g = fl.qkv_rope_merge_dx_op(dq, dk, dv, w_qkv, self.rope_cos, self.rope_sin, folded, ds1)
+        return e.detach(), g
 
     # -- descent ----------------------------------------------------------------------------------------------------
 

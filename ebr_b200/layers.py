@@ -251,9 +251,10 @@ def _engine_needs(node) -> bool:
 
 @torch.library.custom_op("ebr_fused::qkv_rope_merge_dx", mutates_args=())
 def qkv_rope_merge_dx_op(dq: Tensor, dk: Tensor, dv: Tensor, weight: Tensor, cos: Tensor, sin: Tensor,
-                         qscale: Tensor) -> Tensor:  # fmt: skip
-    """``rope_merge(dq, dk, dv, cos, sin, qscale) @ weight`` as one tensor-core GEMM whose A operand is merged in shared
-    memory (``ebr_qkv_rope_merge_dx``): the input gradient of the qkv projection. Shapes ``merge_dx_fusable`` takes."""
+                         qscale: Tensor, addend: Optional[Tensor] = None) -> Tensor:  # fmt: skip
+    """``rope_merge(dq, dk, dv, cos, sin, qscale) @ weight`` (``+ addend``, rounded as a separate add would) as one
+    tensor-core GEMM whose A operand is merged in shared memory (``ebr_qkv_rope_merge_dx``): the input gradient of the
+    qkv projection, with a residual gradient joined in when given. Shapes ``merge_dx_fusable`` takes."""
     _require_cuda(dq, "qkv_rope_merge_dx")
     dk, dv = dk.to(dq.dtype), dv.to(dq.dtype)
     dq, dk, dv = (t if t.stride(-1) == 1 else t.contiguous() for t in (dq, dk, dv))
@@ -263,18 +264,19 @@ def qkv_rope_merge_dx_op(dq: Tensor, dk: Tensor, dv: Tensor, weight: Tensor, cos
     cos, sin = _table(cos, dq.device), _table(sin, dq.device)
     qs, qs_ptr = _qscale_arg(qscale)
     ops = [_native.Operand(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)) for t in (dq, dk, dv)]
+    add = None if addend is None else addend.to(dq.dtype).reshape(out.shape).contiguous()
     r = ctypes.byref
     _native.check(
         _native.lib().ebr_qkv_rope_merge_dx(_DTYPES[dq.dtype], b, n, h, d, w.shape[1], r(ops[0]), r(ops[1]),
                                             r(ops[2]), w.data_ptr(), cos.data_ptr(), sin.data_ptr(), qs_ptr,
-                                            out.data_ptr(), _stream()),  # fmt: skip
+                                            _ptr(add), out.data_ptr(), _stream()),  # fmt: skip
         "qkv_rope_merge_dx",
     )
     return out
 
 
 @qkv_rope_merge_dx_op.register_fake
-def _(dq, dk, dv, weight, cos, sin, qscale):
+def _(dq, dk, dv, weight, cos, sin, qscale, addend=None):
     b, h, n, d = dq.shape
     return dq.new_empty((b, n, weight.shape[1]))
 
@@ -483,22 +485,39 @@ class _RmsNormBwd(torch.autograd.Function):
         return ds, (ds if ctx.has_a else None), None, None, dgy
 
 
+def add_rms_norm_fwd(x: Tensor, a: Optional[Tensor] = None, eps: float = 1e-5) -> Tuple[Tensor, Tensor, Tensor]:
+    """``rms_norm(x + a)`` without autograd, returning (y, s = round(x + a) (x itself when a is None), rstd [rows]
+    float32): what the backward needs, for callers that run it explicitly."""
+    _require_cuda(x, "add_rms_norm")
+    x = x.contiguous()
+    a = None if a is None else a.to(x.dtype).contiguous()
+    rows, c = _rows(x)
+    y = torch.empty_like(x)
+    s = torch.empty_like(x) if a is not None else None
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    _native.check(
+        _native.lib().ebr_add_rms_norm(_DTYPES[x.dtype], rows, c, eps, x.data_ptr(), _ptr(a), _ptr(s),
+                                       y.data_ptr(), rstd.data_ptr(), None, 0.0, _stream()),  # fmt: skip
+        "add_rms_norm",
+    )
+    return y, (x if s is None else s), rstd
+
+
+def rms_norm_bwd(s: Tensor, rstd: Tensor, gy: Tensor) -> Tensor:
+    """The gradient of ``rms_norm(s)`` (both x and a of ``add_rms_norm``) from the forward's s and rstd, one kernel."""
+    return _rms_norm_bwd_kernel(s, rstd, gy)
+
+
+def swiglu_bwd(h: Tensor, gout: Tensor) -> Tensor:
+    """The gradient of the SwiGLU activation with respect to h = [gate, up], one kernel (no higher-order graph)."""
+    return _swiglu_bwd_kernel(h.contiguous(), gout)
+
+
 class _AddRMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x: Tensor, a: Optional[Tensor], eps: float) -> Tensor:
-        _require_cuda(x, "add_rms_norm")
-        x = x.contiguous()
-        a = None if a is None else a.to(x.dtype).contiguous()
-        rows, c = _rows(x)
-        y = torch.empty_like(x)
-        s = torch.empty_like(x) if a is not None else None
-        rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
-        _native.check(
-            _native.lib().ebr_add_rms_norm(_DTYPES[x.dtype], rows, c, eps, x.data_ptr(), _ptr(a), _ptr(s),
-                                           y.data_ptr(), rstd.data_ptr(), None, 0.0, _stream()),  # fmt: skip
-            "add_rms_norm",
-        )
-        ctx.save_for_backward(x, a, x if s is None else s, rstd)
+        y, s, rstd = add_rms_norm_fwd(x, a, eps)
+        ctx.save_for_backward(x.contiguous(), None if a is None else a.to(x.dtype), s, rstd)
         ctx.eps = eps
         ctx.has_a = a is not None
         return y

@@ -49,12 +49,15 @@ int ebr_qkv_rope_split(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, in
  * [B, N, 3 H D] merged gradient (ebr_rope_merge's output, rounded to the I/O type) never stored. dq / dk / dv:
  * [B, H, N, D] operands (16-byte aligned data and strides, unit head-dim stride); w: the [3 H D, C] projection weight,
  * contiguous; cos / sin: float32 [N, D] tables; qscale: NULL or float32 [H] (applied to dq first, as ebr_rope_merge
- * does); dx: [B, N, C] contiguous. bfloat16 / float16 only, D = 64 and C = 512, else EBR_ERR_SHAPE / EBR_ERR_STRIDE
+ * does); addend: NULL or [B, N, C] contiguous, added to the rounded product and rounded again (a residual gradient
+ * joined in, as a separate add of the two would); dx: [B, N, C] contiguous. bfloat16 / float16 only, D = 64 and
+ * C = 512, else EBR_ERR_SHAPE / EBR_ERR_STRIDE
  * (the caller then runs ebr_rope_merge and its GEMM). Replaces: rope_merge + the linear layer's input gradient in the
  * backward of EnergyAttention (models/fused_attn/rope_split.py:84-96). */
 int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D, int64_t C, const ebr_operand* dq,
                           const ebr_operand* dk, const ebr_operand* dv, const void* w, const float* cos_table,
-                          const float* sin_table, const float* qscale, void* dx, void* stream);
+                          const float* sin_table, const float* qscale, const void* addend, void* dx,
+                          void* stream);
 
 /* The attention's output projection from the head-major attention output: y[b, n, :] = sum_h O[b, h, n, :] W_h^T with
  * W_h = W[:, h D : (h + 1) D], fp32 accumulation and one rounding to the I/O type (the [B, N, H D] transpose of O is

@@ -92,12 +92,12 @@ def test_layer_entry_points_reject_bad_arguments_before_device(lib):
     # The qkv input gradient with the merge in the GEMM: 16-bit only, D = 64 and C = 512, aligned operands.
     md = lib.ebr_qkv_rope_merge_dx
     g8 = _op(t, 8 * 4 * 64, 4 * 64, 64)  # [1, 8, 4, 64] contiguous
-    assert md(_native.FLOAT32, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_DTYPE
-    assert md(_native.BFLOAT16, 1, 4, 8, 128, 512, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_SHAPE
-    assert md(_native.BFLOAT16, 1, 4, 8, 64, 256, r(g8), r(g8), r(g8), t, t, t, None, t, None) == _native.ERR_SHAPE
-    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), None, t, t, None, t, None) == _native.ERR_NULL
-    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t + 2, t, t, None, t, None) == _native.ERR_STRIDE
-    assert md(_native.BFLOAT16, 0, 4, 8, 64, 512, None, None, None, None, None, None, None, None, None) == 0
+    assert md(_native.FLOAT32, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t, t, t, None, None, t, None) == _native.ERR_DTYPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 128, 512, r(g8), r(g8), r(g8), t, t, t, None, None, t, None) == _native.ERR_SHAPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 256, r(g8), r(g8), r(g8), t, t, t, None, None, t, None) == _native.ERR_SHAPE
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), None, t, t, None, None, t, None) == _native.ERR_NULL
+    assert md(_native.BFLOAT16, 1, 4, 8, 64, 512, r(g8), r(g8), r(g8), t + 2, t, t, None, None, t, None) == _native.ERR_STRIDE
+    assert md(_native.BFLOAT16, 0, 4, 8, 64, 512, None, None, None, None, None, None, None, None, None, None) == 0
     # The double backwards of rms_norm and SwiGLU: layer dtypes only, a row length, every buffer.
     assert lib.ebr_rms_norm_bwd2(_native.FLOAT64, 4, 8, t, t, t, t, t, t, None) == _native.ERR_DTYPE
     assert lib.ebr_rms_norm_bwd2(_native.BFLOAT16, 4, 0, t, t, t, t, t, t, None) == _native.ERR_SHAPE

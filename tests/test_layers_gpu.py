@@ -362,6 +362,9 @@ def test_qkv_rope_merge_dx_is_the_merge_then_the_gemm(dtype, shape, with_scale):
     finally:
         m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction = flags
     assert float((got != unfused).double().mean()) < 0.01
+    # a residual gradient joined in: exactly the separate 16-bit add of the two
+    res = torch.randn(b, n, c, generator=g).to(dtype).to(DEV)
+    assert torch.equal(qkv_rope_merge_dx_op(dq, dk, dv, w, cos, sin, qs, res), got + res)
 
 
 GU_SHAPES = [(2, 81, 512, 1536), (1, 900, 512, 1536), (3, 100, 256, 128), (2, 37, 128, 256)]
