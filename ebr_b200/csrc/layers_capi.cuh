@@ -92,6 +92,22 @@ int make_matrix_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, 
   return EBR_OK;
 }
 
+// 2-D TMA store map over a row-major [rows, cols] 16-bit matrix: boxes of 16 columns x 32 rows with the 32-byte
+// swizzle (one epilogue warp's output chunk); rows past the end are not written.
+int make_chunk_store_map(CUtensorMap* map, void* ptr, int dtype, int64_t rows, int64_t cols, int64_t row_stride) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  const cuuint32_t box[2] = {16, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled failed%s%s");
+  return EBR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -498,8 +514,9 @@ int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void
                        void* h, void* act, void* stream) {
   if (dtype != EBR_BFLOAT16 && dtype != EBR_FLOAT16)
     return set_error(EBR_ERR_DTYPE, "gate_up_swiglu: bfloat16 or float16 only%s%s");
-  if (rows < 0 || C < 1 || I < 1 || C % 64 != 0 || I % 128 != 0 || C > INT32_MAX || I > INT32_MAX / 2)
-    return set_error(EBR_ERR_SHAPE, "gate_up_swiglu: needs C a multiple of 64 and I a multiple of 128%s%s");
+  if (rows < 0 || C < 1 || I < 1 || C % 64 != 0 || I % 128 != 0 || rows > INT32_MAX || C > INT32_MAX ||
+      I > INT32_MAX / 2)
+    return set_error(EBR_ERR_SHAPE, "gate_up_swiglu: needs C a multiple of 64, I a multiple of 128 and rows < 2^31%s%s");
   if (rows == 0) return EBR_OK;
   if (!x || !w || !h || !act) return set_error(EBR_ERR_NULL, "gate_up_swiglu: NULL pointer%s%s");
   if (x_stride < C || x_stride % 8 != 0 || !all_aligned16({x, w, h, act}))
@@ -510,23 +527,22 @@ int ebr_gate_up_swiglu(int dtype, int64_t rows, int64_t C, int64_t I, const void
   if (rc != EBR_OK) return rc;
   auto st = static_cast<cudaStream_t>(stream);
   using L = ebr::GateUpLayout;
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, th, ta;
   if ((rc = make_matrix_map(&tx, x, dtype, rows, C, x_stride, L::kBM)) != EBR_OK) return rc;
   if ((rc = make_matrix_map(&tw, w, dtype, 2 * I, C, C, 128)) != EBR_OK) return rc;
+  if ((rc = make_chunk_store_map(&th, h, dtype, rows, 2 * I, 2 * I)) != EBR_OK) return rc;
+  if ((rc = make_chunk_store_map(&ta, act, dtype, rows, I, I)) != EBR_OK) return rc;
   const int64_t m_tiles = (rows + L::kBM - 1) / L::kBM;
   const int64_t cap = sm_count(device);
   const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
-  auto launch = [&](auto kernel, auto* out_tag) -> int {
-    using T = std::remove_pointer_t<decltype(out_tag)>;
+  auto launch = [&](auto kernel) -> int {
     if ((rc = prepare_tc_kernel(reinterpret_cast<const void*>(kernel), device, L::kSmem, L::kTmemCols, L::kThreads)))
       return rc;
-    kernel<<<grid, L::kThreads, L::kSmem, st>>>(tx, tw, rows, static_cast<int>(C), static_cast<int>(I),
-                                                static_cast<T*>(h), static_cast<T*>(act));
+    kernel<<<grid, L::kThreads, L::kSmem, st>>>(tx, tw, th, ta, rows, static_cast<int>(C), static_cast<int>(I));
     return check_launch("tc_gate_up_swiglu_kernel");
   };
-  if (dtype == EBR_BFLOAT16)
-    return launch(ebr::tc_gate_up_swiglu_kernel<__nv_bfloat16>, static_cast<__nv_bfloat16*>(nullptr));
-  return launch(ebr::tc_gate_up_swiglu_kernel<__half>, static_cast<__half*>(nullptr));
+  if (dtype == EBR_BFLOAT16) return launch(ebr::tc_gate_up_swiglu_kernel<__nv_bfloat16>);
+  return launch(ebr::tc_gate_up_swiglu_kernel<__half>);
 }
 
 }  // extern "C"

@@ -54,6 +54,19 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 2-D tiled TMA store of one box from shared memory (laid out as the map's swizzle says) to (column c0, row c1); rows
+// past the tensor's end are not written. Tracked by this thread's bulk async-groups (tma_store_commit, wait below).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+// Wait until at most the most recent committed bulk store group of this thread may still be reading shared memory.
+__device__ __forceinline__ void tma_store_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 // Epilogue slots: the 32 columns of a head that one rotation pairs with each other, elements [da, da + 16) and
 // [da + D / 4, da + D / 4 + 16) (quarter_swap (a, b, c, d) -> (b, a, d, c) pairs element e with e +- D / 4). At D = 64 a
 // head has two slots (da = 0, 32), at D = 128 four (da = 0, 16, 64, 80). Warpgroup g of the epilogue takes slots
