@@ -741,7 +741,8 @@ def run_sweep(args) -> None:
             del q, k, v, do, gq, gk, gv, o, lse, dq
             torch.cuda.empty_cache()
             proj = [p for p in ("qkv_rope", "qkv_unfused", "o_proj", "o_unfused", "gate_up", "gate_up_unfused",
-                                "rope_merge", "swiglu_bwd", "qkv_dx", "qkv_dx_unfused") if p in args.passes.split(",")]
+                                "rope_merge", "swiglu_bwd", "qkv_dx", "qkv_dx_add", "qkv_dx_unfused")
+            if p in args.passes.split(",")]
             if proj and args.impl == "ours":
                 out.update(sweep_qkv(args, proj, B, L, H, D, pk))
             _native.device_status()
@@ -761,7 +762,8 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     MLP's gate / up projection with the SwiGLU activation as its epilogue (``gate_up``) and as cuBLAS + the activation
     kernel (``gate_up_unfused``); the two HBM-bound kernels of the dE/dz backward, the RoPE merge of dq / dk / dv into
     d(qkv) (``rope_merge``) and the SwiGLU backward (``swiglu_bwd``); the qkv projection's input gradient with the
-    merge folded into the GEMM (``qkv_dx``) and as the merge kernel + cuBLAS (``qkv_dx_unfused``)."""
+    merge folded into the GEMM (``qkv_dx``; ``qkv_dx_add`` with the residual gradient joined in its epilogue, as the
+    dE/dz backward runs it) and as the merge kernel + cuBLAS (``qkv_dx_unfused``)."""
     import torch.nn.functional as F
 
     from ebr_b200.energy import NetShape, rope_tables
@@ -781,7 +783,7 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
     inter = NetShape(hidden=C, heads=H).mlp_width  # the energy network's SwiGLU width (expansion 4)
     wgu = (torch.randn(2 * inter, C, device="cuda", generator=g) * C**-0.5).to(torch.bfloat16)
     need = set(passes)
-    if need & {"rope_merge", "qkv_dx", "qkv_dx_unfused"}:
+    if need & {"rope_merge", "qkv_dx", "qkv_dx_add", "qkv_dx_unfused"}:
         dq3 = [torch.randn(B, H, L, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3)]
     if "swiglu_bwd" in need:
         hgu = torch.randn(B, L, 2 * inter, device="cuda", generator=g).to(torch.bfloat16)
@@ -795,6 +797,7 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         "gate_up_unfused": lambda: swiglu_act(F.linear(x, wgu)),
         "rope_merge": lambda: rope_merge_op(*dq3, cos_t, sin_t, e),
         "qkv_dx": lambda: qkv_rope_merge_dx_op(*dq3, w, cos_t, sin_t, e),
+        "qkv_dx_add": lambda: qkv_rope_merge_dx_op(*dq3, w, cos_t, sin_t, e, x),
         "qkv_dx_unfused": lambda: rope_merge_op(*dq3, cos_t, sin_t, e) @ w,
         "swiglu_bwd": lambda: _no_grad_call(_swiglu_grad, hgu, gact),  # the fused kernel (no higher-order graph)
     }
@@ -804,6 +807,7 @@ def sweep_qkv(args, passes, B: int, L: int, H: int, D: int, pk: dict) -> dict:
         if name.startswith("qkv_dx"):
             flop = 2.0 * B * L * C * 3 * C
             byt = 2.0 * (3 * B * L * C + 3 * C * C + B * L * C)  # dq, dk, dv, W, dx (the fused path's bytes)
+            byt += 2.0 * B * L * C if name == "qkv_dx_add" else 0.0  # the addend
         elif name.startswith("qkv"):
             flop = 2.0 * B * L * C * 3 * C
             byt = 2.0 * (B * L * C + 3 * C * C + 3 * B * L * C)  # x, W, q / k / v (the fused path's bytes)

@@ -108,6 +108,23 @@ int make_chunk_store_map(CUtensorMap* map, void* ptr, int dtype, int64_t rows, i
   return EBR_OK;
 }
 
+// 3-D TMA store map over a contiguous [B, N, C] 16-bit tensor: boxes of 32 columns x 32 rows of one sample with the
+// 64-byte swizzle (one epilogue warp's output chunk); rows past N are not written, so a box never spills into the next
+// sample.
+int make_sample_store_map(CUtensorMap* map, void* ptr, int dtype, int64_t B, int64_t N, int64_t C) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable%s%s");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(C * 2), static_cast<cuuint64_t>(N * C * 2)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype == EBR_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EBR_ERR_CUDA, "cuTensorMapEncodeTiled failed%s%s");
+  return EBR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -488,11 +505,12 @@ int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
   int device = 0;
   if ((rc = check_device(&device)) != EBR_OK) return rc;
   auto st = static_cast<cudaStream_t>(stream);
-  CUtensorMap tq, tk, tv, tw;
+  CUtensorMap tq, tk, tv, tw, tdx;
   if (make_tile_map(&tq, dq, dtype, B, H, N, D) || make_tile_map(&tk, dk, dtype, B, H, N, D) ||
       make_tile_map(&tv, dv, dtype, B, H, N, D))
     return set_error(EBR_ERR_CUDA, "qkv_rope_merge_dx: tensor map for dq / dk / dv%s%s");
   if ((rc = make_matrix_map(&tw, w, dtype, 3 * H * D, C, C, L::kBK)) != EBR_OK) return rc;
+  if ((rc = make_sample_store_map(&tdx, dx, dtype, B, N, C)) != EBR_OK) return rc;
   const int64_t m_tiles = B * ((N + L::kBM - 1) / L::kBM);
   const int64_t cap = sm_count(device);
   const unsigned grid = static_cast<unsigned>(m_tiles < cap ? m_tiles : cap);
@@ -502,7 +520,7 @@ int ebr_qkv_rope_merge_dx(int dtype, int64_t B, int64_t N, int64_t H, int64_t D,
       return rc;
     kernel<<<grid, L::kThreads, L::kSmem, st>>>(tq, tk, tv, tw, static_cast<int>(B), static_cast<int>(H),
                                                 static_cast<int>(N), cos_table, sin_table, qscale,
-                                                static_cast<const T*>(addend), static_cast<T*>(dx));
+                                                static_cast<const T*>(addend), tdx);
     return check_launch("tc_merge_gemm_kernel");
   };
   if (dtype == EBR_BFLOAT16)

@@ -16,7 +16,9 @@
 //              c = f, f + 2, f + 4, f + 6 of row r: every quarter_swap partner (chunk c ^ 2) is in the same set, so a
 //              thread rotates its 32 elements alone, with its row's 32 cos / sin values held in registers for the
 //              m-tile. dv blocks need no rotation. At the m-tile's end warps w, w + 4 drain TMEM lanes
-//              [32 (w % 4), +32), columns [256 (w / 4), +256), into dx rows.
+//              [32 (w % 4), +32), columns [256 (w / 4), +256), into dx: each [32 x 32] chunk is written to one of
+//              the warp's two shared-memory boxes (64-byte swizzle) and leaves by a 3-D TMA store, which clips the
+//              rows past N; the addend's row piece of the next chunk is loaded while the current one is drained.
 // Rounding as ebr_rope_merge (the merged value is the same 16-bit number the unfused path writes, multiplies and adds
 // rounded separately); the GEMM sums in fp32 in K-steps of 16, where cuBLAS may order the sum differently.
 // The reference's rope_merge + the linear layer's input gradient (models/fused_attn/rope_split.py:52-67, :84-96).
@@ -34,7 +36,9 @@ struct MergeGemmLayout {
   static constexpr uint32_t kBHalf = kBK * kBN * 2;  // 32 KB: W rows [64 kb, +64) x columns [256 h, +256)
   static constexpr int kAStages = 4, kBStages = 4;
   static constexpr uint32_t kBRing = kAStages * kATile;
-  static constexpr uint32_t kBytes = kBRing + kBStages * kBHalf;  // 192 KB
+  static constexpr uint32_t kEpiBox = 32 * 32 * 2;  // one epilogue warp's [32 rows x 32 columns] output chunk
+  static constexpr uint32_t kEpi = kBRing + kBStages * kBHalf;  // 192 KB of rings, then two boxes per epilogue warp
+  static constexpr uint32_t kBytes = kEpi + 8 * 2 * kEpiBox;
   static constexpr uint32_t kSmem = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kThreads = 320;
@@ -79,7 +83,8 @@ __device__ __forceinline__ void merge_rotate_row(unsigned char* tile, int r, int
 }
 
 // tq / tk / tv: 4-D TMA maps over dq / dk / dv (D, N, H, B), box 64 x 128; tw: W [3 H D, C] (box 64 columns x 64
-// rows); dx: [B, N, C]. cos / sin: fp32 [N, D]; qscale: NULL or fp32 [H]. addend: NULL or [B, N, C]: then
+// rows); tdx: 3-D TMA store map over dx [B, N, C] (box 32 x 32 x 1, 64-byte swizzle). cos / sin: fp32 [N, D]; qscale:
+// NULL or fp32 [H]. addend: NULL or [B, N, C]: then
 // dx = round(round(merge W) + addend), the value a separate add of the two 16-bit tensors gives (a block input's
 // residual gradient joined to its qkv-projection gradient).
 template <typename T>
@@ -87,7 +92,8 @@ __global__ void __launch_bounds__(320, 1)
     tc_merge_gemm_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tw, int B, int H,
                          int N, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                         const float* __restrict__ qscale, const T* __restrict__ addend, T* __restrict__ dx) {
+                         const float* __restrict__ qscale, const T* __restrict__ addend,
+                         const __grid_constant__ CUtensorMap tdx) {
   using L = MergeGemmLayout;
   constexpr int NA = L::kAStages, NB = L::kBStages, D = 64;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -192,7 +198,9 @@ __global__ void __launch_bounds__(320, 1)
     // ---------------------------------------------------------------- rotation, then epilogue
     const int r = tid & 127, f = tid >> 7;
     const int wq = warp & 3, half = warp >> 2;
-    uint32_t ause = 0, lt = 0;
+    unsigned char* boxes = smem + L::kEpi + warp * 2 * L::kEpiBox;
+    if (lane == 0) tma_prefetch_desc(&tdx);
+    uint32_t ause = 0, lt = 0, chunk = 0;
     bool ok = true;
     for (int64_t mt = blockIdx.x; mt < n_mt && ok; mt += gridDim.x, ++lt) {
       const int b = static_cast<int>(mt / n_nb), nb = static_cast<int>(mt - static_cast<int64_t>(b) * n_nb);
@@ -218,41 +226,62 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive(&a_ready[s]);
       }
       if (!ok) break;
-      // Epilogue: this warp's 32 rows, columns [256 half, +256).
+      // Epilogue: this warp's 32 rows, columns [256 half, +256), as eight [32 x 32] chunks.
+      const int row0 = nb * L::kBM + wq * 32, row = row0 + lane;
+      const T* add = (row < N && addend) ? addend + (static_cast<int64_t>(b) * N + row) * L::kC + half * L::kBN
+                                         : nullptr;
+      uint4 an[4] = {};  // the addend's row piece of the next chunk
+      if (add) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) an[q] = __ldg(reinterpret_cast<const uint4*>(add) + q);
+      }
       ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&acc_full, lt & 1, 932, abort));
       if (!ok) break;
       tc_fence_after();
-      const int row = nb * L::kBM + wq * 32 + lane;
-      const int64_t orow = (static_cast<int64_t>(b) * N + row) * L::kC + half * L::kBN;
-      T* out = row < N ? dx + orow : nullptr;
-      const T* add = (row < N && addend) ? addend + orow : nullptr;
       const uint32_t tacc = tmem + (static_cast<uint32_t>(wq * 32) << 16) + half * 256;
 #pragma unroll 1
-      for (int c = 0; c < L::kBN; c += 32) {
+      for (int c = 0; c < L::kBN; c += 32, ++chunk) {
         uint32_t v[32];
         tmem_ld32(tacc + c, v);
+        uint4 ac[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ac[q] = an[q];
+        if (add && c + 32 < L::kBN) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) an[q] = __ldg(reinterpret_cast<const uint4*>(add + c + 32) + q);
+        }
         tmem_wait_ld_regs(v);
-        if (out) {
+        if (c + 32 == L::kBN) {  // the accumulator half is read out: the next m-tile's products may start
+          tc_fence_before();
+          mbar_arrive(&acc_empty[half]);
+        }
+        unsigned char* box = boxes + (chunk & 1) * L::kEpiBox;
+        if (lane == 0) tma_store_wait_read_1();  // the store issued from this box two chunks ago has read it
+        __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t w[4];
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) w[e] = pack2<T>(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
-            if (add) {
-              const uint4 a = *reinterpret_cast<const uint4*>(add + c + 8 * q);
-              const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+          for (int e = 0; e < 4; ++e) w[e] = pack2<T>(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+          if (add) {
+            const uint32_t aw[4] = {ac[q].x, ac[q].y, ac[q].z, ac[q].w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                w[e] = pack2<T>(layers::add_rn(unpack_lo<T>(w[e]), unpack_lo<T>(aw[e])),
-                                layers::add_rn(unpack_hi<T>(w[e]), unpack_hi<T>(aw[e])));
-            }
-            *reinterpret_cast<uint4*>(out + c + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack2<T>(layers::add_rn(unpack_lo<T>(w[e]), unpack_lo<T>(aw[e])),
+                              layers::add_rn(unpack_hi<T>(w[e]), unpack_hi<T>(aw[e])));
           }
+          // 64-byte swizzle: the 16-byte piece q of row `lane` sits at piece q ^ ((lane >> 1) & 3)
+          *reinterpret_cast<uint4*>(box + lane * 64 + 16 * (q ^ ((lane >> 1) & 3))) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < N) {  // a box wholly past the sample's last row is not issued
+          tma_store_3d(&tdx, box, half * L::kBN + c, row0, b);
+          tma_store_commit();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[half]);
     }
+    if (lane == 0) tma_store_wait_all();  // the boxes stay valid until every store has completed
   }
   tc_fence_before();
   __syncthreads();

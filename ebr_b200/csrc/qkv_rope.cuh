@@ -62,6 +62,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
                : "memory");
 }
+// 3-D tiled TMA store of one box (coordinates c0 innermost); elements past the tensor's extents are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 // Wait until at most the most recent committed bulk store group of this thread may still be reading shared memory.
 __device__ __forceinline__ void tma_store_wait_read_1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
