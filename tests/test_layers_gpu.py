@@ -636,3 +636,32 @@ def test_training_segment_with_fused_layers():
 
     got, floor = rel(ours, eager), rel(m32, m64)
     assert got <= max(2e-2, 1.25 * floor + 2e-3), (got, floor)
+
+
+def test_silu_rounding_is_exact_for_every_bfloat16_gate():
+    """Every finite bfloat16 gate value through the three kernels that round silu(g): the activation, its backward (du
+    with gout = up = 1) and the gate / up GEMM's epilogue (identity weights, so h reproduces the gates exactly). Each
+    must equal round(g / (1 + exp(-g))) taken in fp32 by torch on the same device, bit for bit."""
+    from ebr_b200.layers import gate_up_swiglu_op, swiglu_act, swiglu_bwd
+
+    bits = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16)
+    g = bits.view(torch.bfloat16).to(DEV)
+    g = g[torch.isfinite(g)]
+    i = 128
+    rows = (g.numel() + i - 1) // i
+    g = torch.cat([g, g.new_zeros(rows * i - g.numel())]).view(rows, i)
+    g32 = g.float()
+    ref = (g32 / (1 + torch.exp(-g32))).to(torch.bfloat16)
+    h = torch.cat([g, torch.ones_like(g)], dim=1)
+    with torch.no_grad():
+        assert torch.equal(swiglu_act(h), ref)
+        assert torch.equal(swiglu_bwd(h, torch.ones_like(g))[:, i:], ref)
+        x = torch.zeros(rows, 256, device=DEV, dtype=torch.bfloat16)
+        x[:, :i] = g
+        x[:, i] = 1
+        w = torch.zeros(2 * i, 256, device=DEV, dtype=torch.bfloat16)
+        w[torch.arange(i), torch.arange(i)] = 1
+        w[i:, i] = 1
+        hh, act = gate_up_swiglu_op(x, w)
+        assert torch.equal(hh, h)
+        assert torch.equal(act, ref)
