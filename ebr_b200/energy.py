@@ -232,17 +232,19 @@ class LatentEnergyNet(nn.Module):
 
     def _dz_fusable(self, v: Tensor) -> bool:
         """Whether the explicit dE/dv path serves this call: the default attention, 16-bit CUDA activations, head dim 64
-        and hidden 512 (the shapes of the merge GEMM; the other fused kernels take them too)."""
+        or 128 and hidden 512 (the shapes the fused projections take; the merge GEMM serves head dim 64, and 128 takes
+        the RoPE-merge kernel and a cuBLAS product)."""
         s = self.shape
         return (self._attention is None and v.is_cuda and v.dtype in (torch.bfloat16, torch.float16)
-                and s.head_dim == 64 and s.hidden == 512 and (2 * s.mlp_width) % 256 == 0)  # fmt: skip
+                and s.head_dim in (64, 128) and s.hidden == 512 and (2 * s.mlp_width) % 256 == 0)  # fmt: skip
 
     def _energy_and_grad_dz(self, v: Tensor, x: Tensor) -> tuple[Tensor, Tensor]:
         """(E, dE/dv) with the blocks' backward run explicitly, not through autograd. Each block's forward runs the same
         fused ops as ``_block`` and keeps what its backward needs; the backward then runs the fused kernels in reverse.
         A block input's residual gradient joins its branch gradient inside a product instead of a separate add:
-        through the merge GEMM's addend at the attention input (rounded as the add would be) and cuBLAS's beta = 1
-        accumulate at the MLP input (one rounding instead of two). Only dE/dv: no parameter gradients."""
+        through the merge GEMM's addend at the attention input (rounded as the add would be; at head dim 128, cuBLAS's
+        beta = 1 accumulate after the RoPE-merge kernel) and cuBLAS's beta = 1 accumulate at the MLP input (one
+        rounding instead of two). Only dE/dv: no parameter gradients."""
         s, dt = self.shape, v.dtype
         b, n, c = v.shape
         hh, d = s.heads, s.head_dim
@@ -275,7 +277,11 @@ class LatentEnergyNet(nn.Module):
                 ds1 = fl.rms_norm_bwd(s1, r1, g1)
                 d_o = (ds1 @ w_out).view(b, n, hh, d).transpose(1, 2)
                 dq, dk, dv = torch.ops.ebr_fused.attn_bwd(q, k, vv, o, lse, d_o, scale)
-                g = fl.qkv_rope_merge_dx_op(dq, dk, dv, w_qkv, self.rope_cos, self.rope_sin, folded, ds1)
+                if fl.merge_dx_fusable(dq, w_qkv):
+                    g = fl.qkv_rope_merge_dx_op(dq, dk, dv, w_qkv, self.rope_cos, self.rope_sin, folded, ds1)
+                else:  # head dim 128: the merged gradient [B N, 3 H D] times W, the residual gradient accumulated
+                    merged = fl.rope_merge_op(dq, dk, dv, self.rope_cos, self.rope_sin, folded)
+                    g = torch.addmm(ds1.reshape(-1, c), merged.reshape(-1, merged.shape[-1]), w_qkv).view(b, n, c)
         return e.detach(), g
 
     # -- descent ----------------------------------------------------------------------------------------------------

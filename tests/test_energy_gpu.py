@@ -328,13 +328,15 @@ def test_graphed_microstep_equals_the_eager_one():
         assert same(got, want)
 
 
-def test_explicit_dz_backward_equals_autograd():
+@pytest.mark.parametrize("heads", [8, 4], ids=["d64", "d128"])
+def test_explicit_dz_backward_equals_autograd(heads):
     """dE/dv through the blocks' explicit backward (the path every no-graph microstep takes) against autograd through
-    the same network: the energy is the same (identical forward ops) and dE/dv differs only by the MLP join's single
-    rounding (cuBLAS accumulates the residual gradient into the product instead of a separate add)."""
+    the same network, at head dims 64 and 128: the energy is the same (identical forward ops) and dE/dv differs only
+    by the single rounding of the residual joins that cuBLAS accumulates into a product instead of a separate add (the
+    MLP input; at head dim 128 also the attention input)."""
     from ebr_b200.energy import LatentEnergyNet, NetShape
 
-    net = LatentEnergyNet(NetShape(board=(9, 9), vocab=10, layers=2, cell_softplus=True)).cuda()
+    net = LatentEnergyNet(NetShape(board=(9, 9), vocab=10, heads=heads, layers=2, cell_softplus=True)).cuda()
     gen = torch.Generator(device="cuda").manual_seed(31)
     x = net.embed(torch.randint(0, 10, (5, 81), generator=gen, device="cuda"))
     v = net.fresh_states(5, gen)
